@@ -1,0 +1,168 @@
+// C ABI entry points (include/atlas_scan.h): argument checks, dispatch to the
+// exact or the tcgen05 implementation, error reporting.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "scan_internal.h"
+
+namespace atlas {
+__device__ int g_status = 0;
+
+int* device_status_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
+  return (int*)p;
+}
+}  // namespace atlas
+
+namespace {
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int check_params(const AtlasScanParams* p) {
+  if (!p) return fail(ATLAS_ERR_INVALID_ARGUMENT, "params is NULL");
+  if (p->abi_version != ATLAS_ABI_VERSION)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "abi_version %d != library %d", p->abi_version, ATLAS_ABI_VERSION);
+  if (p->B <= 0 || p->T <= 0 || p->H <= 0 || p->D <= 0 || p->E <= 0 || p->chunk <= 0)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "B, T, H, D, E and chunk must be positive");
+  if (p->omega < 1) return fail(ATLAS_ERR_INVALID_ARGUMENT, "omega must be >= 1");
+  if (p->ns_steps < 0 || p->ns_steps > 5) return fail(ATLAS_ERR_INVALID_ARGUMENT, "ns_steps must be in 0..5");
+  if (p->act_dtype != ATLAS_F32 && p->act_dtype != ATLAS_BF16)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "act_dtype must be ATLAS_F32 or ATLAS_BF16");
+  if (p->precision != ATLAS_PREC_EXACT && p->precision != ATLAS_PREC_TENSOR)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "precision must be ATLAS_PREC_EXACT or ATLAS_PREC_TENSOR");
+  if (p->precision == ATLAS_PREC_TENSOR) {
+    const char* why = "";
+    if (!atlas::tc::supported(*p, &why)) return fail(ATLAS_ERR_UNSUPPORTED, "tensor path: %s", why);
+  }
+  return ATLAS_OK;
+}
+
+int cuda_result(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(ATLAS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ATLAS_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int atlas_abi_version(void) { return ATLAS_ABI_VERSION; }
+
+const char* atlas_last_error_string(void) { return g_err.c_str(); }
+
+size_t atlas_scan_saved_bytes(const AtlasScanParams* p) {
+  if (check_params(p) != ATLAS_OK) return 0;
+  return p->precision == ATLAS_PREC_EXACT ? atlas::exact::saved_bytes(*p) : atlas::tc::saved_bytes(*p);
+}
+
+size_t atlas_scan_workspace_bytes(const AtlasScanParams* p) {
+  if (check_params(p) != ATLAS_OK) return 0;
+  return p->precision == ATLAS_PREC_EXACT ? atlas::exact::workspace_bytes(*p) : atlas::tc::workspace_bytes(*p);
+}
+
+int atlas_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const void* v, const float* alpha,
+                   const float* eta, const float* theta, const float* gamma, const float* W1_in,
+                   const float* W2_in, const float* S1_in, const float* S2_in, void* y, float* W1_out,
+                   float* W2_out, float* S1_out, float* S2_out, void* saved, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (!q || !k || !v || !alpha || !eta || !theta || !y)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "q, k, v, alpha, eta, theta and y must be non-NULL");
+  if ((W1_in || W2_in || S1_in || S2_in) && !(W1_in && W2_in && S1_in && S2_in))
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "state_in must be all NULL or all non-NULL");
+  size_t need = atlas_scan_workspace_bytes(p);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(ATLAS_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  atlas::FwdArgs a;
+  a.p = *p;
+  a.q = q; a.k = k; a.v = v;
+  a.alpha = alpha; a.eta = eta; a.theta = theta; a.gamma = gamma;
+  a.W1_in = W1_in; a.W2_in = W2_in; a.S1_in = S1_in; a.S2_in = S2_in;
+  a.y = y;
+  a.W1_out = W1_out; a.W2_out = W2_out; a.S1_out = S1_out; a.S2_out = S2_out;
+  a.saved = saved;
+  a.ws = workspace;
+  a.status = atlas::device_status_ptr();
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = p->precision == ATLAS_PREC_EXACT ? atlas::exact::launch_fwd(a, s) : atlas::tc::launch_fwd(a, s);
+  return cuda_result(e, "atlas_scan_fwd launch");
+}
+
+int atlas_scan_bwd(const AtlasScanParams* p, const void* q, const void* k, const void* v, const float* alpha,
+                   const float* eta, const float* theta, const float* gamma, const void* saved, const void* dy,
+                   const float* dW1_out, const float* dW2_out, const float* dS1_out, const float* dS2_out,
+                   void* dq, void* dk, void* dv, float* dalpha, float* deta, float* dtheta, float* dgamma,
+                   float* dW1_in, float* dW2_in, float* dS1_in, float* dS2_in, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (!q || !k || !v || !alpha || !eta || !theta || !saved || !dy || !dq || !dk || !dv)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "q, k, v, gates, saved, dy, dq, dk, dv must be non-NULL");
+  size_t need = atlas_scan_workspace_bytes(p);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(ATLAS_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  atlas::BwdArgs a;
+  a.p = *p;
+  a.q = q; a.k = k; a.v = v;
+  a.alpha = alpha; a.eta = eta; a.theta = theta; a.gamma = gamma;
+  a.saved = saved; a.dy = dy;
+  a.dW1_out = dW1_out; a.dW2_out = dW2_out; a.dS1_out = dS1_out; a.dS2_out = dS2_out;
+  a.dq = dq; a.dk = dk; a.dv = dv;
+  a.dalpha = dalpha; a.deta = deta; a.dtheta = dtheta; a.dgamma = dgamma;
+  a.dW1_in = dW1_in; a.dW2_in = dW2_in; a.dS1_in = dS1_in; a.dS2_in = dS2_in;
+  a.ws = workspace;
+  a.status = atlas::device_status_ptr();
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = p->precision == ATLAS_PREC_EXACT ? atlas::exact::launch_bwd(a, s) : atlas::tc::launch_bwd(a, s);
+  return cuda_result(e, "atlas_scan_bwd launch");
+}
+
+size_t atlas_polar_express_workspace_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ns_steps,
+                                           int32_t precision) {
+  (void)precision;
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  return atlas::exact::pe_workspace_bytes(batch, rows, cols, ns_steps);
+}
+
+int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t rows, int32_t cols,
+                                int32_t ns_steps, float eps_in_sqrt, int32_t precision, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  if (!X || !Y) return fail(ATLAS_ERR_INVALID_ARGUMENT, "X and Y must be non-NULL");
+  if (batch <= 0 || rows <= 0 || cols <= 0) return fail(ATLAS_ERR_INVALID_ARGUMENT, "empty problem");
+  if (ns_steps < 0 || ns_steps > 5) return fail(ATLAS_ERR_INVALID_ARGUMENT, "ns_steps must be in 0..5");
+  if (precision != ATLAS_PREC_EXACT)
+    return fail(ATLAS_ERR_UNSUPPORTED, "batched Polar Express is implemented in ATLAS_PREC_EXACT only");
+  size_t need = atlas_polar_express_workspace_bytes(batch, rows, cols, ns_steps, precision);
+  if (!workspace || workspace_bytes < need)
+    return fail(ATLAS_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  return cuda_result(atlas::exact::launch_pe(X, Y, batch, rows, cols, ns_steps, eps_in_sqrt, workspace,
+                                             (cudaStream_t)stream),
+                     "atlas_polar_express_batched launch");
+}
+
+int atlas_scan_status(void) {
+  int h = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&h, atlas::g_status, sizeof(int));
+  if (e != cudaSuccess) return fail(ATLAS_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+  cudaMemcpyToSymbol(atlas::g_status, &zero, sizeof(int));
+  if (h) fail(h, "device-side wait expired");
+  return h;
+}
+
+}  // extern "C"

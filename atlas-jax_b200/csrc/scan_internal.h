@@ -1,0 +1,59 @@
+// Internal launch interface shared by the ABI layer and the kernel files.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#include "atlas_scan.h"
+
+namespace atlas {
+
+struct FwdArgs {
+  AtlasScanParams p;
+  const void *q, *k, *v;
+  const float *alpha, *eta, *theta, *gamma;
+  const float *W1_in, *W2_in, *S1_in, *S2_in;  // may be null (LM init)
+  void* y;
+  float *W1_out, *W2_out, *S1_out, *S2_out;
+  void* saved;  // may be null
+  void* ws;
+  int* status;  // device status word
+};
+
+struct BwdArgs {
+  AtlasScanParams p;
+  const void *q, *k, *v;
+  const float *alpha, *eta, *theta, *gamma;
+  const void* saved;
+  const void* dy;
+  const float *dW1_out, *dW2_out, *dS1_out, *dS2_out;  // may be null
+  void *dq, *dk, *dv;
+  float *dalpha, *deta, *dtheta, *dgamma;
+  float *dW1_in, *dW2_in, *dS1_in, *dS2_in;
+  void* ws;
+  int* status;
+};
+
+__host__ __device__ inline int n_chunks(const AtlasScanParams& p) { return (p.T + p.chunk - 1) / p.chunk; }
+
+namespace exact {
+size_t saved_bytes(const AtlasScanParams& p);
+size_t workspace_bytes(const AtlasScanParams& p);
+cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t s);
+cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t s);
+cudaError_t launch_pe(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
+                      void* ws, cudaStream_t s);
+size_t pe_workspace_bytes(int64_t batch, int rows, int cols, int steps);
+}  // namespace exact
+
+int* device_status_ptr();  // address of the status word on the current device
+
+namespace tc {
+bool supported(const AtlasScanParams& p, const char** why);
+size_t saved_bytes(const AtlasScanParams& p);
+size_t workspace_bytes(const AtlasScanParams& p);
+cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t s);
+cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t s);
+}  // namespace tc
+
+}  // namespace atlas

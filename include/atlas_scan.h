@@ -1,0 +1,141 @@
+/*
+ * atlas_scan.h -- C ABI of the B200 (sm_100a) Atlas chunked deep-memory scan.
+ *
+ * This boundary replaces the whole scan of AtlasMemoryLayer.__call__ in
+ * rkstgr/atlas-jax (atlas_jax/memory_layer.py:635-718: initial state, padding,
+ * lax.scan over jax.checkpoint(chunk_body), un-chunking) together with the
+ * inner fused-kernel boundary it dispatches to (fused_chunk_scan_kernel,
+ * memory_layer.py:535-541 -> atlas_jax/kernels/fused_chunk.py:321-379, a
+ * jax.custom_vjp whose backward is JAX recompute + vjp, fused_chunk.py:366-376).
+ * A jax.ffi registration binds these entry points one-to-one.
+ *
+ * Conventions
+ *  - All buffers are caller-owned DEVICE pointers; no entry point allocates.
+ *  - Activations q, k, v, y, dy, dq, dk, dv: row-major (B, T, H, D) in
+ *    params->act_dtype (ATLAS_F32 or ATLAS_BF16).
+ *  - Gates alpha, eta, theta, gamma and their gradients: (B, T, H) float32, already
+ *    activated (sigmoid, eta times max_lr), memory_layer.py:627-633.  gamma may be
+ *    NULL (treated as all ones; the reference passes zeros when omega <= 1, which
+ *    the window-1 aggregation never reads).
+ *  - Memory state (carry), always float32, the reference's naming
+ *    (memory_layer.py:106-115): W1, S1 are (B, H, D, E); W2, S2 are (B, H, E, D).
+ *  - T need not be a multiple of chunk: padding follows memory_layer.py:649-660
+ *    (pad tokens have q=k=v=0, alpha=1, eta=theta=gamma=0), so the final S is 0
+ *    when T % chunk != 0, exactly as in the reference.
+ *  - stream is a cudaStream_t passed as void*.  Calls are stream-ordered and
+ *    asynchronous; a returned ATLAS_OK means "launched".  Device-side failures
+ *    (bounded waits that expired) are reported in the status word that
+ *    atlas_scan_status() reads after the stream is synchronised.
+ *  - Thread safety: entry points keep no global mutable state except a
+ *    thread-local error string.
+ */
+#ifndef ATLAS_SCAN_H_
+#define ATLAS_SCAN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATLAS_ABI_VERSION 1
+
+/* status codes */
+enum {
+  ATLAS_OK = 0,
+  ATLAS_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, mismatched version */
+  ATLAS_ERR_UNSUPPORTED = 2,      /* valid but not implemented for this precision/shape */
+  ATLAS_ERR_CUDA = 3,             /* a CUDA runtime call failed */
+  ATLAS_ERR_DEVICE_TIMEOUT = 4,   /* a bounded device-side wait expired */
+  ATLAS_ERR_WORKSPACE = 5         /* workspace smaller than atlas_scan_workspace_bytes() */
+};
+
+/* element types */
+enum { ATLAS_F32 = 0, ATLAS_BF16 = 1 };
+
+/* arithmetic used inside the scan */
+enum {
+  /* float64 CUDA-core arithmetic: reproduces the reference's math well below its
+   * own float32 rounding noise.  For parity runs and small shapes. */
+  ATLAS_PREC_EXACT = 0,
+  /* tcgen05 tensor cores with a three-term bf16 split (hi*hi + hi*lo + lo*hi,
+   * float32 accumulation) for every Polar Express product, float32 carries.
+   * The production path. */
+  ATLAS_PREC_TENSOR = 1
+};
+
+typedef struct AtlasScanParams {
+  int32_t abi_version;      /* must be ATLAS_ABI_VERSION */
+  int32_t B, T, H, D, E;    /* batch, sequence, heads, head_dim, memory hidden (E = memory_expand*D) */
+  int32_t chunk;            /* config.chunk_size   (config.py:14) */
+  int32_t omega;            /* config.omega_window (config.py:17) */
+  int32_t ns_steps;         /* config.ns_steps     (config.py:16), 1..5 */
+  int32_t pe_ste;           /* config.pe_ste       (config.py:21) */
+  int32_t stop_grad_chunks; /* config.stop_grad_chunks (config.py:29) */
+  int32_t act_dtype;        /* ATLAS_F32 or ATLAS_BF16 */
+  int32_t precision;        /* ATLAS_PREC_EXACT or ATLAS_PREC_TENSOR */
+} AtlasScanParams;
+
+/* ABI version of the loaded library. */
+int atlas_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* atlas_last_error_string(void);
+
+/* Bytes of the `saved` buffer atlas_scan_fwd fills for atlas_scan_bwd: the
+ * float32 carry entering every chunk (the reference recomputes each chunk from
+ * its checkpointed carry, memory_layer.py:675). */
+size_t atlas_scan_saved_bytes(const AtlasScanParams* p);
+
+/* Bytes of scratch memory the forward / backward need. */
+size_t atlas_scan_workspace_bytes(const AtlasScanParams* p);
+
+/* Forward scan.  Replaces memory_layer.py:635-718 (scan part of the layer).
+ * state_in may be NULL: the LM-path initial state W1=0, W2=[I;0], S=0 is used
+ * (atlas_jax/model.py:251-264).  saved may be NULL when no backward follows. */
+int atlas_scan_fwd(const AtlasScanParams* p,
+                   const void* q, const void* k, const void* v,
+                   const float* alpha, const float* eta, const float* theta, const float* gamma,
+                   const float* W1_in, const float* W2_in, const float* S1_in, const float* S2_in,
+                   void* y,
+                   float* W1_out, float* W2_out, float* S1_out, float* S2_out,
+                   void* saved, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward scan: the VJP of atlas_scan_fwd, which the reference obtains from
+ * JAX autodiff of the checkpointed lax.scan (memory_layer.py:675, 711).
+ * dW1_out..dS2_out are the cotangents of the final state (each may be NULL =
+ * zero).  dW1_in..dS2_in receive the cotangents of the initial state.
+ * `saved` must come from the atlas_scan_fwd call with the same inputs. */
+int atlas_scan_bwd(const AtlasScanParams* p,
+                   const void* q, const void* k, const void* v,
+                   const float* alpha, const float* eta, const float* theta, const float* gamma,
+                   const void* saved, const void* dy,
+                   const float* dW1_out, const float* dW2_out, const float* dS1_out, const float* dS2_out,
+                   void* dq, void* dk, void* dv,
+                   float* dalpha, float* deta, float* dtheta, float* dgamma,
+                   float* dW1_in, float* dW2_in, float* dS1_in, float* dS2_in,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Batched Polar Express on float32 (batch, rows, cols) matrices, out-of-place.
+ * Replaces fused_polar_express (atlas_jax/kernels/triton_pe.py:26-69, same math
+ * as memory_layer.py:43-71) and the Muon orthogonalisation call site
+ * (atlas_jax/optim.py:68-83, which omits the 1e-12 inside the square root:
+ * pass eps_in_sqrt = 0 for that behaviour, 1e-12 for the memory layer's). */
+int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t rows, int32_t cols,
+                                int32_t ns_steps, float eps_in_sqrt, int32_t precision,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes atlas_polar_express_batched needs for this problem. */
+size_t atlas_polar_express_workspace_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ns_steps,
+                                           int32_t precision);
+
+/* Reads and clears the device status word of the calling device after the
+ * caller synchronised the stream (ATLAS_OK or ATLAS_ERR_DEVICE_TIMEOUT). */
+int atlas_scan_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATLAS_SCAN_H_ */

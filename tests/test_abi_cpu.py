@@ -1,0 +1,48 @@
+"""CPU checks of the C ABI library: it loads, exports every declared symbol,
+and rejects bad arguments before touching the GPU."""
+import ctypes
+
+import pytest
+
+from atlas_b200 import _lib as L
+
+
+def test_library_exports_every_header_function():
+    lib = L.load()
+    names = L.header_functions()
+    assert "atlas_scan_fwd" in names and "atlas_scan_bwd" in names
+    for n in names:
+        assert hasattr(lib, n), n
+    assert lib.atlas_abi_version() == L.ATLAS_ABI_VERSION
+
+
+def _p(**kw):
+    base = dict(B=2, T=100, H=3, D=32, E=128, chunk=64, omega=8, ns_steps=5, pe_ste=0, stop_grad_chunks=0,
+                act_dtype=L.ATLAS_F32, precision=L.ATLAS_PREC_EXACT)
+    base.update(kw)
+    return L.AtlasScanParams(L.ATLAS_ABI_VERSION, *[base[k] for k in (
+        "B", "T", "H", "D", "E", "chunk", "omega", "ns_steps", "pe_ste", "stop_grad_chunks", "act_dtype",
+        "precision")])
+
+
+def test_sizes_and_validation():
+    lib = L.load()
+    p = _p()
+    # exact path saves float64 carries: B*H*ceil(T/cs)*4*D*E*8
+    assert lib.atlas_scan_saved_bytes(ctypes.byref(p)) == 2 * 3 * 2 * 4 * 32 * 128 * 8
+    assert lib.atlas_scan_workspace_bytes(ctypes.byref(p)) > 0
+    bad = _p(ns_steps=7)
+    assert lib.atlas_scan_saved_bytes(ctypes.byref(bad)) == 0
+    assert b"ns_steps" in lib.atlas_last_error_string()
+    bad = _p()
+    bad.abi_version = 99
+    rc = lib.atlas_scan_fwd(ctypes.byref(bad), *([None] * 18), 0, None)
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT
+    rc = lib.atlas_scan_fwd(ctypes.byref(p), *([None] * 18), 0, None)
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT and b"non-NULL" in lib.atlas_last_error_string()
+
+
+def test_polar_express_rejects_empty():
+    lib = L.load()
+    assert lib.atlas_polar_express_batched(None, None, 0, 4, 4, 5, 1e-12, 0, None, 0, None) \
+        == L.ATLAS_ERR_INVALID_ARGUMENT
