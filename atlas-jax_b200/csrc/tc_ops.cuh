@@ -1,0 +1,131 @@
+// Thin inline-PTX layer over the sm_100a tensor-core (tcgen05) instructions
+// used by the scan kernels: TMEM allocation, shared-memory matrix descriptors,
+// the kind::f16 MMA, commit-to-mbarrier, TMEM loads, and bounded mbarrier waits.
+//
+// Shared-memory operand layout ("core-matrix tiles", no swizzle): a logical
+// R x C bf16 tile is stored as 8x8 core matrices of 128 contiguous bytes
+// (8 rows x 16 bytes).  Element (r, c) lives at
+//     (r / 8) * RBS + (c / 8) * 128 + (r % 8) * 16 + (c % 8) * 2,   RBS = 16 * C.
+// The same bytes serve as a K-major operand (rows = M/N index, cols = K index)
+// and as an MN-major operand (rows = K index, cols = M/N index); only the
+// descriptor's leading (K-direction) and stride (MN-direction) byte offsets and
+// the instruction descriptor's major bits differ.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace atlas {
+namespace tcx {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// byte offset of element (r, c) in an R x C core-matrix tile
+__device__ __forceinline__ uint32_t cm_off(int r, int c, int C) {
+  return (uint32_t)((r >> 3) * (C << 4) + (c >> 3) * 128 + ((r & 7) << 4) + ((c & 7) << 1));
+}
+
+// SM100 shared-memory matrix descriptor, SWIZZLE_NONE, version 1.
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // version (Blackwell)
+  // base offset 0, lbo mode 0, layout type 0 (no swizzle)
+  return d;
+}
+
+// K-major operand from a core-matrix tile whose rows are the M/N index:
+// K direction = next column block (128 B), MN direction = next row block.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr, int tileC) {
+  return make_desc(saddr, 128, (uint32_t)tileC * 16);
+}
+// MN-major operand from a tile whose rows are the K index and columns the M/N index.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr, int tileC) {
+  return make_desc(saddr, (uint32_t)tileC * 16, 128);
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                 // D format f32
+         | (1u << 7)               // A bf16
+         | (1u << 10)              // B bf16
+         | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(mbar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// generic-proxy smem writes -> visible to the tensor core (async proxy)
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- TMEM allocation (whole warp) ----
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- TMEM loads: warp reads its 32-lane quadrant, each thread one lane ----
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- mbarrier ----
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~max_iters polls and returns false (the caller
+// records ATLAS_ERR_DEVICE_TIMEOUT and unwinds) instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iters = 20000000u) {
+  for (uint32_t i = 0; i < max_iters; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+}  // namespace tcx
+}  // namespace atlas
