@@ -1,16 +1,620 @@
-// tcgen05 (sm_100a) Atlas scan -- placeholder until the fused kernels land.
+// tcgen05 (sm_100a) Atlas scan, forward.
+//
+// Work decomposition
+//   A (b, h) pair is a "chain" of chunks that must run in order.  A 2-CTA
+//   cluster processes one (chain, chunk) item at a time: CTA rank 0 owns the
+//   memory matrix W1 (and its momentum S1), rank 1 owns W2 / S2.  Items are
+//   dealt to a persistent grid of clusters in chunk-major order
+//   (item k -> chain k % NC, chunk k / NC), so a chain migrates between
+//   clusters from chunk to chunk and every SM stays busy even when the number
+//   of chains is not a multiple of the number of clusters.  The carry between
+//   chunks goes through global memory (it is the `saved` buffer the backward
+//   needs anyway); a per-chain counter released after the carry is written
+//   orders the items of one chain.
+//
+// Per chunk (memory_layer.py:496-597)
+//   * frozen-state pass on CUDA cores in float32, both CTAs reading the carry
+//     from global memory: h = W2 k, act = gelu(h), err = k + W1 act - v and, on
+//     rank 1, chain = (W1^T err) * gelu'(h).  Each CTA keeps the rank-1 factors
+//     of its own per-token gradient: rank 0 u1^T = act err^T, rank 1 u2 = chain k^T.
+//   * per token: S <- theta S - eta * (2/D) sum_{i in window} gamma_i f_i g_i^T in
+//     float32 registers; X0 = S / (1.01 ||S|| + 1e-6); five Polar Express steps on
+//     the tensor cores; W <- alpha W + X5; read-out y = q + W1 gelu(W2 q) with the
+//     gelu(W2 q) vector exchanged through distributed shared memory.
+//
+// Numerics: every Polar Express product runs as three bf16 MMAs
+// (hi*hi + hi*lo + lo*hi, float32 accumulation in TMEM), i.e. ~16 mantissa bits
+// per operand.  A single bf16 pass is not enough: Polar Express amplifies noise
+// in the near-null directions of the low-rank momentum by ~1e3.
+//
+// Storage: each CTA keeps its matrix in the E x D orientation ("tile"): rank 0
+// holds W1^T and S1^T, rank 1 holds W2 and S2.  Polar Express of the wide D x E
+// matrix then reads  A = X~^T X~ (Gram over E),  X~' = X~ B'^T  with
+// B' = a I + b A + c A^2.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "scan_internal.h"
+#include "tc_ops.cuh"
 
 namespace atlas {
 namespace tc {
-bool supported(const AtlasScanParams&, const char** why) {
-  *why = "not built yet";
-  return false;
+using namespace tcx;
+
+constexpr int D = 64;
+constexpr int E = 256;
+constexpr int NT = 256;      // 8 warps: warp w -> TMEM lane quadrant w % 4, column half w / 4
+constexpr int MAXCS = 64;
+constexpr int DE = D * E;
+constexpr int XT_BYTES = E * D * 2;  // bf16 E x D tile
+constexpr int AT_BYTES = D * D * 2;  // bf16 D x D tile
+constexpr int TMEM_COLS = 256;
+// TMEM column map
+constexpr uint32_t TM_X = 0;      // X~ update: rows 0-127 in cols [0,64), rows 128-255 in [64,128)
+constexpr uint32_t TM_GRAM = 128; // Gram A (M=64 layout)
+constexpr uint32_t TM_A2 = 192;   // A*A    (M=64 layout)
+
+struct __align__(1024) Smem {
+  uint8_t Xh[XT_BYTES];   // X~ hi / lo tiles (frozen pass: float scratch)
+  uint8_t Xl[XT_BYTES];
+  uint8_t Ah[AT_BYTES];   // A hi / lo
+  uint8_t Al[AT_BYTES];
+  uint8_t Bh[AT_BYTES];   // B' hi / lo
+  uint8_t Bl[AT_BYTES];
+  float F[MAXCS * E];     // per-token row factor: act (rank 0) or chain (rank 1)
+  float G[MAXCS * D];     // per-token column factor: err (rank 0) or k (rank 1)
+  float Q[MAXCS * D];     // queries of the chunk
+  float gate[4][MAXCS];   // alpha, eta, theta, gamma
+  float zbuf[2][E];
+  float pbuf[2][E];       // gelu(W2 q) written by rank 1 into rank 0
+  float ybuf[4][D];
+  float red[8];
+  uint64_t bar;
+  uint32_t tmem;
+  int bad;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
-size_t saved_bytes(const AtlasScanParams&) { return 0; }
-size_t workspace_bytes(const AtlasScanParams&) { return 0; }
-cudaError_t launch_fwd(const FwdArgs&, cudaStream_t) { return cudaErrorNotSupported; }
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_remote_f32(const float* local_addr, uint32_t rank, float v) {
+  uint32_t la = smem_u32(local_addr), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Split 8 consecutive float32 values into bf16 hi and lo parts and store them
+// as one 16-byte core-matrix row segment in each tile.
+__device__ __forceinline__ void store_split8(uint8_t* th, uint8_t* tl, uint32_t off, const float* v) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * k]);
+    __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * k + 1]);
+    __nv_bfloat16 l0 = __float2bfloat16_rn(v[2 * k] - __bfloat162float(h0));
+    __nv_bfloat16 l1 = __float2bfloat16_rn(v[2 * k + 1] - __bfloat162float(h1));
+    h[k] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+    l[k] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+  }
+  *(uint4*)(th + off) = make_uint4(h[0], h[1], h[2], h[3]);
+  *(uint4*)(tl + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+// 32 consecutive columns [c0, c0+32) of row r of a tile with C columns.
+__device__ __forceinline__ void store_split32(uint8_t* th, uint8_t* tl, int r, int c0, int C, const float* v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) store_split8(th, tl, cm_off(r, c0 + 8 * k, C), v + 8 * k);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  tmem_ld16(taddr, v);
+  tmem_ld16(taddr + 16, v + 16);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  return s;
+}
+
+// Reduce-scatter of 32 per-lane values over a warp: afterwards lane l holds the
+// warp-wide sum of element l in v[0].
+__device__ __forceinline__ float warp_reduce_scatter32(float* v) {
+  const int l = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool up = (l & s) != 0;
+#pragma unroll
+    for (int k = 0; k < s; ++k) {
+      float send = up ? v[k] : v[k + s];
+      float keep = up ? v[k + s] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+}  // namespace tc
+}  // namespace atlas
+
+namespace atlas {
+namespace tc {
+
+// ---- MMA issue (one thread) -----------------------------------------------
+// Gram A = X~^T X~ (M = N = D, K = E), both operands MN-major views of the X~ tiles.
+__device__ void issue_gram(Smem& s, uint32_t tm) {
+  const uint32_t id = idesc_bf16(64, 64, true, true);
+  const uint8_t* ta[3] = {s.Xh, s.Xh, s.Xl};
+  const uint8_t* tb[3] = {s.Xh, s.Xl, s.Xh};
+  for (int t = 0; t < 3; ++t)
+    for (int ks = 0; ks < E / 16; ++ks) {
+      uint64_t da = desc_mnmajor(smem_u32(ta[t]) + ks * 2 * (16 * D), D);
+      uint64_t db = desc_mnmajor(smem_u32(tb[t]) + ks * 2 * (16 * D), D);
+      mma_bf16(tm + TM_GRAM, da, db, id, (t | ks) != 0);
+    }
+}
+// A^2 (M = N = K = D): A operand K-major rows = r; B operand MN-major (rows = k).
+__device__ void issue_a2(Smem& s, uint32_t tm) {
+  const uint32_t id = idesc_bf16(64, 64, false, true);
+  const uint8_t* ta[3] = {s.Ah, s.Ah, s.Al};
+  const uint8_t* tb[3] = {s.Ah, s.Al, s.Ah};
+  for (int t = 0; t < 3; ++t)
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint64_t da = desc_kmajor(smem_u32(ta[t]) + ks * 256, D);
+      uint64_t db = desc_mnmajor(smem_u32(tb[t]) + ks * 2 * (16 * D), D);
+      mma_bf16(tm + TM_A2, da, db, id, (t | ks) != 0);
+    }
+}
+// X~' = X~ B'^T (M = E as two 128-row halves, N = K = D), both operands K-major.
+__device__ void issue_xb(Smem& s, uint32_t tm) {
+  const uint32_t id = idesc_bf16(128, 64, false, false);
+  const uint8_t* ta[3] = {s.Xh, s.Xh, s.Xl};
+  const uint8_t* tb[3] = {s.Bh, s.Bl, s.Bh};
+  for (int h = 0; h < 2; ++h)
+    for (int t = 0; t < 3; ++t)
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint64_t da = desc_kmajor(smem_u32(ta[t]) + h * (128 / 8) * (16 * D) + ks * 256, D);
+        uint64_t db = desc_kmajor(smem_u32(tb[t]) + ks * 256, D);
+        mma_bf16(tm + TM_X + h * 64, da, db, id, (t | ks) != 0);
+      }
+}
+
+// All threads: make the freshly written operand tiles visible to the tensor
+// core, run `issue` on thread 0, wait for completion.  Returns false on timeout.
+template <typename F>
+__device__ __forceinline__ bool run_mma(Smem& s, uint32_t tm, uint32_t& phase, F issue) {
+  fence_async_smem();
+  fence_before();
+  __syncthreads();
+  if (s.bad) return false;  // an earlier wait expired: skip the work, keep the control flow
+  if (threadIdx.x == 0) {
+    fence_after();
+    issue(s, tm);
+    mma_commit(&s.bar);
+  }
+  bool ok = mbar_wait(&s.bar, phase);
+  phase ^= 1;
+  fence_after();
+  return ok;
+}
+
+struct Item {
+  int q, c;
+};
+
+// Carry slot entering chunk c of chain q: [matrix m][W, S][E x D tile].
+__device__ __forceinline__ float* carry_slot(const FwdArgs& a, float* carries, int q, int c, int nch) {
+  return a.saved ? (float*)a.saved + ((size_t)q * nch + c) * 4 * DE : carries + (size_t)q * 4 * DE;
+}
+
+// Frozen-state pass of one chunk (memory_layer.py:504-520), float32 CUDA cores.
+template <typename TA>
+__device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, int b, int hh, int c, int cs,
+                            uint32_t rank) {
+  const AtlasScanParams& P = a.p;
+  const int T = P.T, H = P.H;
+  const TA* kp = (const TA*)a.k;
+  const TA* vp = (const TA*)a.v;
+  const TA* qp = (const TA*)a.q;
+  const float* W1t = slot;            // W1^T: [e][d]
+  const float* W2 = slot + 2 * DE;    // W2:   [e][d]
+  float* kbuf = (float*)s.Ah;         // cs x D  (Ah..Al, 16 KB)
+  float* errb = rank ? (float*)s.Bh : s.G;  // cs x D
+  float* actb = rank ? (float*)s.Xh : s.F;  // cs x E
+  const int tid = threadIdx.x;
+  for (int i = tid; i < cs * D; i += NT) {
+    int r = i / D, d = i % D, t = c * cs + r;
+    size_t o = (((size_t)b * T + t) * H + hh) * D + d;
+    kbuf[i] = t < T ? ld_act(kp, o) : 0.f;
+    s.Q[i] = t < T ? ld_act(qp, o) : 0.f;
+  }
+  for (int r = tid; r < cs; r += NT) {
+    Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + r);
+    s.gate[0][r] = g.a;
+    s.gate[1][r] = g.e;
+    s.gate[2][r] = g.t;
+    s.gate[3][r] = g.g;
+  }
+  __syncthreads();
+  {  // h = W2 k ; thread e
+    const int e = tid;
+    float w[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) w[d] = W2[e * D + d];
+    for (int r = 0; r < cs; ++r) {
+      float hv = 0.f;
+#pragma unroll
+      for (int d = 0; d < D; ++d) hv = fmaf(w[d], kbuf[r * D + d], hv);
+      actb[r * E + e] = gelu_tanh(hv);
+      if (rank) s.F[r * E + e] = hv;  // keep h for gelu'(h)
+    }
+  }
+  __syncthreads();
+  {  // err = k + W1 act - v ; thread (d, token group)
+    const int d = tid % D, grp = tid / D;  // 4 groups
+    const int per = (cs + 3) / 4;
+    float acc[MAXCS / 4];
+#pragma unroll
+    for (int j = 0; j < MAXCS / 4; ++j) acc[j] = 0.f;
+    for (int e = 0; e < E; ++e) {
+      float w = W1t[e * D + d];
+#pragma unroll
+      for (int j = 0; j < MAXCS / 4; ++j) {
+        int r = grp * per + j;
+        if (j < per && r < cs) acc[j] = fmaf(w, actb[r * E + e], acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < MAXCS / 4; ++j) {
+      int r = grp * per + j, t = c * cs + r;
+      if (j < per && r < cs) {
+        float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
+        errb[r * D + d] = kbuf[r * D + d] + acc[j] - vv;
+      }
+    }
+  }
+  __syncthreads();
+  if (rank) {  // chain = (W1^T err) * gelu'(h) ; thread e
+    const int e = tid;
+    float w[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) w[d] = W1t[e * D + d];
+    for (int r = 0; r < cs; ++r) {
+      float rv = 0.f;
+#pragma unroll
+      for (int d = 0; d < D; ++d) rv = fmaf(w[d], errb[r * D + d], rv);
+      s.F[r * E + e] = rv * gelu_erf_prime(s.F[r * E + e]);
+    }
+    for (int i = tid; i < cs * D; i += NT) s.G[i] = kbuf[i];
+  }
+  __syncthreads();
+}
+
+size_t bwd_workspace_bytes(const AtlasScanParams& p);
+
+struct KArgs {
+  FwdArgs a;
+  int nchains, nch;
+  float* carries;  // used when a.saved == nullptr: one slot per chain
+  int* flags;      // chunks completed per chain (zeroed before launch)
+};
+
+template <typename TA>
+__global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const FwdArgs& a = K.a;
+  const AtlasScanParams& P = a.p;
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+  const int qd = w & 3, ch = w >> 2;
+  const int e0 = 32 * qd + l, e1 = e0 + 128, dc = 32 * ch;
+  const uint32_t rank = cluster_rank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int cs = P.chunk, T = P.T, H = P.H, nch = K.nch;
+  const float sc = 2.0f / D;
+  const bool win = P.omega > 1;
+  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+
+  if (w == 0) {
+    tmem_alloc(&s.tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&s.bar, 1);
+    fence_mbar_init();
+    s.bad = 0;
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tm = s.tmem;
+  uint32_t phase = 0;
+
+  float Sv[2][32], Wv[2][32];
+  const long total = (long)K.nchains * nch;
+  for (long k = cluster; k < total; k += nclusters) {
+    const int q = (int)(k % K.nchains), c = (int)(k / K.nchains);
+    const int b = q / H, hh = q % H;
+    // ---- wait for the previous chunk of this chain ----
+    if (c > 0 && tid == 0 && !s.bad) {
+      int spins = 0;
+      while (ld_acquire(&K.flags[q]) < c) {
+        __nanosleep(200);
+        if (++spins > 50000000) {
+          set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
+          s.bad = 1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    float* slot = carry_slot(a, K.carries, q, c, nch);
+    float* mine = slot + 2 * rank * DE;  // [W, S] of this CTA's matrix
+    if (c == 0) {  // initial carry: caller's state or the LM init (model.py:251-264)
+      for (int i = tid; i < DE; i += NT) {
+        int e = i / D, d = i % D;
+        size_t bh = (size_t)q * DE;
+        float wv, sv;
+        if (rank == 0) {  // W1, S1 are (D, E): tile holds the transpose
+          wv = a.W1_in ? a.W1_in[bh + (size_t)d * E + e] : 0.f;
+          sv = a.S1_in ? a.S1_in[bh + (size_t)d * E + e] : 0.f;
+        } else {
+          wv = a.W2_in ? a.W2_in[bh + i] : (e == d ? 1.f : 0.f);
+          sv = a.S2_in ? a.S2_in[bh + i] : 0.f;
+        }
+        mine[i] = wv;
+        mine[DE + i] = sv;
+      }
+      __threadfence();
+    }
+    cluster_sync();
+    frozen_pass<TA>(a, s, slot, b, hh, c, cs, rank);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      Wv[0][j] = mine[e0 * D + dc + j];
+      Wv[1][j] = mine[e1 * D + dc + j];
+      Sv[0][j] = mine[DE + e0 * D + dc + j];
+      Sv[1][j] = mine[DE + e1 * D + dc + j];
+    }
+    cluster_sync();  // both CTAs are done reading the carry slot
+
+    for (int r = 0; r < cs; ++r) {
+      const float al = s.gate[0][r], et = s.gate[1][r], th = s.gate[2][r];
+      // ---- momentum: S <- theta S - eta * s * sum_i gamma_i f_i g_i^T ----
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        Sv[0][j] *= th;
+        Sv[1][j] *= th;
+      }
+      const int i0 = win ? max(0, r - P.omega + 1) : r;
+      for (int i = i0; i <= r; ++i) {
+        const float wgt = -et * sc * (win ? s.gate[3][i] : 1.f);
+        const float f0 = wgt * s.F[i * E + e0], f1 = wgt * s.F[i * E + e1];
+        const float4* g4 = (const float4*)&s.G[i * D + dc];
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float4 g = g4[j4];
+          Sv[0][4 * j4 + 0] = fmaf(f0, g.x, Sv[0][4 * j4 + 0]);
+          Sv[0][4 * j4 + 1] = fmaf(f0, g.y, Sv[0][4 * j4 + 1]);
+          Sv[0][4 * j4 + 2] = fmaf(f0, g.z, Sv[0][4 * j4 + 2]);
+          Sv[0][4 * j4 + 3] = fmaf(f0, g.w, Sv[0][4 * j4 + 3]);
+          Sv[1][4 * j4 + 0] = fmaf(f1, g.x, Sv[1][4 * j4 + 0]);
+          Sv[1][4 * j4 + 1] = fmaf(f1, g.y, Sv[1][4 * j4 + 1]);
+          Sv[1][4 * j4 + 2] = fmaf(f1, g.z, Sv[1][4 * j4 + 2]);
+          Sv[1][4 * j4 + 3] = fmaf(f1, g.w, Sv[1][4 * j4 + 3]);
+        }
+      }
+      // ---- Frobenius normalisation (memory_layer.py:55-56) ----
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(Sv[0][j], Sv[0][j], fmaf(Sv[1][j], Sv[1][j], ss));
+      ss = block_sum(ss, s.red);
+      const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
+      float xv[32];
+      if (P.ns_steps == 0) {  // W += S / kappa
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          Wv[0][j] = al * Wv[0][j] + Sv[0][j] * inv;
+          Wv[1][j] = al * Wv[1][j] + Sv[1][j] * inv;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) xv[j] = Sv[0][j] * inv;
+        store_split32(s.Xh, s.Xl, e0, dc, D, xv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) xv[j] = Sv[1][j] * inv;
+        store_split32(s.Xh, s.Xl, e1, dc, D, xv);
+      }
+      // ---- Polar Express (memory_layer.py:43-71), tall/wide folded into the tile orientation ----
+      for (int st = 0; st < P.ns_steps; ++st) {
+        const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
+        bool ok = run_mma(s, tm, phase, issue_gram);
+        float av[32];
+        tmem_ld32(tm + lane_off + TM_GRAM + dc, av);
+        tmem_wait_ld();
+        const int ra = 16 * qd + l;  // Gram row held by lanes 0-15 of the quadrant
+        if (l < 16) store_split32(s.Ah, s.Al, ra, dc, D, av);
+        ok = ok && run_mma(s, tm, phase, issue_a2);
+        float a2[32];
+        tmem_ld32(tm + lane_off + TM_A2 + dc, a2);
+        tmem_wait_ld();
+        if (l < 16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
+          store_split32(s.Bh, s.Bl, ra, dc, D, a2);  // B'[ra][c]: rows = N index of X~ B'^T
+        }
+        ok = ok && run_mma(s, tm, phase, issue_xb);
+        if (!ok && !s.bad) {
+          set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
+          s.bad = 1;
+        }
+        float x0[32], x1[32];
+        tmem_ld32(tm + lane_off + TM_X + dc, x0);
+        tmem_ld32(tm + lane_off + TM_X + 64 + dc, x1);
+        tmem_wait_ld();
+        if (st + 1 < P.ns_steps) {
+          store_split32(s.Xh, s.Xl, e0, dc, D, x0);
+          store_split32(s.Xh, s.Xl, e1, dc, D, x1);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            Wv[0][j] = fmaf(al, Wv[0][j], x0[j]);
+            Wv[1][j] = fmaf(al, Wv[1][j], x1[j]);
+          }
+        }
+      }
+      // ---- read-out y = q + W1 gelu(W2 q)  (memory_layer.py:592-595) ----
+      const float* qv = &s.Q[r * D + dc];
+      if (rank == 1) {
+        float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          z0 = fmaf(Wv[0][j], qv[j], z0);
+          z1 = fmaf(Wv[1][j], qv[j], z1);
+        }
+        s.zbuf[ch][e0] = z0;
+        s.zbuf[ch][e1] = z1;
+        __syncthreads();
+        const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
+        st_remote_f32(&s.pbuf[r & 1][tid], 0, gelu_tanh(z));
+        cluster_sync();
+      } else {
+        cluster_sync();
+        const float p0 = s.pbuf[r & 1][e0], p1 = s.pbuf[r & 1][e1];
+        float yv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) yv[j] = fmaf(Wv[0][j], p0, Wv[1][j] * p1);
+        float part = warp_reduce_scatter32(yv);
+        s.ybuf[qd][dc + l] = part;
+        __syncthreads();
+        const int t = c * cs + r;
+        if (tid < D && t < T) {
+          float y = s.Q[r * D + tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
+          st_act((TA*)a.y, (((size_t)b * T + t) * H + hh) * D + tid, y);
+        }
+      }
+    }
+    // ---- carry out ----
+    if (c + 1 < nch) {
+      float* nxt = carry_slot(a, K.carries, q, c + 1, nch) + 2 * rank * DE;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        nxt[e0 * D + dc + j] = Wv[0][j];
+        nxt[e1 * D + dc + j] = Wv[1][j];
+        nxt[DE + e0 * D + dc + j] = Sv[0][j];
+        nxt[DE + e1 * D + dc + j] = Sv[1][j];
+      }
+    } else {
+      const size_t bh = (size_t)q * DE;
+      float* Wo = rank ? a.W2_out : a.W1_out;
+      float* So = rank ? a.S2_out : a.S1_out;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int e = h2 ? e1 : e0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int d = dc + j;
+          const size_t o = rank ? bh + (size_t)e * D + d : bh + (size_t)d * E + e;
+          if (Wo) Wo[o] = Wv[h2][j];
+          if (So) So[o] = Sv[h2][j];
+        }
+      }
+    }
+    __threadfence();
+    cluster_sync();
+    if (rank == 0 && tid == 0) st_release(&K.flags[q], c + 1);
+  }
+  fence_before();
+  __syncthreads();
+  if (w == 0) tmem_dealloc(tm, TMEM_COLS);
+}
+
+// ---- host side ----------------------------------------------------------------
+bool supported(const AtlasScanParams& p, const char** why) {
+  if (p.D != D || p.E != E) {
+    *why = "tcgen05 path is built for head_dim 64, memory hidden 256";
+    return false;
+  }
+  if (p.chunk > MAXCS) {
+    *why = "tcgen05 path supports chunk <= 64";
+    return false;
+  }
+  return true;
+}
+size_t saved_bytes(const AtlasScanParams& p) { return (size_t)p.B * p.H * n_chunks(p) * 4 * DE * sizeof(float); }
+static size_t flags_bytes(const AtlasScanParams& p) { return (((size_t)p.B * p.H * sizeof(int)) + 255) & ~size_t(255); }
+size_t workspace_bytes(const AtlasScanParams& p) {
+  return flags_bytes(p) + (size_t)p.B * p.H * 4 * DE * sizeof(float) + bwd_workspace_bytes(p);
+}
+
+static int g_max_clusters = -1;
+
+template <typename TA>
+static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) {
+  size_t smem = sizeof(Smem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(fwd_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * nclusters);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (g_max_clusters < 0) {
+    int n = 0;
+    cfg.gridDim = dim3(2);
+    if (cudaOccupancyMaxActiveClusters(&n, fwd_kernel<TA>, &cfg) != cudaSuccess || n <= 0) n = 1;
+    g_max_clusters = n;
+    cfg.gridDim = dim3(2 * nclusters);
+  }
+  if (nclusters > g_max_clusters) cfg.gridDim = dim3(2 * g_max_clusters);
+  return cudaLaunchKernelEx(&cfg, fwd_kernel<TA>, k);
+}
+
+cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
+  KArgs k;
+  k.a = a;
+  k.nchains = a.p.B * a.p.H;
+  k.nch = n_chunks(a.p);
+  uint8_t* ws = (uint8_t*)a.ws;
+  k.flags = (int*)ws;
+  k.carries = (float*)(ws + flags_bytes(a.p));
+  cudaError_t e = cudaMemsetAsync(k.flags, 0, flags_bytes(a.p), st);
+  if (e != cudaSuccess) return e;
+  int ncl = k.nchains;
+  return a.p.act_dtype == ATLAS_BF16 ? launch_fwd_t<__nv_bfloat16>(k, ncl, st) : launch_fwd_t<float>(k, ncl, st);
+}
+
+}  // namespace tc
+}  // namespace atlas
+
+namespace atlas {
+namespace tc {
+size_t bwd_workspace_bytes(const AtlasScanParams&) { return 0; }
 cudaError_t launch_bwd(const BwdArgs&, cudaStream_t) { return cudaErrorNotSupported; }
 }  // namespace tc
 }  // namespace atlas
