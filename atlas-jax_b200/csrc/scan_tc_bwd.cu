@@ -1,0 +1,864 @@
+// tcgen05 (sm_100a) Atlas scan, backward: the VJP of the forward kernel in
+// scan_tc.cu, i.e. of atlas_jax/memory_layer.py:496-718 (the reference gets it
+// from JAX autodiff of the per-chunk jax.checkpoint'ed lax.scan, 675 / 711).
+//
+// Work decomposition mirrors the forward: a 2-CTA cluster (rank 0: W1/S1,
+// rank 1: W2/S2) processes one (chain, chunk) item at a time, items dealt in
+// reverse chunk order to a persistent grid; the cotangent of the carry flows
+// from chunk c+1 to chunk c through a per-chain global slot ordered by a
+// released counter.
+//
+// Per item:
+//   A. frozen-state pass recomputed from the saved chunk-start carry (CUDA cores,
+//      float32) into a per-cluster L2 scratch: h, act, err, r = W1^T err, chain, k.
+//   B. forward recompute over the chunk's tokens: momentum update, Polar
+//      Express (tensor cores), memory update, read-out backward pieces
+//      (p = gelu(W2 q), dz = (W1^T dy) * gelu'(W2 q), dq = dy + W2^T dz).  S_t,
+//      W_{t-1} and p / dz are saved per token in scratch.
+//   C. reverse over tokens with dW, dS in float32 registers: read-out and memory
+//      scan cotangents, Polar Express VJP on the tensor cores (recomputing the five
+//      Newton-Schulz steps of S_t and keeping their operand tiles in scratch),
+//      momentum scan cotangents, and the Omega-window terms that feed the
+//      rank-1 factors (accumulated with global reductions).
+//   D. frozen-state pass backward (CUDA cores), carry cotangent out.
+//
+// Polar Express VJP of one step, tile orientation (X~ = X^T, G~ = dX~_{k+1}):
+//   X~_{k+1} = X~ B'^T,  B' = a I + b A + c A A,  A = X~^T X~
+//   P   = G~^T X~                       (dB')
+//   Sym = dA + dA^T = b Ps + c (Ps A + A Ps),  Ps = P + P^T
+//   dX~ = G~ B' + X~ Sym
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "scan_internal.h"
+#include "tc_common.cuh"
+
+namespace atlas {
+namespace tc {
+
+namespace bwd {
+
+struct __align__(1024) Smem {
+  uint8_t Xh[XT_BYTES];  // X~_k tiles (phase D: float dw1t)
+  uint8_t Xl[XT_BYTES];
+  uint8_t Gh[XT_BYTES];  // G~ tiles (phase D: float dh)
+  uint8_t Gl[XT_BYTES];
+  uint8_t Ah[AT_BYTES];
+  uint8_t Al[AT_BYTES];
+  uint8_t Bh[AT_BYTES];  // B'_k
+  uint8_t Bl[AT_BYTES];
+  uint8_t Ph[AT_BYTES];  // Ps
+  uint8_t Pl[AT_BYTES];
+  uint8_t Yh[AT_BYTES];  // Sym
+  uint8_t Yl[AT_BYTES];
+  float Pf[D * D];       // P in float32 (transpose); phase A/D: k or derr of the chunk
+  float zbuf[2][E];
+  float xbuf[2][E];      // exchanged vector (p into rank 0, dp into rank 1), double-buffered
+  float ybuf[4][D];
+  float qv[D], dyv[D];
+  float ipacc[MAXCS];
+  float red[8];
+  uint64_t bar;
+  uint32_t tmem;
+  int bad;
+};
+
+// per-cluster scratch, in floats
+constexpr size_t FRZ_E = (size_t)MAXCS * E, FRZ_D = (size_t)MAXCS * D;
+struct ClusterWS {
+  float *h, *act, *chain, *r, *err, *k;    // frozen pass
+  float *dF[2], *dG[2], *scal;             // accumulators: dF/dG per rank; scal[4][MAXCS]
+  float *Ssave[2], *Wsave[2], *vec[2];     // per rank: S_{t-1..}, W_{t-1}, p or dz
+  uint8_t* ns[2];                           // per rank: 5 steps of (X hi, X lo, A hi, A lo, B hi, B lo)
+};
+constexpr size_t NS_STEP_BYTES = 2 * XT_BYTES + 4 * AT_BYTES;
+constexpr size_t RANK_FLOATS = (size_t)(MAXCS + 1) * DE + (size_t)MAXCS * DE + FRZ_E + 5 * NS_STEP_BYTES / 4;
+constexpr size_t CLUSTER_FLOATS = 4 * FRZ_E + 2 * FRZ_D + 2 * FRZ_E + 2 * FRZ_D + 4 * MAXCS + 2 * RANK_FLOATS;
+
+__device__ ClusterWS carve(float* base) {
+  ClusterWS w;
+  float* p = base;
+  w.h = p; p += FRZ_E;
+  w.act = p; p += FRZ_E;
+  w.chain = p; p += FRZ_E;
+  w.r = p; p += FRZ_E;
+  w.err = p; p += FRZ_D;
+  w.k = p; p += FRZ_D;
+  w.dF[0] = p; p += FRZ_E;
+  w.dF[1] = p; p += FRZ_E;
+  w.dG[0] = p; p += FRZ_D;
+  w.dG[1] = p; p += FRZ_D;
+  w.scal = p; p += 4 * MAXCS;
+  for (int r = 0; r < 2; ++r) {
+    w.Ssave[r] = p; p += (size_t)(MAXCS + 1) * DE;
+    w.Wsave[r] = p; p += (size_t)MAXCS * DE;
+    w.vec[r] = p; p += FRZ_E;
+    w.ns[r] = (uint8_t*)p; p += 5 * NS_STEP_BYTES / 4;
+  }
+  return w;
+}
+
+struct KArgs {
+  BwdArgs a;
+  int nchains, nch;
+  int* flags;        // chunks finished per chain, counted from the end
+  float* cot;        // per chain: carry cotangent [m][W, S][E x D]
+  float* cws;        // per cluster scratch
+};
+
+__device__ __forceinline__ void red_add(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// 32 consecutive floats at p (16-byte aligned) <-> registers
+__device__ __forceinline__ void ld32(const float* p, float* v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float4 x = ((const float4*)p)[j];
+    v[4 * j] = x.x; v[4 * j + 1] = x.y; v[4 * j + 2] = x.z; v[4 * j + 3] = x.w;
+  }
+}
+__device__ __forceinline__ void st32(float* p, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ((float4*)p)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+// block-wide copy of n bytes (multiple of 16)
+__device__ __forceinline__ void copy16(void* dst, const void* src, int n) {
+  for (int i = threadIdx.x; i < n / 16; i += NT) ((uint4*)dst)[i] = ((const uint4*)src)[i];
+}
+
+}  // namespace bwd
+}  // namespace tc
+}  // namespace atlas
+
+namespace atlas {
+namespace tc {
+namespace bwd {
+
+// Phase A: frozen-state pass of chunk c into cluster scratch (memory_layer.py:504-520).
+// Rank 0 computes h, act, err; rank 1 then computes r = W1^T err and chain.
+template <typename TA>
+__device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w, const float* slot, int b, int hh,
+                                  int c, int cs, uint32_t rank) {
+  const AtlasScanParams& P = a.p;
+  const int T = P.T, H = P.H, tid = threadIdx.x;
+  const float* W1t = slot;
+  const float* W2 = slot + 2 * DE;
+  float* kb = s.Pf;  // cs x D
+  if (rank == 0) {
+    const TA* kp = (const TA*)a.k;
+    for (int i = tid; i < cs * D; i += NT) {
+      int r = i / D, d = i % D, t = c * cs + r;
+      float kv = t < T ? ld_act(kp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
+      kb[i] = kv;
+      w.k[i] = kv;
+    }
+    __syncthreads();
+    {
+      const int e = tid;
+      float wr[D];
+#pragma unroll
+      for (int d = 0; d < D; ++d) wr[d] = W2[e * D + d];
+      for (int r = 0; r < cs; ++r) {
+        float hv = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) hv = fmaf(wr[d], kb[r * D + d], hv);
+        w.h[r * E + e] = hv;
+        w.act[r * E + e] = gelu_tanh(hv);
+      }
+    }
+    __threadfence_block();
+    __syncthreads();
+    {
+      const TA* vp = (const TA*)a.v;
+      const int d = tid % D, grp = tid / D;
+      const int per = (cs + 3) / 4;
+      float acc[MAXCS / 4];
+#pragma unroll
+      for (int j = 0; j < MAXCS / 4; ++j) acc[j] = 0.f;
+      for (int e = 0; e < E; ++e) {
+        float wv = W1t[e * D + d];
+#pragma unroll
+        for (int j = 0; j < MAXCS / 4; ++j) {
+          int r = grp * per + j;
+          if (j < per && r < cs) acc[j] = fmaf(wv, w.act[r * E + e], acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < MAXCS / 4; ++j) {
+        int r = grp * per + j, t = c * cs + r;
+        if (j < per && r < cs) {
+          float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
+          w.err[r * D + d] = kb[r * D + d] + acc[j] - vv;
+        }
+      }
+    }
+  }
+  __threadfence();
+  cluster_sync();
+  if (rank == 1) {
+    const int e = tid;
+    float wr[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) wr[d] = W1t[e * D + d];
+    for (int r = 0; r < cs; ++r) {
+      float rv = 0.f;
+#pragma unroll
+      for (int d = 0; d < D; ++d) rv = fmaf(wr[d], w.err[r * D + d], rv);
+      w.r[r * E + e] = rv;
+      w.chain[r * E + e] = rv * gelu_erf_prime(w.h[r * E + e]);
+    }
+  }
+  __threadfence();
+  cluster_sync();
+}
+
+// Polar Express forward of the tiles in s.X (X0 already stored), five steps,
+// optionally saving each step's operand tiles to `ns`.  On return the final
+// X~ (float32) is in xo (rows e0 / e1, 32 columns each).
+__device__ bool pe_forward_tc(Smem& s, uint32_t tm, uint32_t& phase, int steps, uint8_t* ns, float (*xo)[32]) {
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
+  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
+  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+  bool ok = true;
+  for (int st = 0; st < steps; ++st) {
+    const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
+    ok = mma_sync_run(&s.bar, &s.bad, phase, [&] { mma3(tm + TM_GRAM, s.Xh, s.Xl, true, s.Xh, s.Xl, true, 64, E, 0, false); }) && ok;
+    float av[32], a2[32];
+    tmem_ld32(tm + lane_off + TM_GRAM + dc, av);
+    tmem_wait_ld();
+    if (l < 16) store_split32(s.Ah, s.Al, ra, dc, D, av);
+    ok = mma_sync_run(&s.bar, &s.bad, phase, [&] { mma3(tm + TM_A2, s.Ah, s.Al, false, s.Ah, s.Al, true, 64, D, 0, false); }) && ok;
+    tmem_ld32(tm + lane_off + TM_A2 + dc, a2);
+    tmem_wait_ld();
+    if (l < 16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
+      store_split32(s.Bh, s.Bl, ra, dc, D, a2);
+    }
+    ok = mma_sync_run(&s.bar, &s.bad, phase, [&] {
+           mma3(tm + TM_X, s.Xh, s.Xl, false, s.Bh, s.Bl, false, 128, D, 0, false);
+           mma3(tm + TM_X + 64, s.Xh, s.Xl, false, s.Bh, s.Bl, false, 128, D, 16384, false);
+         }) && ok;
+    if (ns) {  // operand tiles of this step, for the VJP
+      uint8_t* o = ns + (size_t)st * NS_STEP_BYTES;
+      copy16(o, s.Xh, XT_BYTES);
+      copy16(o + XT_BYTES, s.Xl, XT_BYTES);
+      copy16(o + 2 * XT_BYTES, s.Ah, AT_BYTES);
+      copy16(o + 2 * XT_BYTES + AT_BYTES, s.Al, AT_BYTES);
+      copy16(o + 2 * XT_BYTES + 2 * AT_BYTES, s.Bh, AT_BYTES);
+      copy16(o + 2 * XT_BYTES + 3 * AT_BYTES, s.Bl, AT_BYTES);
+      __syncthreads();  // all reads of X tiles done before they are overwritten
+    }
+    tmem_ld32(tm + lane_off + TM_X + dc, xo[0]);
+    tmem_ld32(tm + lane_off + TM_X + 64 + dc, xo[1]);
+    tmem_wait_ld();
+    if (st + 1 < steps) {
+      store_split32(s.Xh, s.Xl, e0, dc, D, xo[0]);
+      store_split32(s.Xh, s.Xl, e1, dc, D, xo[1]);
+    }
+  }
+  return ok;
+}
+
+}  // namespace bwd
+}  // namespace tc
+}  // namespace atlas
+
+namespace atlas {
+namespace tc {
+namespace bwd {
+
+template <typename TA>
+__global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const BwdArgs& a = K.a;
+  const AtlasScanParams& P = a.p;
+  const int tid = threadIdx.x, wp = tid >> 5, l = tid & 31;
+  const int qd = wp & 3, ch = wp >> 2;
+  const int e0 = 32 * qd + l, e1 = e0 + 128, dc = 32 * ch, ra = 16 * qd + l;
+  const uint32_t rank = cluster_rank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int cs = P.chunk, T = P.T, H = P.H, nch = K.nch;
+  const float sc = 2.0f / D;
+  const bool win = P.omega > 1;
+  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+  const ClusterWS w = carve(K.cws + (size_t)cluster * CLUSTER_FLOATS);
+  float* Ssave = w.Ssave[rank];
+  float* Wsave = w.Wsave[rank];
+  float* vec = w.vec[rank];
+  const float* Fm = rank ? w.chain : w.act;  // row factor of this CTA's per-token gradient
+  const float* Gm = rank ? w.k : w.err;      // column factor
+
+  if (wp == 0) {
+    tmem_alloc(&s.tmem, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&s.bar, 1);
+    fence_mbar_init();
+    s.bad = 0;
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tm = s.tmem;
+  uint32_t phase = 0;
+
+  const long total = (long)K.nchains * nch;
+  for (long kk = cluster; kk < total; kk += nclusters) {
+    const int q = (int)(kk % K.nchains), j = (int)(kk / K.nchains), c = nch - 1 - j;
+    const int b = q / H, hh = q % H;
+    if (j > 0 && tid == 0 && !s.bad) {
+      int spins = 0;
+      while (ld_acquire(&K.flags[q]) < j) {
+        __nanosleep(200);
+        if (++spins > 50000000) {
+          set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
+          s.bad = 1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    const float* slot = (const float*)a.saved + ((size_t)q * nch + c) * 4 * DE;
+    const float* mine = slot + 2 * rank * DE;
+    // zero the accumulators of this cluster (rank 0: dF, rank 1: dG and scalars)
+    if (rank == 0)
+      for (int i = tid; i < 2 * (int)FRZ_E; i += NT) w.dF[0][i] = 0.f;
+    else
+      for (int i = tid; i < 2 * (int)FRZ_D + 4 * MAXCS; i += NT) w.dG[0][i] = 0.f;
+    frozen_to_scratch<TA>(a, s, w, slot, b, hh, c, cs, rank);
+
+    // ================= B: forward recompute over the chunk =================
+    float Sv[2][32], Wv[2][32];
+    ld32(mine + e0 * D + dc, Wv[0]);
+    ld32(mine + e1 * D + dc, Wv[1]);
+    ld32(mine + DE + e0 * D + dc, Sv[0]);
+    ld32(mine + DE + e1 * D + dc, Sv[1]);
+    st32(Ssave + e0 * D + dc, Sv[0]);
+    st32(Ssave + e1 * D + dc, Sv[1]);
+    for (int r = 0; r < cs; ++r) {
+      const int t = c * cs + r;
+      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, t);
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        Sv[0][jj] *= g.t;
+        Sv[1][jj] *= g.t;
+      }
+      const int i0 = win ? max(0, r - P.omega + 1) : r;
+      for (int i = i0; i <= r; ++i) {
+        const float gi = win ? load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + i).g : 1.f;
+        const float wgt = -g.e * sc * gi;
+        const float f0 = wgt * Fm[i * E + e0], f1 = wgt * Fm[i * E + e1];
+        float gv[32];
+        ld32(Gm + i * D + dc, gv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          Sv[0][jj] = fmaf(f0, gv[jj], Sv[0][jj]);
+          Sv[1][jj] = fmaf(f1, gv[jj], Sv[1][jj]);
+        }
+      }
+      st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
+      st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
+      st32(Wsave + (size_t)r * DE + e0 * D + dc, Wv[0]);
+      st32(Wsave + (size_t)r * DE + e1 * D + dc, Wv[1]);
+      float ss = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
+      ss = block_sum(ss, s.red);
+      const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
+      if (P.ns_steps == 0) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          Wv[0][jj] = g.a * Wv[0][jj] + Sv[0][jj] * inv;
+          Wv[1][jj] = g.a * Wv[1][jj] + Sv[1][jj] * inv;
+        }
+      } else {
+        float xo[2][32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          xo[0][jj] = Sv[0][jj] * inv;
+          xo[1][jj] = Sv[1][jj] * inv;
+        }
+        store_split32(s.Xh, s.Xl, e0, dc, D, xo[0]);
+        store_split32(s.Xh, s.Xl, e1, dc, D, xo[1]);
+        if (!pe_forward_tc(s, tm, phase, P.ns_steps, nullptr, xo) && !s.bad) {
+          set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
+          s.bad = 1;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          Wv[0][jj] = fmaf(g.a, Wv[0][jj], xo[0][jj]);
+          Wv[1][jj] = fmaf(g.a, Wv[1][jj], xo[1][jj]);
+        }
+      }
+      // read-out backward pieces (memory_layer.py:592-595)
+      if (tid < D) {
+        const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
+        s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
+        s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
+      }
+      __syncthreads();
+      {
+        const float* xv = rank ? s.qv : s.dyv;  // rank 1: z = W2 q ; rank 0: dp = W1^T dy
+        float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          z0 = fmaf(Wv[0][jj], xv[dc + jj], z0);
+          z1 = fmaf(Wv[1][jj], xv[dc + jj], z1);
+        }
+        s.zbuf[ch][e0] = z0;
+        s.zbuf[ch][e1] = z1;
+        __syncthreads();
+        const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
+        // rank 1 sends p = gelu(z) to rank 0; rank 0 sends dp to rank 1
+        st_remote_f32(&s.xbuf[r & 1][tid], rank ^ 1u, rank ? gelu_tanh(z) : z);
+        cluster_sync();
+        if (rank == 0) {
+          vec[r * E + tid] = s.xbuf[r & 1][tid];  // p_t
+        } else {
+          const float dz = s.xbuf[r & 1][tid] * gelu_tanh_grad(z);
+          vec[r * E + tid] = dz;
+          s.zbuf[0][tid] = dz;
+          __syncthreads();
+          const float dz0 = s.zbuf[0][e0], dz1 = s.zbuf[0][e1];
+          float yv[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(Wv[0][jj], dz0, Wv[1][jj] * dz1);
+          float part = warp_reduce_scatter32(yv);
+          s.ybuf[qd][dc + l] = part;
+          __syncthreads();
+          if (tid < D && t < T) {
+            const float dq = s.dyv[tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
+            st_act((TA*)a.dq, (((size_t)b * T + t) * H + hh) * D + tid, dq);
+          }
+        }
+      }
+      __syncthreads();
+    }
+
+    // ================= C: reverse over the chunk's tokens =================
+    float dW[2][32], dS[2][32];
+    {
+      float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
+      if (j > 0) {
+        ld32(cq + e0 * D + dc, dW[0]);
+        ld32(cq + e1 * D + dc, dW[1]);
+        ld32(cq + DE + e0 * D + dc, dS[0]);
+        ld32(cq + DE + e1 * D + dc, dS[1]);
+      } else {
+        const float* gW = rank ? a.dW2_out : a.dW1_out;
+        const float* gS = rank ? a.dS2_out : a.dS1_out;
+        const size_t bh = (size_t)q * DE;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int e = h2 ? e1 : e0;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int d = dc + jj;
+            const size_t o = rank ? bh + (size_t)e * D + d : bh + (size_t)d * E + e;
+            dW[h2][jj] = gW ? gW[o] : 0.f;
+            dS[h2][jj] = gS ? gS[o] : 0.f;
+          }
+        }
+      }
+    }
+    for (int r = cs - 1; r >= 0; --r) {
+      const int t = c * cs + r;
+      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, t);
+      if (tid < D) {
+        const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
+        s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
+        s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
+      }
+      if (tid < MAXCS) s.ipacc[tid] = 0.f;
+      __syncthreads();
+      {  // read-out: rank 0 dW1 += dy p^T (tile: p[e] dy[d]); rank 1 dW2 += dz q^T
+        const float v0 = vec[r * E + e0], v1 = vec[r * E + e1];
+        const float* xv = rank ? s.qv : s.dyv;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          dW[0][jj] = fmaf(v0, xv[dc + jj], dW[0][jj]);
+          dW[1][jj] = fmaf(v1, xv[dc + jj], dW[1][jj]);
+        }
+      }
+      float dal = 0.f;
+      {
+        float wv[32];
+        ld32(Wsave + (size_t)r * DE + e0 * D + dc, wv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[0][jj], wv[jj], dal);
+        ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[1][jj], wv[jj], dal);
+      }
+      // ---- Polar Express VJP ----
+      if (P.pe_ste || P.ns_steps == 0) {
+        if (P.pe_ste) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            dS[0][jj] += dW[0][jj];
+            dS[1][jj] += dW[1][jj];
+          }
+        }
+      }
+      if (!P.pe_ste) {
+        const float* St = Ssave + (size_t)(r + 1) * DE;
+        float xo[2][32];
+        ld32(St + e0 * D + dc, xo[0]);
+        ld32(St + e1 * D + dc, xo[1]);
+        float ss = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) ss = fmaf(xo[0][jj], xo[0][jj], fmaf(xo[1][jj], xo[1][jj], ss));
+        ss = block_sum(ss, s.red);
+        const float nrm = sqrtf(ss + 1e-12f);
+        const float kap = nrm * 1.01f + 1e-6f, inv = 1.0f / kap;
+        float gx[2][32];
+        if (P.ns_steps > 0) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            xo[0][jj] *= inv;
+            xo[1][jj] *= inv;
+          }
+          store_split32(s.Xh, s.Xl, e0, dc, D, xo[0]);
+          store_split32(s.Xh, s.Xl, e1, dc, D, xo[1]);
+          bool ok = pe_forward_tc(s, tm, phase, P.ns_steps, w.ns[rank], xo);
+          store_split32(s.Gh, s.Gl, e0, dc, D, dW[0]);
+          store_split32(s.Gh, s.Gl, e1, dc, D, dW[1]);
+          for (int st = P.ns_steps - 1; st >= 0; --st) {
+            const float cb = (float)kPE[st][1], cc = (float)kPE[st][2];
+            const uint8_t* o = w.ns[rank] + (size_t)st * NS_STEP_BYTES;
+            __syncthreads();
+            copy16(s.Xh, o, XT_BYTES);
+            copy16(s.Xl, o + XT_BYTES, XT_BYTES);
+            copy16(s.Ah, o + 2 * XT_BYTES, AT_BYTES);
+            copy16(s.Al, o + 2 * XT_BYTES + AT_BYTES, AT_BYTES);
+            copy16(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES);
+            copy16(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES);
+            // P = G~^T X~
+            ok = mma_sync_run(&s.bar, &s.bad, phase, [&] { mma3(tm + TM_GRAM, s.Gh, s.Gl, true, s.Xh, s.Xl, true, 64, E, 0, false); }) && ok;
+            float pv[32];
+            tmem_ld32(tm + lane_off + TM_GRAM + dc, pv);
+            tmem_wait_ld();
+            if (l < 16) st32(&s.Pf[ra * D + dc], pv);
+            __syncthreads();
+            if (l < 16) {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) pv[jj] += s.Pf[(dc + jj) * D + ra];  // Ps = P + P^T
+              store_split32(s.Ph, s.Pl, ra, dc, D, pv);
+            }
+            // Sym = b Ps + c (Ps A + A Ps)
+            ok = mma_sync_run(&s.bar, &s.bad, phase, [&] {
+                   mma3(tm + TM_A2, s.Ph, s.Pl, false, s.Ah, s.Al, true, 64, D, 0, false);
+                   mma3(tm + TM_A2, s.Ah, s.Al, false, s.Ph, s.Pl, true, 64, D, 0, true);
+                 }) && ok;
+            float yv[32];
+            tmem_ld32(tm + lane_off + TM_A2 + dc, yv);
+            tmem_wait_ld();
+            if (l < 16) {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(cc, yv[jj], cb * pv[jj]);
+              store_split32(s.Yh, s.Yl, ra, dc, D, yv);
+            }
+            // dX~ = G~ B' + X~ Sym
+            ok = mma_sync_run(&s.bar, &s.bad, phase, [&] {
+                   for (int h2 = 0; h2 < 2; ++h2) {
+                     mma3(tm + TM_X + 64 * h2, s.Gh, s.Gl, false, s.Bh, s.Bl, true, 128, D, 16384 * h2, false);
+                     mma3(tm + TM_X + 64 * h2, s.Xh, s.Xl, false, s.Yh, s.Yl, true, 128, D, 16384 * h2, true);
+                   }
+                 }) && ok;
+            tmem_ld32(tm + lane_off + TM_X + dc, gx[0]);
+            tmem_ld32(tm + lane_off + TM_X + 64 + dc, gx[1]);
+            tmem_wait_ld();
+            if (st > 0) {
+              store_split32(s.Gh, s.Gl, e0, dc, D, gx[0]);
+              store_split32(s.Gh, s.Gl, e1, dc, D, gx[1]);
+            }
+          }
+          if (!ok && !s.bad) {
+            set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
+            s.bad = 1;
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            gx[0][jj] = dW[0][jj];
+            gx[1][jj] = dW[1][jj];
+          }
+        }
+        // X0 = S / kappa, kappa = 1.01 sqrt(sum S^2 + 1e-12) + 1e-6
+        ld32(St + e0 * D + dc, xo[0]);
+        ld32(St + e1 * D + dc, xo[1]);
+        float dot = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dot = fmaf(gx[0][jj], xo[0][jj], fmaf(gx[1][jj], xo[1][jj], dot));
+        dot = block_sum(dot, s.red);
+        const float coef = dot / (kap * kap) * 1.01f / nrm;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          dS[0][jj] += gx[0][jj] * inv - coef * xo[0][jj];
+          dS[1][jj] += gx[1][jj] * inv - coef * xo[1][jj];
+        }
+      }
+      // ---- momentum scan: dtheta_t = <dS, S_{t-1}>, Omega-window terms ----
+      float dth = 0.f;
+      {
+        float sv[32];
+        ld32(Ssave + (size_t)r * DE + e0 * D + dc, sv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dth = fmaf(dS[0][jj], sv[jj], dth);
+        ld32(Ssave + (size_t)r * DE + e1 * D + dc, sv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dth = fmaf(dS[1][jj], sv[jj], dth);
+      }
+      const int i0 = win ? max(0, r - P.omega + 1) : r;
+      for (int i = i0; i <= r; ++i) {
+        const float gi = win ? load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + i).g : 1.f;
+        const float cf = -g.e * sc * gi;
+        const float f0 = Fm[i * E + e0], f1 = Fm[i * E + e1];
+        float gv[32], cv[32];
+        ld32(Gm + i * D + dc, gv);
+        float rv0 = 0.f, rv1 = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          rv0 = fmaf(dS[0][jj], gv[jj], rv0);
+          rv1 = fmaf(dS[1][jj], gv[jj], rv1);
+          cv[jj] = fmaf(dS[0][jj], f0, dS[1][jj] * f1);
+        }
+        float ip = fmaf(f0, rv0, f1 * rv1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ip += __shfl_xor_sync(0xffffffffu, ip, o);
+        if (l == 0) atomicAdd(&s.ipacc[i], ip);
+        red_add(&w.dF[rank][i * E + e0], cf * rv0);
+        red_add(&w.dF[rank][i * E + e1], cf * rv1);
+        const float part = warp_reduce_scatter32(cv);
+        red_add(&w.dG[rank][i * D + dc + l], cf * part);
+      }
+      dal = block_sum(dal, s.red);
+      dth = block_sum(dth, s.red);  // also orders the ipacc atomics before the reads below
+      if (tid >= i0 && tid <= r) {
+        const float ip = s.ipacc[tid];
+        const float gi = win ? load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + tid).g : 1.f;
+        red_add(&w.scal[MAXCS + r], -sc * gi * ip);          // deta_t
+        if (win) red_add(&w.scal[3 * MAXCS + tid], -g.e * sc * ip);  // dgamma_i
+      }
+      if (tid == 0) {
+        red_add(&w.scal[r], dal);
+        red_add(&w.scal[2 * MAXCS + r], dth);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        dW[0][jj] *= g.a;
+        dW[1][jj] *= g.a;
+        dS[0][jj] *= g.t;
+        dS[1][jj] *= g.t;
+      }
+    }
+
+    // ================= D: frozen-state pass backward =================
+    __threadfence();
+    cluster_sync();  // both ranks' window accumulations are complete
+    {
+      const float* W1t = slot;
+      const float* W2 = slot + 2 * DE;
+      float* dw1t = (float*)s.Xh;  // cs x E
+      float* dhb = (float*)s.Gh;   // cs x E
+      float* derr = s.Pf;          // cs x D
+      {  // thread e: d(W1^T err) = dchain * gelu'(h); dh = dchain * r * gelu''(h)
+        const int e = tid;
+        for (int i = 0; i < cs; ++i) {
+          const float dcv = w.dF[1][i * E + e], hv = w.h[i * E + e];
+          dw1t[i * E + e] = dcv * gelu_erf_prime(hv);
+          dhb[i * E + e] = dcv * w.r[i * E + e] * gelu_erf_second(hv);
+        }
+      }
+      __syncthreads();
+      const int d = tid % D, grp = tid / D, per = (cs + 3) / 4;
+      {  // derr = derr_window + W1 d(W1^T err)
+        float acc[MAXCS / 4];
+#pragma unroll
+        for (int jj = 0; jj < MAXCS / 4; ++jj) acc[jj] = 0.f;
+        for (int e = 0; e < E; ++e) {
+          const float wv = W1t[e * D + d];
+#pragma unroll
+          for (int jj = 0; jj < MAXCS / 4; ++jj) {
+            const int i = grp * per + jj;
+            if (jj < per && i < cs) acc[jj] = fmaf(wv, dw1t[i * E + e], acc[jj]);
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < MAXCS / 4; ++jj) {
+          const int i = grp * per + jj;
+          if (jj < per && i < cs) derr[i * D + d] = w.dG[0][i * D + d] + acc[jj];
+        }
+      }
+      __syncthreads();
+      {  // thread e: dact = dact_window + W1^T derr ; dh += dact * gelu_tanh'(h)
+        const int e = tid;
+        float wr[D];
+#pragma unroll
+        for (int dd = 0; dd < D; ++dd) wr[dd] = W1t[e * D + dd];
+        for (int i = 0; i < cs; ++i) {
+          float da = w.dF[0][i * E + e];
+#pragma unroll
+          for (int dd = 0; dd < D; ++dd) da = fmaf(wr[dd], derr[i * D + dd], da);
+          dhb[i * E + e] += da * gelu_tanh_grad(w.h[i * E + e]);
+        }
+      }
+      __syncthreads();
+      if (rank == 0) {  // dk = dk_window + derr + W2^T dh ; dv = -derr
+        float acc[MAXCS / 4];
+#pragma unroll
+        for (int jj = 0; jj < MAXCS / 4; ++jj) acc[jj] = 0.f;
+        for (int e = 0; e < E; ++e) {
+          const float wv = W2[e * D + d];
+#pragma unroll
+          for (int jj = 0; jj < MAXCS / 4; ++jj) {
+            const int i = grp * per + jj;
+            if (jj < per && i < cs) acc[jj] = fmaf(wv, dhb[i * E + e], acc[jj]);
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < MAXCS / 4; ++jj) {
+          const int i = grp * per + jj, t = c * cs + i;
+          if (jj < per && i < cs && t < T) {
+            const size_t o = (((size_t)b * T + t) * H + hh) * D + d;
+            st_act((TA*)a.dk, o, w.dG[1][i * D + d] + derr[i * D + d] + acc[jj]);
+            st_act((TA*)a.dv, o, -derr[i * D + d]);
+          }
+        }
+        if (tid < cs && c * cs + tid < T) {
+          const size_t o = ((size_t)b * T + c * cs + tid) * H + hh;
+          if (a.dalpha) a.dalpha[o] = w.scal[tid];
+          if (a.deta) a.deta[o] = w.scal[MAXCS + tid];
+          if (a.dtheta) a.dtheta[o] = w.scal[2 * MAXCS + tid];
+          if (a.dgamma) a.dgamma[o] = win ? w.scal[3 * MAXCS + tid] : 0.f;
+        }
+      }
+      // chunk-start weight cotangents of the frozen pass
+      for (int i = 0; i < cs; ++i) {
+        float gv[32], hv2[32];
+        if (rank == 0) {  // dW1^T[e][d] += dw1t[e] err[d] + act[e] derr[d]
+          ld32(w.err + i * D + dc, gv);
+          ld32(derr + i * D + dc, hv2);
+          const float a0 = dw1t[i * E + e0], a1 = dw1t[i * E + e1];
+          const float b0 = w.act[i * E + e0], b1 = w.act[i * E + e1];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            dW[0][jj] = fmaf(a0, gv[jj], fmaf(b0, hv2[jj], dW[0][jj]));
+            dW[1][jj] = fmaf(a1, gv[jj], fmaf(b1, hv2[jj], dW[1][jj]));
+          }
+        } else {          // dW2[e][d] += dh[e] k[d]
+          ld32(w.k + i * D + dc, gv);
+          const float a0 = dhb[i * E + e0], a1 = dhb[i * E + e1];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            dW[0][jj] = fmaf(a0, gv[jj], dW[0][jj]);
+            dW[1][jj] = fmaf(a1, gv[jj], dW[1][jj]);
+          }
+        }
+      }
+    }
+    if (P.stop_grad_chunks) {  // memory_layer.py:665: the incoming carry is detached
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) dW[0][jj] = dW[1][jj] = dS[0][jj] = dS[1][jj] = 0.f;
+    }
+    if (c > 0) {
+      float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
+      st32(cq + e0 * D + dc, dW[0]);
+      st32(cq + e1 * D + dc, dW[1]);
+      st32(cq + DE + e0 * D + dc, dS[0]);
+      st32(cq + DE + e1 * D + dc, dS[1]);
+    } else {
+      float* oW = rank ? a.dW2_in : a.dW1_in;
+      float* oS = rank ? a.dS2_in : a.dS1_in;
+      const size_t bh = (size_t)q * DE;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int e = h2 ? e1 : e0;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int d = dc + jj;
+          const size_t o = rank ? bh + (size_t)e * D + d : bh + (size_t)d * E + e;
+          if (oW) oW[o] = dW[h2][jj];
+          if (oS) oS[o] = dS[h2][jj];
+        }
+      }
+    }
+    __threadfence();
+    cluster_sync();
+    if (rank == 0 && tid == 0) st_release(&K.flags[q], j + 1);
+  }
+  fence_before();
+  __syncthreads();
+  if (wp == 0) tmem_dealloc(tm, TMEM_COLS);
+}
+
+}  // namespace bwd
+
+// ---- host side ----------------------------------------------------------------
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static int max_clusters_bound() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms / 2;
+}
+
+size_t bwd_workspace_bytes(const AtlasScanParams& p) {
+  const size_t nc = (size_t)p.B * p.H;
+  const size_t ncl = std::min(nc, (size_t)max_clusters_bound());
+  return align256(nc * sizeof(int)) + nc * 4 * DE * sizeof(float) + ncl * bwd::CLUSTER_FLOATS * sizeof(float);
+}
+
+static int g_bwd_max_clusters = -1;
+
+template <typename TA>
+static cudaError_t launch_bwd_t(const bwd::KArgs& k, int nclusters, cudaStream_t st) {
+  size_t smem = sizeof(bwd::Smem) + 1024;
+  cudaError_t e =
+      cudaFuncSetAttribute(bwd::bwd_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (g_bwd_max_clusters < 0) {
+    int n = 0;
+    cfg.gridDim = dim3(2);
+    if (cudaOccupancyMaxActiveClusters(&n, bwd::bwd_kernel<TA>, &cfg) != cudaSuccess || n <= 0) n = 1;
+    g_bwd_max_clusters = n;
+  }
+  cfg.gridDim = dim3(2 * std::min(nclusters, g_bwd_max_clusters));
+  return cudaLaunchKernelEx(&cfg, bwd::bwd_kernel<TA>, k);
+}
+
+cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t st) {
+  bwd::KArgs k;
+  k.a = a;
+  k.nchains = a.p.B * a.p.H;
+  k.nch = n_chunks(a.p);
+  uint8_t* ws = (uint8_t*)a.ws;
+  k.flags = (int*)ws;
+  k.cot = (float*)(ws + align256((size_t)k.nchains * sizeof(int)));
+  k.cws = k.cot + (size_t)k.nchains * 4 * DE;
+  cudaError_t e = cudaMemsetAsync(k.flags, 0, (size_t)k.nchains * sizeof(int), st);
+  if (e != cudaSuccess) return e;
+  const int ncl = std::min(k.nchains, max_clusters_bound());
+  return a.p.act_dtype == ATLAS_BF16 ? launch_bwd_t<__nv_bfloat16>(k, ncl, st) : launch_bwd_t<float>(k, ncl, st);
+}
+
+}  // namespace tc
+}  // namespace atlas

@@ -1,0 +1,61 @@
+"""GPU parity of the tcgen05 backward scan against the oracle's float64 VJP.
+
+Tolerance 2e-2 relative (Frobenius) per gradient tensor (the bf16-activation
+bound of the north star); inputs are rounded to bf16 for both sides when the
+activations are bf16.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import atlas_oracle as O
+from gpu_util import rel, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _bf(x):
+    import ml_dtypes
+    return x.astype(ml_dtypes.bfloat16).astype(np.float32)
+
+
+@pytest.mark.parametrize("T,omega,ste,sg,act,xav", [
+    (128, 16, False, False, torch.float32, False),
+    (100, 4, False, False, torch.bfloat16, True),
+    (128, 16, True, False, torch.float32, True),
+    (128, 8, False, True, torch.float32, True),
+])
+def test_tc_backward(T, omega, ste, sg, act, xav):
+    from atlas_b200 import ScanConfig, ATLAS_PREC_TENSOR, scan_forward, scan_backward, device_status
+    B, H, D, E, cs = 1, 2, 64, 256, 64
+    ins = O.make_inputs(B, T, H, D, seed=11, gamma_mode="random")
+    if act == torch.bfloat16:
+        ins = tuple(_bf(x) for x in ins[:3]) + tuple(ins[3:])
+    if xav:
+        st = O.make_xavier_state(B, H, D, E, seed=12)
+        st = (st[0], st[1], 0.05 * st[0], 0.05 * st[1])
+    else:
+        st = O.lm_initial_state(B, H, D, E)
+    cfg = ScanConfig(chunk=cs, omega=omega, ns_steps=5, pe_ste=ste, stop_grad_chunks=sg,
+                     precision=ATLAS_PREC_TENSOR)
+    q, k, v, a, e, t, g = ins
+    dev_in = [to_dev(q, act), to_dev(k, act), to_dev(v, act), to_dev(a), to_dev(e), to_dev(t), to_dev(g)]
+    y, out, saved = scan_forward(*dev_in, tuple(to_dev(x) for x in st), cfg)
+    rng = np.random.default_rng(13)
+    dy = rng.standard_normal((B, T, H, D)).astype(np.float32)
+    if act == torch.bfloat16:
+        dy = _bf(dy)
+    dfin = [0.1 * rng.standard_normal(x.shape).astype(np.float32) for x in st]
+    res = scan_backward(*dev_in, saved, to_dev(dy, act), tuple(to_dev(x) for x in dfin), cfg, E)
+    torch.cuda.synchronize()
+    device_status()
+    grads, dst = O.scan_backward(*ins, st, dy, dfin, cs, omega, 5, pe_ste=ste, stop_grad_chunks=sg)
+    errs = {}
+    for name, val in zip(("q", "k", "v", "alpha", "eta", "theta", "gamma"), res[:7]):
+        errs[name] = rel(to_np(val), grads[name])
+    for i, n in enumerate(("dW1", "dW2", "dS1", "dS2")):
+        if np.abs(dst[i]).max() > 0:
+            errs[n] = rel(to_np(res[7][i]), dst[i])
+    print({k_: f"{v_:.2e}" for k_, v_ in errs.items()})
+    assert max(errs.values()) < TOL, errs
