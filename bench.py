@@ -1,0 +1,310 @@
+"""Headline benchmark: Atlas scan fwd+bwd tokens/s at the 170M configuration.
+
+One step = for each of the 12 layers the forward scan (B=8/GPU, T=8192, 12 heads x 64,
+memory MLP 64->256->64, chunk 64, Omega 16, 5 Polar Express steps, pe_ste=False,
+bf16 activations, fp32 carry), then the 12 backward scans in reverse layer order,
+then (N > 1) the NCCL all-reduce of an fp32 gradient buffer of the model's exact
+parameter count (atlas_jax/train.py:150-152).  Inputs are synthetic with the
+BASELINE distributions (q,k,v ~ N(0,1) L2-normalised per head, sigmoid gates), one
+independent set per layer; every layer's inputs (~420 MB) exceed the 126 MB L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  --impl reference times the CPU restatement of the
+reference scan (oracle/, numpy) on the host cores on a bounded sample.
+"""
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "atlas-jax_b200"))
+
+CFG = dict(layers=12, B=8, T=8192, H=12, D=64, E=256, chunk=64, omega=16, ns_steps=5)
+METRIC = "Atlas scan tokens/s fwd+bwd (170M cfg)"
+# algorithmic FLOPs per token-head-layer (m = D, n = E = 4D, ns steps); recompute not counted
+F_FWD = lambda D, ns: ns * 36 * D ** 3 + 40 * D ** 2   # noqa: E731
+F_BWD = lambda D, ns: ns * 56 * D ** 3 + 80 * D ** 2   # noqa: E731
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops_sustained"], p["hbm_gbs"], "measured"
+    except Exception:
+        return 1400.0, 6650.0, "fallback"
+
+
+def cpu_baseline(sample_T=64, sample_H=4, threads=None):
+    """Times the oracle (numpy restatement of the reference scan) fwd+bwd on one
+    layer of B=1, H=sample_H, T=sample_T, D=64; returns full-model tokens/s
+    (a full token passes 12 heads x 12 layers)."""
+    import numpy as np
+    from oracle import atlas_oracle as O
+    c = CFG
+    ins = O.make_inputs(1, sample_T, sample_H, c["D"], seed=0)
+    st = O.lm_initial_state(1, sample_H, c["D"], c["E"])
+    t0 = time.perf_counter()
+    y, _ = O.scan_forward(*ins, st, c["chunk"], c["omega"], c["ns_steps"])
+    dy = np.ones_like(y)
+    O.scan_backward(*ins, st, dy, None, c["chunk"], c["omega"], c["ns_steps"], dtype=np.float32)
+    dt = time.perf_counter() - t0
+    equiv_tokens = sample_T * sample_H / (c["H"] * c["layers"])
+    return equiv_tokens / dt, dt, os.cpu_count()
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, dt, cores = cpu_baseline()
+        if i >= args.warmup:
+            vals.append(v)
+    v = sorted(vals)[len(vals) // 2]
+    sample = "oracle numpy restatement, fwd+bwd of 1 layer, B=1 H=4 T=64 D=64 E=256, scaled to 12 heads x 12 layers"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "170M scan (CPU sample)", **CFG},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+class Clocks:
+    def __init__(self, path):
+        self.path, self.proc = path, None
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpu_index):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9 or p[0] != str(gpu_index):
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_arm(args, rank, world):
+    import torch
+    from atlas_b200 import _lib as L
+    from atlas_b200 import dp
+    lib = L.load()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    c = CFG
+    B, T, H, D, E, NL = c["B"], c["T"], c["H"], c["D"], c["E"], c["layers"]
+    p = L.AtlasScanParams(L.ATLAS_ABI_VERSION, B, T, H, D, E, c["chunk"], c["omega"], c["ns_steps"], 0, 0,
+                          L.ATLAS_BF16, L.ATLAS_PREC_TENSOR)
+    pp = ctypes.byref(p)
+    nsave = lib.atlas_scan_saved_bytes(pp)
+    nws = lib.atlas_scan_workspace_bytes(pp)
+    if nsave == 0 or nws == 0:
+        raise RuntimeError(lib.atlas_last_error_string().decode())
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def unit(x):
+        return (x / x.norm(dim=-1, keepdim=True)).bfloat16()
+    layers = []
+    for _ in range(NL):
+        Ld = dict(q=unit(torch.randn(B, T, H, D, device=dev, generator=g)),
+                  k=unit(torch.randn(B, T, H, D, device=dev, generator=g)),
+                  v=unit(torch.randn(B, T, H, D, device=dev, generator=g)))
+        for n, mu in (("alpha", 3.0), ("eta", -3.0), ("theta", 1.0), ("gamma", 0.0)):
+            Ld[n] = torch.sigmoid(mu + 0.5 * torch.randn(B, T, H, device=dev, generator=g))
+        Ld["dy"] = (torch.randn(B, T, H, D, device=dev, generator=g) * 0.01).bfloat16()
+        Ld["y"] = torch.empty_like(Ld["q"])
+        Ld["saved"] = torch.empty(nsave, dtype=torch.uint8, device=dev)
+        for n in ("dq", "dk", "dv"):
+            Ld[n] = torch.empty_like(Ld["q"])
+        for n in ("dalpha", "deta", "dtheta", "dgamma"):
+            Ld[n] = torch.empty(B, T, H, device=dev)
+        layers.append(Ld)
+    st_out = [torch.empty(B, H, D, E, device=dev), torch.empty(B, H, E, D, device=dev),
+              torch.empty(B, H, D, E, device=dev), torch.empty(B, H, E, D, device=dev)]
+    dst_in = [torch.empty_like(x) for x in st_out]
+    ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+    grad_buf = torch.zeros(dp.atlas_param_count(), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    fwd_ev, bwd_ev = [], []
+
+    def fwd(Ld, timed):
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        L.check(lib.atlas_scan_fwd(pp, P(Ld["q"]), P(Ld["k"]), P(Ld["v"]), P(Ld["alpha"]), P(Ld["eta"]),
+                                   P(Ld["theta"]), P(Ld["gamma"]), None, None, None, None, P(Ld["y"]),
+                                   *[P(x) for x in st_out], P(Ld["saved"]), P(ws), nws, sp))
+        if timed:
+            e1.record(stream)
+            fwd_ev.append((e0, e1))
+
+    def bwd(Ld, timed):
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        L.check(lib.atlas_scan_bwd(pp, P(Ld["q"]), P(Ld["k"]), P(Ld["v"]), P(Ld["alpha"]), P(Ld["eta"]),
+                                   P(Ld["theta"]), P(Ld["gamma"]), P(Ld["saved"]), P(Ld["dy"]), None, None,
+                                   None, None, P(Ld["dq"]), P(Ld["dk"]), P(Ld["dv"]), P(Ld["dalpha"]),
+                                   P(Ld["deta"]), P(Ld["dtheta"]), P(Ld["dgamma"]), *[P(x) for x in dst_in],
+                                   P(ws), nws, sp))
+        if timed:
+            e1.record(stream)
+            bwd_ev.append((e0, e1))
+
+    def step(timed=False, host=None):
+        for i, Ld in enumerate(layers):
+            if host is not None:
+                for n in ("q", "k", "v", "alpha", "eta", "theta", "gamma"):
+                    Ld[n].copy_(host[n], non_blocking=True)
+            fwd(Ld, timed)
+        for Ld in reversed(layers):
+            if host is not None:
+                Ld["dy"].copy_(host["dy"], non_blocking=True)
+            bwd(Ld, timed)
+            if host is not None:
+                for n in ("dq", "dk", "dv", "dalpha", "deta", "dtheta", "dgamma"):
+                    host["out_" + n].copy_(Ld[n], non_blocking=True)
+        dp.allreduce_mean_(grad_buf)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    L.check(lib.atlas_scan_status())
+    clocks = Clocks(os.path.join(HERE, "gpurun_out" if os.path.isdir(os.path.join(HERE, "gpurun_out"))
+                                 else ".", f"clocks_rank{rank}.csv"))
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(timed=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ck = clocks.stop(dev.index)
+    L.check(lib.atlas_scan_status())
+    ms = dp.max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    tokens = B * T * world
+    value = tokens / (ms / 1e3)
+    fwd_ms = sum(a.elapsed_time(b) for a, b in fwd_ev) / len(fwd_ev)
+    bwd_ms = sum(a.elapsed_time(b) for a, b in bwd_ev) / len(bwd_ev)
+
+    # ---- end to end: host inputs in, host gradients out, every step ----
+    host = {n: torch.empty_like(layers[0][n], device="cpu").pin_memory().copy_(layers[0][n])
+            for n in ("q", "k", "v", "alpha", "eta", "theta", "gamma", "dy")}
+    for n in ("dq", "dk", "dv", "dalpha", "deta", "dtheta", "dgamma"):
+        host["out_" + n] = torch.empty_like(layers[0][n], device="cpu").pin_memory()
+    h2d = NL * sum(host[n].numel() * host[n].element_size()
+                   for n in ("q", "k", "v", "alpha", "eta", "theta", "gamma", "dy"))
+    d2h = NL * sum(host["out_" + n].numel() * host["out_" + n].element_size()
+                   for n in ("dq", "dk", "dv", "dalpha", "deta", "dtheta", "dgamma"))
+    e2e_steps = max(1, min(args.steps, 2))
+    barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(e2e_steps):
+        step(host=host)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = dp.max_over_ranks(t0.elapsed_time(t1)) / e2e_steps
+    e2e = tokens / (e2e_ms / 1e3)
+
+    peak_tf, hbm, peak_kind = _peaks()
+    f_bwd = B * T * H * F_BWD(D, c["ns_steps"])
+    f_fwd = B * T * H * F_FWD(D, c["ns_steps"])
+    dom_ms, dom_f, dom = (bwd_ms, f_bwd, "tc_bwd_kernel") if bwd_ms >= fwd_ms else (fwd_ms, f_fwd, "tc_fwd_kernel")
+    achieved = dom_f / (dom_ms / 1e3) / 1e12
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "170M Atlas scan fwd+bwd, 12 layers, per GPU B=8 T=8192 H=12 D=64 E=256 "
+                               "chunk=64 omega=16 ns=5 pe_ste=False", "model": "atlas-170M (scan only)",
+                   "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (per-layer inputs ~420 MB)",
+                   "grad_allreduce_params": grad_buf.numel()},
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": achieved / peak_tf, "traffic": None,
+                     "peak_source": f"bf16_tflops_sustained ({peak_kind})",
+                     "fwd_ms_per_layer": fwd_ms, "bwd_ms_per_layer": bwd_ms},
+        "gpu_launches": 2 * NL * args.steps,
+        "clocks": ck,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, dt, cores = cpu_baseline()
+        out["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                               "sample": f"oracle numpy fwd+bwd, 1 layer B=1 H=4 T=64 ({dt:.1f} s), "
+                                         "scaled to 12 heads x 12 layers"}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    if world > 1:
+        from atlas_b200 import dp
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dp.init("nccl")
+    gpu_arm(args, rank, world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
