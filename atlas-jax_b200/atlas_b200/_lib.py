@@ -65,6 +65,8 @@ def load():
     lib.atlas_polar_express_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                                         ctypes.c_int32, ctypes.c_int32]
     lib.atlas_scan_status.restype = ctypes.c_int
+    lib.atlas_scan_fwd_noalloc.restype = ctypes.c_int
+    lib.atlas_scan_fwd_noalloc.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 4 + [_P] + [_F] * 4 + [_P]
     if lib.atlas_abi_version() != ATLAS_ABI_VERSION:
         raise OSError(f"libatlas_scan ABI {lib.atlas_abi_version()} != {ATLAS_ABI_VERSION}")
     _lib = lib

@@ -56,6 +56,8 @@ int cuda_result(cudaError_t e, const char* what) {
 }
 }  // namespace
 
+int atlas::report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 int atlas_abi_version(void) { return ATLAS_ABI_VERSION; }

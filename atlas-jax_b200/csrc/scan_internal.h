@@ -46,7 +46,8 @@ cudaError_t launch_pe(const float* X, float* Y, int64_t batch, int rows, int col
 size_t pe_workspace_bytes(int64_t batch, int rows, int cols, int steps);
 }  // namespace exact
 
-int* device_status_ptr();  // address of the status word on the current device
+int* device_status_ptr();
+int report_error(int code, const char* msg);  // sets atlas_last_error_string(), returns code  // address of the status word on the current device
 
 namespace tc {
 bool supported(const AtlasScanParams& p, const char** why);

@@ -117,6 +117,26 @@ int atlas_scan_bwd(const AtlasScanParams* p,
                    float* dW1_in, float* dW2_in, float* dS1_in, float* dS2_in,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Forward scan that allocates nothing and takes no workspace, for callers that
+ * cannot call cudaMalloc (for example code running inside an allocator or an
+ * inference runtime that forbids device allocations after start-up).  It has no
+ * counterpart in the reference.  Same arguments and semantics as atlas_scan_fwd
+ * without `saved` and `workspace`; tensor path only (params->precision must be
+ * ATLAS_PREC_TENSOR).  Its scratch is a fixed 4 MiB array inside the library,
+ * enough for B*H <= ATLAS_NOALLOC_MAX_CHAINS; larger problems are rejected with
+ * ATLAS_ERR_INVALID_ARGUMENT.  Every GPU that loads the library keeps that array
+ * until the process exits.  The first call on a device looks up the array's
+ * device address; make that first call before any stream capture.  All calls
+ * share the array, so calls whose executions overlap on the GPU (different
+ * streams, no ordering between them) race and corrupt each other's results. */
+#define ATLAS_NOALLOC_MAX_CHAINS 16
+int atlas_scan_fwd_noalloc(const AtlasScanParams* p,
+                           const void* q, const void* k, const void* v,
+                           const float* alpha, const float* eta, const float* theta, const float* gamma,
+                           const float* W1_in, const float* W2_in, const float* S1_in, const float* S2_in,
+                           void* y,
+                           float* W1_out, float* W2_out, float* S1_out, float* S2_out, void* stream);
+
 /* Batched Polar Express on float32 (batch, rows, cols) matrices, out-of-place.
  * Replaces fused_polar_express (atlas_jax/kernels/triton_pe.py:26-69, same math
  * as memory_layer.py:43-71) and the Muon orthogonalisation call site
