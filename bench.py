@@ -241,15 +241,17 @@ def gpu_arm(args, rank, world):
     d2h = NL * sum(host["out_" + n].numel() * host["out_" + n].element_size()
                    for n in ("dq", "dk", "dv", "dalpha", "deta", "dtheta", "dgamma"))
     e2e_steps = max(1, min(args.steps, 2))
-    barrier()
-    torch.cuda.synchronize()
-    t0.record(stream)
-    for _ in range(e2e_steps):
-        step(host=host)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = dp.max_over_ranks(t0.elapsed_time(t1)) / e2e_steps
-    e2e = tokens / (e2e_ms / 1e3)
+    e2e = None
+    if not args.no_e2e:
+        barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(e2e_steps):
+            step(host=host)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = dp.max_over_ranks(t0.elapsed_time(t1)) / e2e_steps
+        e2e = tokens / (e2e_ms / 1e3)
 
     peak_tf, hbm, peak_kind = _peaks()
     f_bwd = B * T * H * F_BWD(D, c["ns_steps"])
@@ -260,8 +262,8 @@ def gpu_arm(args, rank, world):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "170M Atlas scan fwd+bwd, 12 layers, per GPU B=8 T=8192 H=12 D=64 E=256 "
-                               "chunk=64 omega=16 ns=5 pe_ste=False", "model": "atlas-170M (scan only)",
+        "config": {"workload": f"170M Atlas scan fwd+bwd, {NL} layers, per GPU B={B} T={T} H={H} D={D} "
+                               f"E={E} chunk=64 omega=16 ns=5 pe_ste=False", "model": "atlas-170M (scan only)",
                    "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (per-layer inputs ~420 MB)",
                    "grad_allreduce_params": grad_buf.numel()},
@@ -289,7 +291,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--layers", type=int, default=CFG["layers"], help="profiling only: fewer layers")
+    ap.add_argument("--seq", type=int, default=CFG["T"], help="profiling only: shorter sequences")
+    ap.add_argument("--no-e2e", action="store_true", help="profiling only: skip the end-to-end leg")
     args = ap.parse_args()
+    if args.layers != CFG["layers"] or args.seq != CFG["T"]:
+        CFG["layers"], CFG["T"] = args.layers, args.seq
+        args.no_cpu = True
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
