@@ -11,12 +11,12 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
-OUT = os.path.join(HERE, "atlas_b200", "libatlas_scan.so")
-OBJ = os.path.join(HERE, "_build")
+OUT = os.environ.get("ATLAS_LIB_OUT", os.path.join(HERE, "atlas_b200", "libatlas_scan.so"))
+OBJ = os.environ.get("ATLAS_OBJ_DIR", os.path.join(HERE, "_build"))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
-         "-I", os.path.join(ROOT, "include"), "-I", CSRC]
+         "-I", os.path.join(ROOT, "include"), "-I", CSRC] + os.environ.get("ATLAS_NVCC_DEFS", "").split()
 
 
 def sources():

@@ -1,6 +1,6 @@
 // atlas_scan_fwd_noalloc: the tensor-path forward scan for callers that may not
 // allocate device memory.  The scratch the forward kernel needs (per-chain
-// progress counters and one carry slot per chain) lives in a fixed array in
+// progress counters, one carry slot per chain and per-cluster factor rows) lives in a fixed array in
 // this file instead of a caller-provided workspace.
 #include <mutex>
 
@@ -9,9 +9,11 @@
 
 namespace {
 
-constexpr size_t kChainSlotBytes = 4ull * 64 * 256 * sizeof(float);  // W1, S1, W2, S2 of one (b, h)
-constexpr size_t kFlagBytes = 256;                                     // counters, padded
-constexpr size_t kScratchBytes = kFlagBytes + ATLAS_NOALLOC_MAX_CHAINS * kChainSlotBytes;  // 4 MiB + 256 B
+constexpr size_t kChainSlotBytes = 4ull * 64 * 256 * sizeof(float);    // W1, S1, W2, S2 of one (b, h)
+constexpr size_t kFlagBytes = 256;                                       // counters, padded
+constexpr size_t kFactorBytes = 2ull * 64 * 256 * sizeof(float);       // per cluster: both CTAs' row factors
+// at most one cluster per chain, so 16 chains need at most 16 clusters: 6 MiB + 256 B
+constexpr size_t kScratchBytes = kFlagBytes + ATLAS_NOALLOC_MAX_CHAINS * (kChainSlotBytes + kFactorBytes);
 
 // Device-resident scratch shared by every call on a device.  In host code this
 // name is only a handle: its device address comes from cudaGetSymbolAddress.

@@ -21,6 +21,9 @@
 //     float32 registers; X0 = S / (1.01 ||S|| + 1e-6); five Polar Express steps on
 //     the tensor cores; W <- alpha W + X5; read-out y = q + W1 gelu(W2 q) with the
 //     gelu(W2 q) vector exchanged through distributed shared memory.
+//   * tokens go through Polar Express in pairs: two operand-tile sets and two TMEM
+//     regions let one token's epilogue overlap the other token's MMAs
+//     (pe_forward_multi); the momentum / memory recurrences stay in token order.
 //
 // Numerics: every Polar Express product runs as three bf16 MMAs
 // (hi*hi + hi*lo + lo*hi, float32 accumulation in TMEM), i.e. ~16 mantissa bits
@@ -44,95 +47,36 @@ namespace atlas {
 namespace tc {
 using namespace tcx;
 
-
 struct __align__(1024) Smem {
-  uint8_t Xh[XT_BYTES];   // X~ hi / lo tiles (frozen pass: float scratch)
-  uint8_t Xl[XT_BYTES];
-  uint8_t Ah[AT_BYTES];   // A hi / lo
-  uint8_t Al[AT_BYTES];
-  uint8_t Bh[AT_BYTES];   // B' hi / lo
-  uint8_t Bl[AT_BYTES];
-  float F[MAXCS * E];     // per-token row factor: act (rank 0) or chain (rank 1)
-  float G[MAXCS * D];     // per-token column factor: err (rank 0) or k (rank 1)
-  float Q[MAXCS * D];     // queries of the chunk
-  float gate[4][MAXCS];   // alpha, eta, theta, gamma
+  uint8_t slot[2][NS_TILE_BYTES];  // per in-flight token: X~ hi/lo, A hi/lo, B' hi/lo (frozen pass: scratch)
+  float G[MAXCS * D];              // per-token column factor: err (rank 0) or k (rank 1)
+  float gate[4][MAXCS];            // alpha, eta, theta, gamma
+  float qv[D];
   float zbuf[2][E];
-  float pbuf[2][E];       // gelu(W2 q) written by rank 1 into rank 0
+  float pbuf[2][E];                // gelu(W2 q) written by rank 1 into rank 0
   float ybuf[4][D];
   float red[8];
-  uint64_t bar;
+  uint64_t bar[2];
   uint32_t tmem;
   int bad;
 };
 
-
-}  // namespace tc
-}  // namespace atlas
-
-namespace atlas {
-namespace tc {
-
-// ---- MMA issue (one thread) -----------------------------------------------
-// Gram A = X~^T X~ (M = N = D, K = E), both operands MN-major views of the X~ tiles.
-__device__ void issue_gram(Smem& s, uint32_t tm) {
-  const uint32_t id = idesc_bf16(64, 64, true, true);
-  const uint8_t* ta[3] = {s.Xh, s.Xh, s.Xl};
-  const uint8_t* tb[3] = {s.Xh, s.Xl, s.Xh};
-  for (int t = 0; t < 3; ++t)
-    for (int ks = 0; ks < E / 16; ++ks) {
-      uint64_t da = desc_mnmajor(smem_u32(ta[t]) + ks * 2 * (16 * D), D);
-      uint64_t db = desc_mnmajor(smem_u32(tb[t]) + ks * 2 * (16 * D), D);
-      mma_bf16(tm + TM_GRAM, da, db, id, (t | ks) != 0);
-    }
+__device__ __forceinline__ PESlot make_slot(Smem& s, int j, uint32_t tmem) {
+  PESlot p;
+  uint8_t* b = s.slot[j];
+  p.Xh = b;
+  p.Xl = b + XT_BYTES;
+  p.Ah = b + 2 * XT_BYTES;
+  p.Al = p.Ah + AT_BYTES;
+  p.Bh = p.Al + AT_BYTES;
+  p.Bl = p.Bh + AT_BYTES;
+  p.bar = &s.bar[j];
+  p.tm = tmem + 256u * j;
+  p.phase = 0;
+  p.ns = nullptr;
+  p.save_last = 0;
+  return p;
 }
-// A^2 (M = N = K = D): A operand K-major rows = r; B operand MN-major (rows = k).
-__device__ void issue_a2(Smem& s, uint32_t tm) {
-  const uint32_t id = idesc_bf16(64, 64, false, true);
-  const uint8_t* ta[3] = {s.Ah, s.Ah, s.Al};
-  const uint8_t* tb[3] = {s.Ah, s.Al, s.Ah};
-  for (int t = 0; t < 3; ++t)
-    for (int ks = 0; ks < D / 16; ++ks) {
-      uint64_t da = desc_kmajor(smem_u32(ta[t]) + ks * 256, D);
-      uint64_t db = desc_mnmajor(smem_u32(tb[t]) + ks * 2 * (16 * D), D);
-      mma_bf16(tm + TM_A2, da, db, id, (t | ks) != 0);
-    }
-}
-// X~' = X~ B'^T (M = E as two 128-row halves, N = K = D), both operands K-major.
-__device__ void issue_xb(Smem& s, uint32_t tm) {
-  const uint32_t id = idesc_bf16(128, 64, false, false);
-  const uint8_t* ta[3] = {s.Xh, s.Xh, s.Xl};
-  const uint8_t* tb[3] = {s.Bh, s.Bl, s.Bh};
-  for (int h = 0; h < 2; ++h)
-    for (int t = 0; t < 3; ++t)
-      for (int ks = 0; ks < D / 16; ++ks) {
-        uint64_t da = desc_kmajor(smem_u32(ta[t]) + h * (128 / 8) * (16 * D) + ks * 256, D);
-        uint64_t db = desc_kmajor(smem_u32(tb[t]) + ks * 256, D);
-        mma_bf16(tm + TM_X + h * 64, da, db, id, (t | ks) != 0);
-      }
-}
-
-// All threads: make the freshly written operand tiles visible to the tensor
-// core, run `issue` on thread 0, wait for completion.  Returns false on timeout.
-template <typename F>
-__device__ __forceinline__ bool run_mma(Smem& s, uint32_t tm, uint32_t& phase, F issue) {
-  fence_async_smem();
-  fence_before();
-  __syncthreads();
-  if (s.bad) return false;  // an earlier wait expired: skip the work, keep the control flow
-  if (threadIdx.x == 0) {
-    fence_after();
-    issue(s, tm);
-    mma_commit(&s.bar);
-  }
-  bool ok = mbar_wait(&s.bar, phase);
-  phase ^= 1;
-  fence_after();
-  return ok;
-}
-
-struct Item {
-  int q, c;
-};
 
 // Carry slot entering chunk c of chain q: [matrix m][W, S][E x D tile].
 __device__ __forceinline__ float* carry_slot(const FwdArgs& a, float* carries, int q, int c, int nch) {
@@ -140,25 +84,24 @@ __device__ __forceinline__ float* carry_slot(const FwdArgs& a, float* carries, i
 }
 
 // Frozen-state pass of one chunk (memory_layer.py:504-520), float32 CUDA cores.
+// Writes this CTA's row factor (act on rank 0, chain on rank 1) to Fg (cs x E,
+// global scratch) and its column factor (err / k) to s.G.
 template <typename TA>
-__device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, int b, int hh, int c, int cs,
-                            uint32_t rank) {
+__device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float* Fg, int b, int hh, int c,
+                            int cs, uint32_t rank) {
   const AtlasScanParams& P = a.p;
   const int T = P.T, H = P.H;
   const TA* kp = (const TA*)a.k;
   const TA* vp = (const TA*)a.v;
-  const TA* qp = (const TA*)a.q;
   const float* W1t = slot;            // W1^T: [e][d]
   const float* W2 = slot + 2 * DE;    // W2:   [e][d]
-  float* kbuf = (float*)s.Ah;         // cs x D  (Ah..Al, 16 KB)
-  float* errb = rank ? (float*)s.Bh : s.G;  // cs x D
-  float* actb = rank ? (float*)s.Xh : s.F;  // cs x E
+  float* actb = (float*)s.slot[0];                     // cs x E  (64 KB)
+  float* kbuf = (float*)s.slot[1];                     // cs x D  (16 KB)
+  float* errb = (float*)(s.slot[1] + MAXCS * D * 4);   // cs x D  (16 KB)
   const int tid = threadIdx.x;
   for (int i = tid; i < cs * D; i += NT) {
     int r = i / D, d = i % D, t = c * cs + r;
-    size_t o = (((size_t)b * T + t) * H + hh) * D + d;
-    kbuf[i] = t < T ? ld_act(kp, o) : 0.f;
-    s.Q[i] = t < T ? ld_act(qp, o) : 0.f;
+    kbuf[i] = t < T ? ld_act(kp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
   }
   for (int r = tid; r < cs; r += NT) {
     Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + r);
@@ -177,8 +120,9 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, int b,
       float hv = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) hv = fmaf(w[d], kbuf[r * D + d], hv);
-      actb[r * E + e] = gelu_tanh(hv);
-      if (rank) s.F[r * E + e] = hv;  // keep h for gelu'(h)
+      const float av = gelu_tanh(hv);
+      actb[r * E + e] = av;
+      Fg[r * E + e] = rank ? hv : av;  // rank 1 keeps h for gelu'(h)
     }
   }
   __syncthreads();
@@ -215,10 +159,10 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, int b,
       float rv = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) rv = fmaf(w[d], errb[r * D + d], rv);
-      s.F[r * E + e] = rv * gelu_erf_prime(s.F[r * E + e]);
+      Fg[r * E + e] = rv * gelu_erf_prime(Fg[r * E + e]);
     }
-    for (int i = tid; i < cs * D; i += NT) s.G[i] = kbuf[i];
   }
+  for (int i = tid; i < cs * D; i += NT) s.G[i] = rank ? kbuf[i] : errb[i];
   __syncthreads();
 }
 
@@ -229,10 +173,16 @@ struct KArgs {
   int nchains, nch;
   float* carries;  // used when a.saved == nullptr: one slot per chain
   int* flags;      // chunks completed per chain (zeroed before launch)
+  float* fscr;     // per cluster, per rank: the chunk's row factors (MAXCS x E)
 };
+
+#ifdef ATLAS_PHASE_PROF
+__device__ unsigned long long g_prof_fwd[16];
+#endif
 
 template <typename TA>
 __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
+  PROF_DECL
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const FwdArgs& a = K.a;
@@ -246,21 +196,23 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
   const float sc = 2.0f / D;
   const bool win = P.omega > 1;
   const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+  float* Fg = K.fscr + ((size_t)cluster * 2 + rank) * MAXCS * E;
 
   if (w == 0) {
     tmem_alloc(&s.tmem, TMEM_COLS);
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(&s.bar, 1);
+    mbar_init(&s.bar[0], 1);
+    mbar_init(&s.bar[1], 1);
     fence_mbar_init();
     s.bad = 0;
   }
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tm = s.tmem;
-  uint32_t phase = 0;
+  PESlot sl[2] = {make_slot(s, 0, s.tmem), make_slot(s, 1, s.tmem)};
+  PROF_INIT
 
   float Sv[2][32], Wv[2][32];
   const long total = (long)K.nchains * nch;
@@ -300,7 +252,9 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
       __threadfence();
     }
     cluster_sync();
-    frozen_pass<TA>(a, s, slot, b, hh, c, cs, rank);
+    PROF_T(tfz)
+    frozen_pass<TA>(a, s, slot, Fg, b, hh, c, cs, rank);
+    PROF_ADD(5, tfz)
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       Wv[0][j] = mine[e0 * D + dc + j];
@@ -310,121 +264,119 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
     }
     cluster_sync();  // both CTAs are done reading the carry slot
 
-    for (int r = 0; r < cs; ++r) {
-      const float al = s.gate[0][r], et = s.gate[1][r], th = s.gate[2][r];
-      // ---- momentum: S <- theta S - eta * s * sum_i gamma_i f_i g_i^T ----
+    const int npair = P.ns_steps > 0 ? 2 : 1;
+    for (int r0 = 0; r0 < cs; r0 += npair) {
+      PROF_T(tpair)
+      const int n = min(npair, cs - r0);
+      float inv0 = 0.f;
+      for (int j = 0; j < n; ++j) {
+        PROF_T(ttok)
+        const int r = r0 + j;
+        const float et = s.gate[1][r], th = s.gate[2][r];
+        // ---- momentum: S <- theta S - eta * s * sum_i gamma_i f_i g_i^T ----
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        Sv[0][j] *= th;
-        Sv[1][j] *= th;
-      }
-      const int i0 = win ? max(0, r - P.omega + 1) : r;
-      for (int i = i0; i <= r; ++i) {
-        const float wgt = -et * sc * (win ? s.gate[3][i] : 1.f);
-        const float f0 = wgt * s.F[i * E + e0], f1 = wgt * s.F[i * E + e1];
-        const float4* g4 = (const float4*)&s.G[i * D + dc];
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float4 g = g4[j4];
-          Sv[0][4 * j4 + 0] = fmaf(f0, g.x, Sv[0][4 * j4 + 0]);
-          Sv[0][4 * j4 + 1] = fmaf(f0, g.y, Sv[0][4 * j4 + 1]);
-          Sv[0][4 * j4 + 2] = fmaf(f0, g.z, Sv[0][4 * j4 + 2]);
-          Sv[0][4 * j4 + 3] = fmaf(f0, g.w, Sv[0][4 * j4 + 3]);
-          Sv[1][4 * j4 + 0] = fmaf(f1, g.x, Sv[1][4 * j4 + 0]);
-          Sv[1][4 * j4 + 1] = fmaf(f1, g.y, Sv[1][4 * j4 + 1]);
-          Sv[1][4 * j4 + 2] = fmaf(f1, g.z, Sv[1][4 * j4 + 2]);
-          Sv[1][4 * j4 + 3] = fmaf(f1, g.w, Sv[1][4 * j4 + 3]);
+        for (int jj = 0; jj < 32; ++jj) {
+          Sv[0][jj] *= th;
+          Sv[1][jj] *= th;
         }
-      }
-      // ---- Frobenius normalisation (memory_layer.py:55-56) ----
-      float ss = 0.f;
+        const int i0 = win ? max(0, r - P.omega + 1) : r;
+        for (int i = i0; i <= r; ++i) {
+          const float wgt = -et * sc * (win ? s.gate[3][i] : 1.f);
+          const float f0 = wgt * Fg[i * E + e0], f1 = wgt * Fg[i * E + e1];
+          const float4* g4 = (const float4*)&s.G[i * D + dc];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) ss = fmaf(Sv[0][j], Sv[0][j], fmaf(Sv[1][j], Sv[1][j], ss));
-      ss = block_sum(ss, s.red);
-      const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
-      float xv[32];
-      if (P.ns_steps == 0) {  // W += S / kappa
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          Wv[0][j] = al * Wv[0][j] + Sv[0][j] * inv;
-          Wv[1][j] = al * Wv[1][j] + Sv[1][j] * inv;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) xv[j] = Sv[0][j] * inv;
-        store_split32(s.Xh, s.Xl, e0, dc, D, xv);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) xv[j] = Sv[1][j] * inv;
-        store_split32(s.Xh, s.Xl, e1, dc, D, xv);
-      }
-      // ---- Polar Express (memory_layer.py:43-71), tall/wide folded into the tile orientation ----
-      for (int st = 0; st < P.ns_steps; ++st) {
-        const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
-        bool ok = run_mma(s, tm, phase, issue_gram);
-        float av[32];
-        tmem_ld32(tm + lane_off + TM_GRAM + dc, av);
-        tmem_wait_ld();
-        const int ra = 16 * qd + l;  // Gram row held by lanes 0-15 of the quadrant
-        if (l < 16) store_split32(s.Ah, s.Al, ra, dc, D, av);
-        ok = ok && run_mma(s, tm, phase, issue_a2);
-        float a2[32];
-        tmem_ld32(tm + lane_off + TM_A2 + dc, a2);
-        tmem_wait_ld();
-        if (l < 16) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
-          store_split32(s.Bh, s.Bl, ra, dc, D, a2);  // B'[ra][c]: rows = N index of X~ B'^T
-        }
-        ok = ok && run_mma(s, tm, phase, issue_xb);
-        if (!ok && !s.bad) {
-          set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
-          s.bad = 1;
-        }
-        float x0[32], x1[32];
-        tmem_ld32(tm + lane_off + TM_X + dc, x0);
-        tmem_ld32(tm + lane_off + TM_X + 64 + dc, x1);
-        tmem_wait_ld();
-        if (st + 1 < P.ns_steps) {
-          store_split32(s.Xh, s.Xl, e0, dc, D, x0);
-          store_split32(s.Xh, s.Xl, e1, dc, D, x1);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            Wv[0][j] = fmaf(al, Wv[0][j], x0[j]);
-            Wv[1][j] = fmaf(al, Wv[1][j], x1[j]);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 g = g4[j4];
+            Sv[0][4 * j4 + 0] = fmaf(f0, g.x, Sv[0][4 * j4 + 0]);
+            Sv[0][4 * j4 + 1] = fmaf(f0, g.y, Sv[0][4 * j4 + 1]);
+            Sv[0][4 * j4 + 2] = fmaf(f0, g.z, Sv[0][4 * j4 + 2]);
+            Sv[0][4 * j4 + 3] = fmaf(f0, g.w, Sv[0][4 * j4 + 3]);
+            Sv[1][4 * j4 + 0] = fmaf(f1, g.x, Sv[1][4 * j4 + 0]);
+            Sv[1][4 * j4 + 1] = fmaf(f1, g.y, Sv[1][4 * j4 + 1]);
+            Sv[1][4 * j4 + 2] = fmaf(f1, g.z, Sv[1][4 * j4 + 2]);
+            Sv[1][4 * j4 + 3] = fmaf(f1, g.w, Sv[1][4 * j4 + 3]);
           }
         }
-      }
-      // ---- read-out y = q + W1 gelu(W2 q)  (memory_layer.py:592-595) ----
-      const float* qv = &s.Q[r * D + dc];
-      if (rank == 1) {
-        float z0 = 0.f, z1 = 0.f;
+        PROF_ADD(2, ttok)
+        PROF_T(tnorm)
+        // ---- Frobenius normalisation (memory_layer.py:55-56) ----
+        float ss = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          z0 = fmaf(Wv[0][j], qv[j], z0);
-          z1 = fmaf(Wv[1][j], qv[j], z1);
-        }
-        s.zbuf[ch][e0] = z0;
-        s.zbuf[ch][e1] = z1;
-        __syncthreads();
-        const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
-        st_remote_f32(&s.pbuf[r & 1][tid], 0, gelu_tanh(z));
-        cluster_sync();
-      } else {
-        cluster_sync();
-        const float p0 = s.pbuf[r & 1][e0], p1 = s.pbuf[r & 1][e1];
-        float yv[32];
+        for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
+        ss = block_sum(ss, s.red);
+        const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
+        inv0 = inv;
+        if (P.ns_steps > 0) {
+          float xv[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) yv[j] = fmaf(Wv[0][j], p0, Wv[1][j] * p1);
-        float part = warp_reduce_scatter32(yv);
-        s.ybuf[qd][dc + l] = part;
-        __syncthreads();
-        const int t = c * cs + r;
-        if (tid < D && t < T) {
-          float y = s.Q[r * D + tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
-          st_act((TA*)a.y, (((size_t)b * T + t) * H + hh) * D + tid, y);
+          for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[0][jj] * inv;
+          store_split32(sl[j].Xh, sl[j].Xl, e0, dc, D, xv);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[1][jj] * inv;
+          store_split32(sl[j].Xh, sl[j].Xl, e1, dc, D, xv);
         }
+        PROF_ADD(3, tnorm)
       }
+      // ---- Polar Express (memory_layer.py:43-71) for the pair, interleaved ----
+      if (P.ns_steps > 0 && !pe_forward_multi(sl, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
+        set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
+        s.bad = 1;
+      }
+      for (int j = 0; j < n; ++j) {
+        PROF_T(tro)
+        const int r = r0 + j, t = c * cs + r;
+        const float al = s.gate[0][r];
+        if (P.ns_steps > 0) {
+          float x0[32], x1[32];
+          tmem_ld32(sl[j].tm + lane_off + TM_X + dc, x0);
+          tmem_ld32(sl[j].tm + lane_off + TM_X + 64 + dc, x1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            Wv[0][jj] = fmaf(al, Wv[0][jj], x0[jj]);
+            Wv[1][jj] = fmaf(al, Wv[1][jj], x1[jj]);
+          }
+        } else {  // PE with zero steps is the normalisation alone
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            Wv[0][jj] = al * Wv[0][jj] + Sv[0][jj] * inv0;
+            Wv[1][jj] = al * Wv[1][jj] + Sv[1][jj] * inv0;
+          }
+        }
+        // ---- read-out y = q + W1 gelu(W2 q)  (memory_layer.py:592-595) ----
+        if (tid < D) s.qv[tid] = t < T ? ld_act((const TA*)a.q, (((size_t)b * T + t) * H + hh) * D + tid) : 0.f;
+        __syncthreads();
+        if (rank == 1) {
+          float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            z0 = fmaf(Wv[0][jj], s.qv[dc + jj], z0);
+            z1 = fmaf(Wv[1][jj], s.qv[dc + jj], z1);
+          }
+          s.zbuf[ch][e0] = z0;
+          s.zbuf[ch][e1] = z1;
+          __syncthreads();
+          const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
+          st_remote_f32(&s.pbuf[r & 1][tid], 0, gelu_tanh(z));
+          cluster_sync();
+        } else {
+          cluster_sync();
+          const float p0 = s.pbuf[r & 1][e0], p1 = s.pbuf[r & 1][e1];
+          float yv[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(Wv[0][jj], p0, Wv[1][jj] * p1);
+          float part = warp_reduce_scatter32(yv);
+          s.ybuf[qd][dc + l] = part;
+          __syncthreads();
+          if (tid < D && t < T) {
+            float y = s.qv[tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
+            st_act((TA*)a.y, (((size_t)b * T + t) * H + hh) * D + tid, y);
+          }
+        }
+        __syncthreads();
+        PROF_ADD(6, tro)
+      }
+      PROF_ADD(4, tpair)
     }
     // ---- carry out ----
     if (c + 1 < nch) {
@@ -458,7 +410,8 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
   }
   fence_before();
   __syncthreads();
-  if (w == 0) tmem_dealloc(tm, TMEM_COLS);
+  if (w == 0) tmem_dealloc(s.tmem, TMEM_COLS);
+  PROF_FLUSH(g_prof_fwd)
 }
 
 // ---- host side ----------------------------------------------------------------
@@ -474,10 +427,19 @@ bool supported(const AtlasScanParams& p, const char** why) {
   return true;
 }
 size_t saved_bytes(const AtlasScanParams& p) { return (size_t)p.B * p.H * n_chunks(p) * 4 * DE * sizeof(float); }
-static size_t flags_bytes(const AtlasScanParams& p) { return (((size_t)p.B * p.H * sizeof(int)) + 255) & ~size_t(255); }
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+static size_t flags_bytes(const AtlasScanParams& p) { return align256((size_t)p.B * p.H * sizeof(int)); }
+static size_t fwd_clusters(const AtlasScanParams& p) {
+  return std::min((size_t)p.B * p.H, (size_t)max_clusters_bound());
+}
+size_t fwd_workspace_bytes(const AtlasScanParams& p) {
+  return flags_bytes(p) + (size_t)p.B * p.H * 4 * DE * sizeof(float) +
+         fwd_clusters(p) * 2 * MAXCS * E * sizeof(float);
+}
 size_t workspace_bytes(const AtlasScanParams& p) {
-  // one buffer serves the forward (flags + carry slots) and the backward
-  return std::max(flags_bytes(p) + (size_t)p.B * p.H * 4 * DE * sizeof(float), bwd_workspace_bytes(p));
+  // one buffer serves the forward and the backward
+  return std::max(fwd_workspace_bytes(p), bwd_workspace_bytes(p));
 }
 
 static int g_max_clusters = -1;
@@ -488,7 +450,6 @@ static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) 
   cudaError_t e = cudaFuncSetAttribute(fwd_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * nclusters);
   cfg.blockDim = dim3(NT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -504,9 +465,8 @@ static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) 
     cfg.gridDim = dim3(2);
     if (cudaOccupancyMaxActiveClusters(&n, fwd_kernel<TA>, &cfg) != cudaSuccess || n <= 0) n = 1;
     g_max_clusters = n;
-    cfg.gridDim = dim3(2 * nclusters);
   }
-  if (nclusters > g_max_clusters) cfg.gridDim = dim3(2 * g_max_clusters);
+  cfg.gridDim = dim3(2 * std::min(nclusters, g_max_clusters));
   return cudaLaunchKernelEx(&cfg, fwd_kernel<TA>, k);
 }
 
@@ -518,12 +478,21 @@ cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
   uint8_t* ws = (uint8_t*)a.ws;
   k.flags = (int*)ws;
   k.carries = (float*)(ws + flags_bytes(a.p));
+  k.fscr = k.carries + (size_t)k.nchains * 4 * DE;
   cudaError_t e = cudaMemsetAsync(k.flags, 0, flags_bytes(a.p), st);
   if (e != cudaSuccess) return e;
-  int ncl = k.nchains;
+  const int ncl = (int)fwd_clusters(a.p);
   return a.p.act_dtype == ATLAS_BF16 ? launch_fwd_t<__nv_bfloat16>(k, ncl, st) : launch_fwd_t<float>(k, ncl, st);
 }
 
 }  // namespace tc
 }  // namespace atlas
 
+#ifdef ATLAS_PHASE_PROF
+// Instrumented builds only: read and clear the forward kernel's phase cycle counters.
+extern "C" int atlas_debug_prof_fwd(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, atlas::tc::g_prof_fwd, 16 * sizeof(unsigned long long));
+  unsigned long long z[16] = {};
+  return cudaMemcpyToSymbol(atlas::tc::g_prof_fwd, z, sizeof(z)) == cudaSuccess ? 0 : 3;
+}
+#endif

@@ -53,17 +53,26 @@ struct __align__(1024) Smem {
   uint8_t Pl[AT_BYTES];
   uint8_t Yh[AT_BYTES];  // Sym
   uint8_t Yl[AT_BYTES];
-  float Pf[D * D];       // P in float32 (transpose); phase A/D: k or derr of the chunk
+  float Gc[MAXCS * D];   // column factors (err or k) of the chunk
   float zbuf[2][E];
   float xbuf[2][E];      // exchanged vector (p into rank 0, dp into rank 1), double-buffered
   float ybuf[4][D];
   float qv[D], dyv[D];
   float ipacc[MAXCS];
+  float gate[4][MAXCS];  // alpha, eta, theta, gamma of the chunk
+  float nrm[MAXCS];      // ||S_t||_F (with the 1e-12) per token, from phase B
   float red[8];
   uint64_t bar;
+  uint64_t bar2;         // completion barrier of the second in-flight Polar Express
+  uint64_t bar_ld;       // bulk loads of saved Newton-Schulz tiles
   uint32_t tmem;
   int bad;
 };
+// P in float32 for the transpose (and the chunk's k / derr in phases A and D)
+// lives in the Sym tiles' 16 KB, free at those times.  16-byte chunks of a row
+// are XOR-swizzled by the row so row stores and column reads avoid bank conflicts.
+__device__ __forceinline__ float* pf_base(Smem& s) { return (float*)s.Yh; }
+__device__ __forceinline__ int pf_idx(int r, int c) { return r * 64 + ((((c >> 2) ^ (r & 15))) << 2) + (c & 3); }
 
 // per-cluster scratch, in floats
 constexpr size_t FRZ_E = (size_t)MAXCS * E, FRZ_D = (size_t)MAXCS * D;
@@ -71,10 +80,10 @@ struct ClusterWS {
   float *h, *act, *chain, *r, *err, *k;    // frozen pass
   float *dF[2], *dG[2], *scal;             // accumulators: dF/dG per rank; scal[4][MAXCS]
   float *Ssave[2], *Wsave[2], *vec[2];     // per rank: S_{t-1..}, W_{t-1}, p or dz
-  uint8_t* ns[2];                           // per rank: 5 steps of (X hi, X lo, A hi, A lo, B hi, B lo)
+  uint8_t* ns[2];                           // per rank, per token: 5 steps of (X hi, X lo, A hi, A lo, B hi, B lo)
 };
 constexpr size_t NS_STEP_BYTES = 2 * XT_BYTES + 4 * AT_BYTES;
-constexpr size_t RANK_FLOATS = (size_t)(MAXCS + 1) * DE + (size_t)MAXCS * DE + FRZ_E + 5 * NS_STEP_BYTES / 4;
+constexpr size_t RANK_FLOATS = (size_t)(MAXCS + 1) * DE + (size_t)MAXCS * DE + FRZ_E + (size_t)MAXCS * 5 * NS_STEP_BYTES / 4;
 constexpr size_t CLUSTER_FLOATS = 4 * FRZ_E + 2 * FRZ_D + 2 * FRZ_E + 2 * FRZ_D + 4 * MAXCS + 2 * RANK_FLOATS;
 
 __device__ ClusterWS carve(float* base) {
@@ -95,7 +104,7 @@ __device__ ClusterWS carve(float* base) {
     w.Ssave[r] = p; p += (size_t)(MAXCS + 1) * DE;
     w.Wsave[r] = p; p += (size_t)MAXCS * DE;
     w.vec[r] = p; p += FRZ_E;
-    w.ns[r] = (uint8_t*)p; p += 5 * NS_STEP_BYTES / 4;
+    w.ns[r] = (uint8_t*)p; p += (size_t)MAXCS * 5 * NS_STEP_BYTES / 4;  // every token's 5 steps
   }
   return w;
 }
@@ -146,7 +155,7 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
   const int T = P.T, H = P.H, tid = threadIdx.x;
   const float* W1t = slot;
   const float* W2 = slot + 2 * DE;
-  float* kb = s.Pf;  // cs x D
+  float* kb = pf_base(s);  // cs x D
   if (rank == 0) {
     const TA* kp = (const TA*)a.k;
     for (int i = tid; i < cs * D; i += NT) {
@@ -215,54 +224,6 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
   cluster_sync();
 }
 
-// Polar Express forward of the tiles in s.X (X0 already stored), five steps,
-// optionally saving each step's operand tiles to `ns`.  On return the final
-// X~ (float32) is in xo (rows e0 / e1, 32 columns each).
-__device__ bool pe_forward_tc(Smem& s, uint32_t tm, uint32_t& phase, int steps, uint8_t* ns, float (*xo)[32]) {
-  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
-  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
-  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
-  bool ok = true;
-  for (int st = 0; st < steps; ++st) {
-    const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
-    ok = mma_sync_run(&s.bar, &s.bad, phase, [&] { mma3(tm + TM_GRAM, s.Xh, s.Xl, true, s.Xh, s.Xl, true, 64, E, 0, false); }) && ok;
-    float av[32], a2[32];
-    tmem_ld32(tm + lane_off + TM_GRAM + dc, av);
-    tmem_wait_ld();
-    if (l < 16) store_split32(s.Ah, s.Al, ra, dc, D, av);
-    ok = mma_sync_run(&s.bar, &s.bad, phase, [&] { mma3(tm + TM_A2, s.Ah, s.Al, false, s.Ah, s.Al, true, 64, D, 0, false); }) && ok;
-    tmem_ld32(tm + lane_off + TM_A2 + dc, a2);
-    tmem_wait_ld();
-    if (l < 16) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
-      store_split32(s.Bh, s.Bl, ra, dc, D, a2);
-    }
-    ok = mma_sync_run(&s.bar, &s.bad, phase, [&] {
-           mma3(tm + TM_X, s.Xh, s.Xl, false, s.Bh, s.Bl, false, 128, D, 0, false);
-           mma3(tm + TM_X + 64, s.Xh, s.Xl, false, s.Bh, s.Bl, false, 128, D, 16384, false);
-         }) && ok;
-    if (ns) {  // operand tiles of this step, for the VJP
-      uint8_t* o = ns + (size_t)st * NS_STEP_BYTES;
-      copy16(o, s.Xh, XT_BYTES);
-      copy16(o + XT_BYTES, s.Xl, XT_BYTES);
-      copy16(o + 2 * XT_BYTES, s.Ah, AT_BYTES);
-      copy16(o + 2 * XT_BYTES + AT_BYTES, s.Al, AT_BYTES);
-      copy16(o + 2 * XT_BYTES + 2 * AT_BYTES, s.Bh, AT_BYTES);
-      copy16(o + 2 * XT_BYTES + 3 * AT_BYTES, s.Bl, AT_BYTES);
-      __syncthreads();  // all reads of X tiles done before they are overwritten
-    }
-    tmem_ld32(tm + lane_off + TM_X + dc, xo[0]);
-    tmem_ld32(tm + lane_off + TM_X + 64 + dc, xo[1]);
-    tmem_wait_ld();
-    if (st + 1 < steps) {
-      store_split32(s.Xh, s.Xl, e0, dc, D, xo[0]);
-      store_split32(s.Xh, s.Xl, e1, dc, D, xo[1]);
-    }
-  }
-  return ok;
-}
-
 }  // namespace bwd
 }  // namespace tc
 }  // namespace atlas
@@ -271,8 +232,13 @@ namespace atlas {
 namespace tc {
 namespace bwd {
 
+#ifdef ATLAS_PHASE_PROF
+__device__ unsigned long long g_prof_bwd[16];
+#endif
+
 template <typename TA>
 __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
+  PROF_DECL
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const BwdArgs& a = K.a;
@@ -299,6 +265,8 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
   }
   if (tid == 0) {
     mbar_init(&s.bar, 1);
+    mbar_init(&s.bar_ld, 1);
+    mbar_init(&s.bar2, 1);
     fence_mbar_init();
     s.bad = 0;
   }
@@ -306,7 +274,11 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
   __syncthreads();
   fence_after();
   const uint32_t tm = s.tmem;
-  uint32_t phase = 0;
+  uint32_t phase_ld = 0;
+  PROF_INIT
+  PESlot sl[2];
+  sl[0] = PESlot{s.Xh, s.Xl, s.Ah, s.Al, s.Bh, s.Bl, &s.bar, tm, 0, nullptr, 0};
+  sl[1] = PESlot{s.Gh, s.Gl, s.Ph, s.Pl, s.Yh, s.Yl, &s.bar2, tm + 256, 0, nullptr, 0};
 
   const long total = (long)K.nchains * nch;
   for (long kk = cluster; kk < total; kk += nclusters) {
@@ -331,9 +303,23 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
       for (int i = tid; i < 2 * (int)FRZ_E; i += NT) w.dF[0][i] = 0.f;
     else
       for (int i = tid; i < 2 * (int)FRZ_D + 4 * MAXCS; i += NT) w.dG[0][i] = 0.f;
+    PROF_T(tA)
     frozen_to_scratch<TA>(a, s, w, slot, b, hh, c, cs, rank);
+    for (int i = tid; i < cs * D / 4; i += NT) ((float4*)s.Gc)[i] = ((const float4*)Gm)[i];
+    for (int r = tid; r < cs; r += NT) {
+      const Gates gg = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + r);
+      s.gate[0][r] = gg.a;
+      s.gate[1][r] = gg.e;
+      s.gate[2][r] = gg.t;
+      s.gate[3][r] = gg.g;
+    }
+    __syncthreads();
+    PROF_ADD(2, tA)
+    PROF_T(tB)
 
     // ================= B: forward recompute over the chunk =================
+    // Tokens go through Polar Express in pairs (slot 0: X/A/B tiles, slot 1: the
+    // G/P/Y tiles, free during this phase) so MMAs overlap the other token's epilogue.
     float Sv[2][32], Wv[2][32];
     ld32(mine + e0 * D + dc, Wv[0]);
     ld32(mine + e1 * D + dc, Wv[1]);
@@ -341,106 +327,130 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
     ld32(mine + DE + e1 * D + dc, Sv[1]);
     st32(Ssave + e0 * D + dc, Sv[0]);
     st32(Ssave + e1 * D + dc, Sv[1]);
-    for (int r = 0; r < cs; ++r) {
-      const int t = c * cs + r;
-      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, t);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        Sv[0][jj] *= g.t;
-        Sv[1][jj] *= g.t;
-      }
-      const int i0 = win ? max(0, r - P.omega + 1) : r;
-      for (int i = i0; i <= r; ++i) {
-        const float gi = win ? load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + i).g : 1.f;
-        const float wgt = -g.e * sc * gi;
-        const float f0 = wgt * Fm[i * E + e0], f1 = wgt * Fm[i * E + e1];
-        float gv[32];
-        ld32(Gm + i * D + dc, gv);
+    const int npair = P.ns_steps > 0 ? 2 : 1;
+    for (int r0 = 0; r0 < cs; r0 += npair) {
+      const int n = min(npair, cs - r0);
+      float inv0 = 0.f;
+      for (int jp = 0; jp < n; ++jp) {
+        const int r = r0 + jp;
+        const float et = s.gate[1][r], th = s.gate[2][r];
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
-          Sv[0][jj] = fmaf(f0, gv[jj], Sv[0][jj]);
-          Sv[1][jj] = fmaf(f1, gv[jj], Sv[1][jj]);
+          Sv[0][jj] *= th;
+          Sv[1][jj] *= th;
+        }
+        const int i0 = win ? max(0, r - P.omega + 1) : r;
+        for (int i = i0; i <= r; ++i) {
+          const float wgt = -et * sc * (win ? s.gate[3][i] : 1.f);
+          const float f0 = wgt * Fm[i * E + e0], f1 = wgt * Fm[i * E + e1];
+          float gv[32];
+          ld32(&s.Gc[i * D + dc], gv);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            Sv[0][jj] = fmaf(f0, gv[jj], Sv[0][jj]);
+            Sv[1][jj] = fmaf(f1, gv[jj], Sv[1][jj]);
+          }
+        }
+        st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
+        st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
+        float ss = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
+        ss = block_sum(ss, s.red);
+        const float nrm_r = sqrtf(ss + 1e-12f);
+        const float inv = 1.0f / (nrm_r * 1.01f + 1e-6f);
+        if (tid == 0) s.nrm[r] = nrm_r;
+        inv0 = inv;
+        if (P.ns_steps > 0) {
+          float xv[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[0][jj] * inv;
+          store_split32(sl[jp].Xh, sl[jp].Xl, e0, dc, D, xv);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[1][jj] * inv;
+          store_split32(sl[jp].Xh, sl[jp].Xl, e1, dc, D, xv);
         }
       }
-      st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
-      st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
-      st32(Wsave + (size_t)r * DE + e0 * D + dc, Wv[0]);
-      st32(Wsave + (size_t)r * DE + e1 * D + dc, Wv[1]);
-      float ss = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
-      ss = block_sum(ss, s.red);
-      const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
-      if (P.ns_steps == 0) {
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          Wv[0][jj] = g.a * Wv[0][jj] + Sv[0][jj] * inv;
-          Wv[1][jj] = g.a * Wv[1][jj] + Sv[1][jj] * inv;
-        }
-      } else {
-        float xo[2][32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          xo[0][jj] = Sv[0][jj] * inv;
-          xo[1][jj] = Sv[1][jj] * inv;
-        }
-        store_split32(s.Xh, s.Xl, e0, dc, D, xo[0]);
-        store_split32(s.Xh, s.Xl, e1, dc, D, xo[1]);
-        if (!pe_forward_tc(s, tm, phase, P.ns_steps, nullptr, xo) && !s.bad) {
+      if (P.ns_steps > 0) {
+        // keep every step's operand tiles of these tokens for the VJP in phase C
+        sl[0].ns = w.ns[rank] + (size_t)r0 * 5 * NS_STEP_BYTES;
+        sl[1].ns = sl[0].ns + 5 * NS_STEP_BYTES;
+        if (P.pe_ste) sl[0].ns = sl[1].ns = nullptr;
+        if (!pe_forward_multi(sl, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
           set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
           s.bad = 1;
         }
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          Wv[0][jj] = fmaf(g.a, Wv[0][jj], xo[0][jj]);
-          Wv[1][jj] = fmaf(g.a, Wv[1][jj], xo[1][jj]);
-        }
       }
-      // read-out backward pieces (memory_layer.py:592-595)
-      if (tid < D) {
-        const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
-        s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
-        s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
-      }
-      __syncthreads();
-      {
-        const float* xv = rank ? s.qv : s.dyv;  // rank 1: z = W2 q ; rank 0: dp = W1^T dy
-        float z0 = 0.f, z1 = 0.f;
+      for (int jp = 0; jp < n; ++jp) {
+        const int r = r0 + jp, t = c * cs + r;
+        const float al = s.gate[0][r];
+        st32(Wsave + (size_t)r * DE + e0 * D + dc, Wv[0]);  // W_{t-1}
+        st32(Wsave + (size_t)r * DE + e1 * D + dc, Wv[1]);
+        if (P.ns_steps > 0) {
+          float x0[32], x1[32];
+          tmem_ld32(sl[jp].tm + lane_off + TM_X + dc, x0);
+          tmem_ld32(sl[jp].tm + lane_off + TM_X + 64 + dc, x1);
+          tmem_wait_ld();
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          z0 = fmaf(Wv[0][jj], xv[dc + jj], z0);
-          z1 = fmaf(Wv[1][jj], xv[dc + jj], z1);
-        }
-        s.zbuf[ch][e0] = z0;
-        s.zbuf[ch][e1] = z1;
-        __syncthreads();
-        const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
-        // rank 1 sends p = gelu(z) to rank 0; rank 0 sends dp to rank 1
-        st_remote_f32(&s.xbuf[r & 1][tid], rank ^ 1u, rank ? gelu_tanh(z) : z);
-        cluster_sync();
-        if (rank == 0) {
-          vec[r * E + tid] = s.xbuf[r & 1][tid];  // p_t
+          for (int jj = 0; jj < 32; ++jj) {
+            Wv[0][jj] = fmaf(al, Wv[0][jj], x0[jj]);
+            Wv[1][jj] = fmaf(al, Wv[1][jj], x1[jj]);
+          }
         } else {
-          const float dz = s.xbuf[r & 1][tid] * gelu_tanh_grad(z);
-          vec[r * E + tid] = dz;
-          s.zbuf[0][tid] = dz;
-          __syncthreads();
-          const float dz0 = s.zbuf[0][e0], dz1 = s.zbuf[0][e1];
-          float yv[32];
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(Wv[0][jj], dz0, Wv[1][jj] * dz1);
-          float part = warp_reduce_scatter32(yv);
-          s.ybuf[qd][dc + l] = part;
-          __syncthreads();
-          if (tid < D && t < T) {
-            const float dq = s.dyv[tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
-            st_act((TA*)a.dq, (((size_t)b * T + t) * H + hh) * D + tid, dq);
+          for (int jj = 0; jj < 32; ++jj) {
+            Wv[0][jj] = al * Wv[0][jj] + Sv[0][jj] * inv0;
+            Wv[1][jj] = al * Wv[1][jj] + Sv[1][jj] * inv0;
           }
         }
+        // read-out backward pieces (memory_layer.py:592-595)
+        if (tid < D) {
+          const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
+          s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
+          s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
+        }
+        __syncthreads();
+        {
+          const float* xv = rank ? s.qv : s.dyv;  // rank 1: z = W2 q ; rank 0: dp = W1^T dy
+          float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            z0 = fmaf(Wv[0][jj], xv[dc + jj], z0);
+            z1 = fmaf(Wv[1][jj], xv[dc + jj], z1);
+          }
+          s.zbuf[ch][e0] = z0;
+          s.zbuf[ch][e1] = z1;
+          __syncthreads();
+          const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
+          // rank 1 sends p = gelu(z) to rank 0; rank 0 sends dp to rank 1
+          st_remote_f32(&s.xbuf[r & 1][tid], rank ^ 1u, rank ? gelu_tanh(z) : z);
+          cluster_sync();
+          if (rank == 0) {
+            vec[r * E + tid] = s.xbuf[r & 1][tid];  // p_t
+          } else {
+            const float dz = s.xbuf[r & 1][tid] * gelu_tanh_grad(z);
+            vec[r * E + tid] = dz;
+            s.zbuf[0][tid] = dz;
+            __syncthreads();
+            const float dz0 = s.zbuf[0][e0], dz1 = s.zbuf[0][e1];
+            float yv[32];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(Wv[0][jj], dz0, Wv[1][jj] * dz1);
+            float part = warp_reduce_scatter32(yv);
+            s.ybuf[qd][dc + l] = part;
+            __syncthreads();
+            if (tid < D && t < T) {
+              const float dq = s.dyv[tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
+              st_act((TA*)a.dq, (((size_t)b * T + t) * H + hh) * D + tid, dq);
+            }
+          }
+        }
+        __syncthreads();
       }
-      __syncthreads();
     }
 
+    PROF_ADD(3, tB)
+    PROF_T(tC)
     // ================= C: reverse over the chunk's tokens =================
     float dW[2][32], dS[2][32];
     {
@@ -469,7 +479,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
     }
     for (int r = cs - 1; r >= 0; --r) {
       const int t = c * cs + r;
-      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, t);
+      const Gates g = {s.gate[0][r], s.gate[1][r], s.gate[2][r], s.gate[3][r]};
       if (tid < D) {
         const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
         s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
@@ -508,54 +518,63 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
       }
       if (!P.pe_ste) {
         const float* St = Ssave + (size_t)(r + 1) * DE;
+        const float nrm = s.nrm[r], kap = nrm * 1.01f + 1e-6f, inv = 1.0f / kap;
         float xo[2][32];
-        ld32(St + e0 * D + dc, xo[0]);
-        ld32(St + e1 * D + dc, xo[1]);
-        float ss = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) ss = fmaf(xo[0][jj], xo[0][jj], fmaf(xo[1][jj], xo[1][jj], ss));
-        ss = block_sum(ss, s.red);
-        const float nrm = sqrtf(ss + 1e-12f);
-        const float kap = nrm * 1.01f + 1e-6f, inv = 1.0f / kap;
         float gx[2][32];
         if (P.ns_steps > 0) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            xo[0][jj] *= inv;
-            xo[1][jj] *= inv;
+          PROF_T(tns)
+          bool ok = true;
+          uint8_t* nscur = w.ns[rank] + (size_t)r * 5 * NS_STEP_BYTES;
+          if (!s.bad) {  // last step's tiles of token r (saved in phase B)
+            __syncthreads();
+            if (tid == 0) {
+              const uint8_t* o = nscur + (size_t)(P.ns_steps - 1) * NS_STEP_BYTES;
+              mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
+              bulk_g2s(s.Xh, o, XT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Xl, o + XT_BYTES, XT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Ah, o + 2 * XT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Al, o + 2 * XT_BYTES + AT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES, &s.bar_ld);
+            }
+            if (!mbar_wait(&s.bar_ld, phase_ld)) ok = false;
+            phase_ld ^= 1;
           }
-          store_split32(s.Xh, s.Xl, e0, dc, D, xo[0]);
-          store_split32(s.Xh, s.Xl, e1, dc, D, xo[1]);
-          bool ok = pe_forward_tc(s, tm, phase, P.ns_steps, w.ns[rank], xo);
+          PROF_ADD(5, tns)
+          PROF_T(tvjp)
           store_split32(s.Gh, s.Gl, e0, dc, D, dW[0]);
           store_split32(s.Gh, s.Gl, e1, dc, D, dW[1]);
-          for (int st = P.ns_steps - 1; st >= 0; --st) {
+          const int steps_ = P.ns_steps;
+          for (int st = steps_ - 1; st >= 0; --st) {
             const float cb = (float)kPE[st][1], cc = (float)kPE[st][2];
-            const uint8_t* o = w.ns[rank] + (size_t)st * NS_STEP_BYTES;
-            __syncthreads();
-            copy16(s.Xh, o, XT_BYTES);
-            copy16(s.Xl, o + XT_BYTES, XT_BYTES);
-            copy16(s.Ah, o + 2 * XT_BYTES, AT_BYTES);
-            copy16(s.Al, o + 2 * XT_BYTES + AT_BYTES, AT_BYTES);
-            copy16(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES);
-            copy16(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES);
+            if (st + 1 < steps_ && !s.bad) {  // tiles of step st were prefetched during step st + 1
+              if (!mbar_wait(&s.bar_ld, phase_ld)) ok = false;
+              phase_ld ^= 1;
+            }
+            PROF_T(tcp)
+            PROF_ADD(9, tcp)
             // P = G~^T X~
-            ok = mma_sync_run(&s.bar, &s.bad, phase, [&] { mma3(tm + TM_GRAM, s.Gh, s.Gl, true, s.Xh, s.Xl, true, 64, E, 0, false); }) && ok;
+            ok = mma_sync_run(&s.bar, &s.bad, sl[0].phase, [&] { mma3<E>(tm + TM_GRAM, s.Gh, s.Gl, true, s.Xh, s.Xl, true, 64, 0, false); }, PROF_PTR) && ok;
             float pv[32];
             tmem_ld32(tm + lane_off + TM_GRAM + dc, pv);
             tmem_wait_ld();
-            if (l < 16) st32(&s.Pf[ra * D + dc], pv);
+            float* Pf = pf_base(s);
+            if (l < 16) {
+#pragma unroll
+              for (int m = 0; m < 8; ++m)
+                *(float4*)&Pf[pf_idx(ra, dc + 4 * m)] = make_float4(pv[4 * m], pv[4 * m + 1], pv[4 * m + 2], pv[4 * m + 3]);
+            }
             __syncthreads();
             if (l < 16) {
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) pv[jj] += s.Pf[(dc + jj) * D + ra];  // Ps = P + P^T
+              for (int jj = 0; jj < 32; ++jj) pv[jj] += Pf[pf_idx(dc + jj, ra)];  // Ps = P + P^T
               store_split32(s.Ph, s.Pl, ra, dc, D, pv);
             }
             // Sym = b Ps + c (Ps A + A Ps)
-            ok = mma_sync_run(&s.bar, &s.bad, phase, [&] {
-                   mma3(tm + TM_A2, s.Ph, s.Pl, false, s.Ah, s.Al, true, 64, D, 0, false);
-                   mma3(tm + TM_A2, s.Ah, s.Al, false, s.Ph, s.Pl, true, 64, D, 0, true);
-                 }) && ok;
+            ok = mma_sync_run(&s.bar, &s.bad, sl[0].phase, [&] {
+                   mma3<D>(tm + TM_A2, s.Ph, s.Pl, false, s.Ah, s.Al, true, 64, 0, false);
+                   mma3<D>(tm + TM_A2, s.Ah, s.Al, false, s.Ph, s.Pl, true, 64, 0, true);
+                 }, PROF_PTR) && ok;
             float yv[32];
             tmem_ld32(tm + lane_off + TM_A2 + dc, yv);
             tmem_wait_ld();
@@ -565,12 +584,22 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
               store_split32(s.Yh, s.Yl, ra, dc, D, yv);
             }
             // dX~ = G~ B' + X~ Sym
-            ok = mma_sync_run(&s.bar, &s.bad, phase, [&] {
+            ok = mma_sync_run(&s.bar, &s.bad, sl[0].phase, [&] {
                    for (int h2 = 0; h2 < 2; ++h2) {
-                     mma3(tm + TM_X + 64 * h2, s.Gh, s.Gl, false, s.Bh, s.Bl, true, 128, D, 16384 * h2, false);
-                     mma3(tm + TM_X + 64 * h2, s.Xh, s.Xl, false, s.Yh, s.Yl, true, 128, D, 16384 * h2, true);
+                     mma3<D>(tm + TM_X + 64 * h2, s.Gh, s.Gl, false, s.Bh, s.Bl, true, 128, 16384 * h2, false);
+                     mma3<D>(tm + TM_X + 64 * h2, s.Xh, s.Xl, false, s.Yh, s.Yl, true, 128, 16384 * h2, true);
                    }
-                 }) && ok;
+                 }, PROF_PTR) && ok;
+            if (st > 0 && tid == 0 && !s.bad) {  // prefetch step st-1's tiles; X, A, B' are free now
+              const uint8_t* o = nscur + (size_t)(st - 1) * NS_STEP_BYTES;
+              mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
+              bulk_g2s(s.Xh, o, XT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Xl, o + XT_BYTES, XT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Ah, o + 2 * XT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Al, o + 2 * XT_BYTES + AT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES, &s.bar_ld);
+            }
             tmem_ld32(tm + lane_off + TM_X + dc, gx[0]);
             tmem_ld32(tm + lane_off + TM_X + 64 + dc, gx[1]);
             tmem_wait_ld();
@@ -579,6 +608,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
               store_split32(s.Gh, s.Gl, e1, dc, D, gx[1]);
             }
           }
+          PROF_ADD(6, tvjp)
           if (!ok && !s.bad) {
             set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
             s.bad = 1;
@@ -615,13 +645,14 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dth = fmaf(dS[1][jj], sv[jj], dth);
       }
+      PROF_T(twin)
       const int i0 = win ? max(0, r - P.omega + 1) : r;
       for (int i = i0; i <= r; ++i) {
-        const float gi = win ? load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + i).g : 1.f;
+        const float gi = win ? s.gate[3][i] : 1.f;
         const float cf = -g.e * sc * gi;
         const float f0 = Fm[i * E + e0], f1 = Fm[i * E + e1];
         float gv[32], cv[32];
-        ld32(Gm + i * D + dc, gv);
+        ld32(&s.Gc[i * D + dc], gv);
         float rv0 = 0.f, rv1 = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -638,11 +669,12 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         const float part = warp_reduce_scatter32(cv);
         red_add(&w.dG[rank][i * D + dc + l], cf * part);
       }
+      PROF_ADD(7, twin)
       dal = block_sum(dal, s.red);
       dth = block_sum(dth, s.red);  // also orders the ipacc atomics before the reads below
       if (tid >= i0 && tid <= r) {
         const float ip = s.ipacc[tid];
-        const float gi = win ? load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + tid).g : 1.f;
+        const float gi = win ? s.gate[3][tid] : 1.f;
         red_add(&w.scal[MAXCS + r], -sc * gi * ip);          // deta_t
         if (win) red_add(&w.scal[3 * MAXCS + tid], -g.e * sc * ip);  // dgamma_i
       }
@@ -659,6 +691,8 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
       }
     }
 
+    PROF_ADD(4, tC)
+    PROF_T(tD)
     // ================= D: frozen-state pass backward =================
     __threadfence();
     cluster_sync();  // both ranks' window accumulations are complete
@@ -667,7 +701,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
       const float* W2 = slot + 2 * DE;
       float* dw1t = (float*)s.Xh;  // cs x E
       float* dhb = (float*)s.Gh;   // cs x E
-      float* derr = s.Pf;          // cs x D
+      float* derr = pf_base(s);    // cs x D
       {  // thread e: d(W1^T err) = dchain * gelu'(h); dh = dchain * r * gelu''(h)
         const int e = tid;
         for (int i = 0; i < cs; ++i) {
@@ -763,6 +797,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         }
       }
     }
+    PROF_ADD(8, tD)
     if (P.stop_grad_chunks) {  // memory_layer.py:665: the incoming carry is detached
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) dW[0][jj] = dW[1][jj] = dS[0][jj] = dS[1][jj] = 0.f;
@@ -796,6 +831,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
   fence_before();
   __syncthreads();
   if (wp == 0) tmem_dealloc(tm, TMEM_COLS);
+  PROF_FLUSH(g_prof_bwd)
 }
 
 }  // namespace bwd
@@ -803,12 +839,6 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
 // ---- host side ----------------------------------------------------------------
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-static int max_clusters_bound() {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms / 2;
-}
 
 size_t bwd_workspace_bytes(const AtlasScanParams& p) {
   const size_t nc = (size_t)p.B * p.H;
@@ -862,3 +892,12 @@ cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t st) {
 
 }  // namespace tc
 }  // namespace atlas
+
+#ifdef ATLAS_PHASE_PROF
+// Instrumented builds only: read and clear the backward kernel's phase cycle counters.
+extern "C" int atlas_debug_prof_bwd(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, atlas::tc::bwd::g_prof_bwd, 16 * sizeof(unsigned long long));
+  unsigned long long z[16] = {};
+  return cudaMemcpyToSymbol(atlas::tc::bwd::g_prof_bwd, z, sizeof(z)) == cudaSuccess ? 0 : 3;
+}
+#endif

@@ -16,7 +16,7 @@ constexpr int MAXCS = 64;
 constexpr int DE = D * E;
 constexpr int XT_BYTES = E * D * 2;  // bf16 E x D tile
 constexpr int AT_BYTES = D * D * 2;  // bf16 D x D tile
-constexpr int TMEM_COLS = 256;
+constexpr int TMEM_COLS = 512;  // two in-flight problems of 256 columns each
 // TMEM column map
 constexpr uint32_t TM_X = 0;      // X~ update: rows 0-127 in cols [0,64), rows 128-255 in [64,128)
 constexpr uint32_t TM_GRAM = 128; // Gram A (M=64 layout)
@@ -50,12 +50,14 @@ __device__ __forceinline__ void store_split8(uint8_t* th, uint8_t* tl, uint32_t 
   uint32_t h[4], l[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * k]);
-    __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * k + 1]);
-    __nv_bfloat16 l0 = __float2bfloat16_rn(v[2 * k] - __bfloat162float(h0));
-    __nv_bfloat16 l1 = __float2bfloat16_rn(v[2 * k + 1] - __bfloat162float(h1));
-    h[k] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-    l[k] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+    // packed conversions (one cvt.rn.bf16x2.f32 per pair); bf16 -> f32 is a bit shift
+    __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    uint32_t hb = *reinterpret_cast<uint32_t*>(&hv);
+    float r0 = v[2 * k] - __uint_as_float(hb << 16);
+    float r1 = v[2 * k + 1] - __uint_as_float(hb & 0xFFFF0000u);
+    __nv_bfloat162 lv = __floats2bfloat162_rn(r0, r1);
+    h[k] = hb;
+    l[k] = *reinterpret_cast<uint32_t*>(&lv);
   }
   *(uint4*)(th + off) = make_uint4(h[0], h[1], h[2], h[3]);
   *(uint4*)(tl + off) = make_uint4(l[0], l[1], l[2], l[3]);
@@ -105,32 +107,56 @@ __device__ __forceinline__ float warp_reduce_scatter32(float* v) {
 // Operand tiles have 64 columns (core-matrix tiles of C = 64).  amn / bmn pick
 // the MN-major view (rows = K index) instead of the K-major view (rows = M/N).
 // a_off is a byte offset into the A tiles (selects the 128-row half for M = 128).
+// Descriptors are built once per term; stepping K by 16 adds to the 14-bit
+// start-address field (shared-memory addresses < 256 KB never carry out of it).
+template <int K>
 __device__ __forceinline__ void mma3(uint32_t tmd, const uint8_t* ah, const uint8_t* al, bool amn,
-                                     const uint8_t* bh, const uint8_t* bl, bool bmn, int M, int K,
-                                     uint32_t a_off, bool accumulate) {
+                                     const uint8_t* bh, const uint8_t* bl, bool bmn, int M, uint32_t a_off,
+                                     bool accumulate) {
   const uint32_t id = idesc_bf16(M, 64, amn, bmn);
+  const uint64_t sa = amn ? (2048 >> 4) : (256 >> 4);
+  const uint64_t sb = bmn ? (2048 >> 4) : (256 >> 4);
   const uint8_t* ta[3] = {ah, ah, al};
   const uint8_t* tb[3] = {bh, bl, bh};
-  for (int t = 0; t < 3; ++t)
-    for (int ks = 0; ks < K / 16; ++ks) {
-      uint32_t aa = smem_u32(ta[t]) + a_off + (amn ? ks * 2048 : ks * 256);
-      uint32_t bb = smem_u32(tb[t]) + (bmn ? ks * 2048 : ks * 256);
-      uint64_t da = amn ? desc_mnmajor(aa, 64) : desc_kmajor(aa, 64);
-      uint64_t db = bmn ? desc_mnmajor(bb, 64) : desc_kmajor(bb, 64);
-      mma_bf16(tmd, da, db, id, (accumulate || t || ks) ? 1u : 0u);
-    }
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const uint32_t aa = smem_u32(ta[t]) + a_off, bb = smem_u32(tb[t]);
+    const uint64_t da = amn ? desc_mnmajor(aa, 64) : desc_kmajor(aa, 64);
+    const uint64_t db = bmn ? desc_mnmajor(bb, 64) : desc_kmajor(bb, 64);
+#pragma unroll
+    for (int ks = 0; ks < K / 16; ++ks)
+      mma_bf16(tmd, da + ks * sa, db + ks * sb, id, (accumulate || t || ks) ? 1u : 0u);
+  }
 }
 
-// All threads of the CTA: publish freshly written operand tiles to the tensor
-// core, let thread 0 issue, wait for the commit.  When an earlier wait expired
-// (*bad != 0) the work is skipped but the control flow is kept.
+// Optional phase timers (build with -DATLAS_PHASE_PROF; thread 0 accumulates
+// clock64() deltas into a shared array; off in the product build).
+#ifdef ATLAS_PHASE_PROF
+#define PROF_DECL __shared__ unsigned long long s_prof[16];
+#define PROF_INIT if (threadIdx.x < 16) s_prof[threadIdx.x] = 0;
+#define PROF_T(v) long long v = clock64();
+#define PROF_ADD(slot, v) if (threadIdx.x == 0) s_prof[slot] += clock64() - v;
+#define PROF_PTR s_prof
+#define PROF_FLUSH(g) if (threadIdx.x < 16) atomicAdd(&g[threadIdx.x], s_prof[threadIdx.x]);
+#else
+#define PROF_DECL
+#define PROF_INIT
+#define PROF_T(v)
+#define PROF_ADD(slot, v)
+#define PROF_PTR nullptr
+#define PROF_FLUSH(g)
+#endif
+
 template <typename F>
-__device__ __forceinline__ bool mma_sync_run(uint64_t* bar, volatile int* bad, uint32_t& phase, F issue) {
+__device__ __forceinline__ bool mma_sync_run(uint64_t* bar, volatile int* bad, uint32_t& phase, F issue,
+                                             unsigned long long* prof = nullptr) {
+  long long t0 = prof ? clock64() : 0;
   fence_async_smem();
   fence_before();
   __syncthreads();
   if (*bad) return false;
-  if (threadIdx.x == 0) {
+  long long t1 = prof ? clock64() : 0;
+  if (threadIdx.x < 32) {  // warp 0 issues (one elected lane)
     fence_after();
     issue();
     mma_commit(bar);
@@ -138,6 +164,148 @@ __device__ __forceinline__ bool mma_sync_run(uint64_t* bar, volatile int* bad, u
   bool ok = mbar_wait(bar, phase);
   phase ^= 1;
   fence_after();
+  if (prof && threadIdx.x == 0) {
+    prof[0] += t1 - t0;
+    prof[1] += clock64() - t1;
+  }
+  return ok;
+}
+
+}  // namespace tc
+}  // namespace atlas
+
+namespace atlas {
+namespace tc {
+
+// Host: upper bound on resident 2-CTA clusters (one CTA per SM).
+inline int max_clusters_bound() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms / 2;
+}
+
+// One Polar Express problem in flight: its operand tiles, TMEM base column,
+// completion barrier, and (optionally) where to save each step's operand tiles.
+struct PESlot {
+  uint8_t *Xh, *Xl, *Ah, *Al, *Bh, *Bl;
+  uint64_t* bar;
+  uint32_t tm;       // TMEM base of this slot: X~ at +TM_X (+64), Gram at +TM_GRAM, A*A at +TM_A2
+  uint32_t phase;
+  uint8_t* ns;       // global destination of step k's tiles at ns + k * NS_TILE_BYTES, or null
+  int save_last;     // unused (every step is saved when ns is set)
+};
+constexpr size_t NS_TILE_BYTES = 2 * XT_BYTES + 4 * AT_BYTES;
+
+__device__ __forceinline__ void pe_issue(const PESlot& p, int type) {
+  if (type == 0) {         // Gram A = X~^T X~
+    mma3<E>(p.tm + TM_GRAM, p.Xh, p.Xl, true, p.Xh, p.Xl, true, 64, 0, false);
+  } else if (type == 1) {  // A * A
+    mma3<D>(p.tm + TM_A2, p.Ah, p.Al, false, p.Ah, p.Al, true, 64, 0, false);
+  } else {                 // X~ B'^T, two 128-row halves
+    mma3<D>(p.tm + TM_X, p.Xh, p.Xl, false, p.Bh, p.Bl, false, 128, 0, false);
+    mma3<D>(p.tm + TM_X + 64, p.Xh, p.Xl, false, p.Bh, p.Bl, false, 128, 16384, false);
+  }
+}
+
+// Thread 0: copy the tile the epilogue of phase `type` of step `st` just produced
+// to the slot's scratch (step k at ns + k * NS_TILE_BYTES: X hi, X lo, A hi, A lo,
+// B' hi, B' lo).  type 0 -> A_st, 1 -> B'_st, 2 -> X_{st+1}.  Bulk copies are
+// asynchronous; before issuing, all but the most recent earlier copy must have
+// finished reading shared memory -- a tile is rewritten three phases after it was
+// produced, so this never stalls on a copy whose source is still needed.
+__device__ __forceinline__ void pe_save(const PESlot& q, int type, int st) {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  if (type == 2) {
+    uint8_t* o = q.ns + (size_t)(st + 1) * NS_TILE_BYTES;
+    bulk_s2g(o, q.Xh, XT_BYTES);
+    bulk_s2g(o + XT_BYTES, q.Xl, XT_BYTES);
+  } else {
+    uint8_t* o = q.ns + (size_t)st * NS_TILE_BYTES + 2 * XT_BYTES + (type == 0 ? 0 : 2 * AT_BYTES);
+    bulk_s2g(o, type == 0 ? q.Ah : q.Bh, AT_BYTES);
+    bulk_s2g(o + AT_BYTES, type == 0 ? q.Al : q.Bl, AT_BYTES);
+  }
+  bulk_commit();
+}
+
+// Up to two independent Polar Express forwards, interleaved so that one slot's
+// epilogue (TMEM read-out, bf16 split, tile stores) overlaps the other slot's
+// MMAs.  The caller has stored X0 into each slot's X tiles.  On return each
+// slot's final X~ (float32) is in TMEM at tm + TM_X (+64 for rows 128-255).
+// Returns false if a bounded wait expired.
+__device__ __noinline__ static bool pe_forward_multi(PESlot* sl, int nslots, int steps, volatile int* bad,
+                                 unsigned long long* prof = nullptr) {
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
+  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
+  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+  const int P = 3 * steps;
+  bool ok = true;
+  fence_async_smem();
+  fence_before();
+  __syncthreads();
+  if (*bad) return false;
+  if (tid == 0)
+    for (int s = 0; s < nslots; ++s)
+      if (sl[s].ns) pe_save(sl[s], 2, -1);  // X0
+  for (int s = 0; s < nslots; ++s)
+    if (w == 4 * s) {  // slot s is issued by warp 4s (one elected lane)
+      fence_after();
+      pe_issue(sl[s], 0);
+      mma_commit(sl[s].bar);
+    }
+  for (int p = 0; p < P; ++p) {
+    const int type = p % 3, st = p / 3;
+    for (int s = 0; s < nslots; ++s) {
+      PESlot& q = sl[s];
+      long long t0 = prof ? clock64() : 0;
+      if (!*bad && !mbar_wait(q.bar, q.phase)) ok = false;
+      q.phase ^= 1;
+      fence_after();
+      if (prof && tid == 0) prof[1] += clock64() - t0;
+      long long te = prof ? clock64() : 0;
+      if (type == 0) {
+        float av[32];
+        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
+        tmem_wait_ld();
+        if (l < 16) store_split32(q.Ah, q.Al, ra, dc, D, av);
+      } else if (type == 1) {
+        const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
+        float av[32], a2[32];
+        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
+        tmem_ld32(q.tm + lane_off + TM_A2 + dc, a2);
+        tmem_wait_ld();
+        if (l < 16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
+          store_split32(q.Bh, q.Bl, ra, dc, D, a2);  // B'[ra][c]
+        }
+      } else if (st + 1 < steps) {
+        float x0[32], x1[32];
+        tmem_ld32(q.tm + lane_off + TM_X + dc, x0);
+        tmem_ld32(q.tm + lane_off + TM_X + 64 + dc, x1);
+        tmem_wait_ld();
+        store_split32(q.Xh, q.Xl, e0, dc, D, x0);
+        store_split32(q.Xh, q.Xl, e1, dc, D, x1);
+      }
+      if (prof && tid == 0) prof[8] += clock64() - te;
+      if (p + 1 < P) {
+        long long t1 = prof ? clock64() : 0;
+        fence_async_smem();
+        fence_before();
+        __syncthreads();
+        if (prof && tid == 0) prof[0] += clock64() - t1;
+        if (q.ns && tid == 0) pe_save(q, type, st);
+        if (w == 4 * s && !*bad) {
+          long long ti = prof ? clock64() : 0;
+          fence_after();
+          pe_issue(q, (p + 1) % 3);
+          mma_commit(q.bar);
+          if (prof && l == 0) prof[7] += clock64() - ti;
+        }
+      }
+    }
+  }
+  if (tid == 0) bulk_wait0();  // saved tiles globally visible before anyone reads them back
   return ok;
 }
 

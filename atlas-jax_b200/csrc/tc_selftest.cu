@@ -38,7 +38,7 @@ __global__ void selftest_gemm(const float* A, const float* B, float* D, int M, i
   __syncthreads();
   fence_after();
   uint32_t tm = tbase;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {  // one warp issues (elected lane)
     uint32_t id = idesc_bf16(M, N, amn, bmn);
     for (int kb = 0; kb < K / 16; ++kb) {
       // advance two core matrices along K
@@ -79,3 +79,4 @@ extern "C" int atlas_selftest_tc_gemm(const float* A, const float* B, float* D, 
   atlas::selftest_gemm<<<1, 128, smem, (cudaStream_t)stream>>>(A, B, D, M, N, K, a_mn_major, b_mn_major);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
+

@@ -122,7 +122,7 @@ int atlas_scan_bwd(const AtlasScanParams* p,
  * inference runtime that forbids device allocations after start-up).  It has no
  * counterpart in the reference.  Same arguments and semantics as atlas_scan_fwd
  * without `saved` and `workspace`; tensor path only (params->precision must be
- * ATLAS_PREC_TENSOR).  Its scratch is a fixed 4 MiB array inside the library,
+ * ATLAS_PREC_TENSOR).  Its scratch is a fixed 6 MiB array inside the library,
  * enough for B*H <= ATLAS_NOALLOC_MAX_CHAINS; larger problems are rejected with
  * ATLAS_ERR_INVALID_ARGUMENT.  Every GPU that loads the library keeps that array
  * until the process exits.  The first call on a device looks up the array's
