@@ -56,7 +56,8 @@ struct __align__(1024) Smem {
   float pbuf[2][E];                // gelu(W2 q) written by rank 1 into rank 0
   float ybuf[4][D];
   float red[8];
-  uint64_t bar[2];
+  uint64_t bar[2];    // done[s]: MMAs of slot s complete
+  uint64_t ready[2];  // ready[s]: slot s operand tiles published by the 8 epilogue warps
   uint32_t tmem;
   int bad;
 };
@@ -110,7 +111,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
     s.gate[2][r] = g.t;
     s.gate[3][r] = g.g;
   }
-  __syncthreads();
+  epi_sync();
   {  // h = W2 k ; thread e
     const int e = tid;
     float w[D];
@@ -125,7 +126,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
       Fg[r * E + e] = rank ? hv : av;  // rank 1 keeps h for gelu'(h)
     }
   }
-  __syncthreads();
+  epi_sync();
   {  // err = k + W1 act - v ; thread (d, token group)
     const int d = tid % D, grp = tid / D;  // 4 groups
     const int per = (cs + 3) / 4;
@@ -149,7 +150,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
       }
     }
   }
-  __syncthreads();
+  epi_sync();
   if (rank) {  // chain = (W1^T err) * gelu'(h) ; thread e
     const int e = tid;
     float w[D];
@@ -163,7 +164,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
     }
   }
   for (int i = tid; i < cs * D; i += NT) s.G[i] = rank ? kbuf[i] : errb[i];
-  __syncthreads();
+  epi_sync();
 }
 
 size_t bwd_workspace_bytes(const AtlasScanParams& p);
@@ -181,7 +182,7 @@ __device__ unsigned long long g_prof_fwd[16];
 #endif
 
 template <typename TA>
-__global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
+__global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   PROF_DECL
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -203,8 +204,10 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(&s.bar[0], 1);
-    mbar_init(&s.bar[1], 1);
+    mbar_init(&s.bar[0], 1);  // done[0]
+    mbar_init(&s.bar[1], 1);  // done[1]
+    mbar_init(&s.ready[0], 8);
+    mbar_init(&s.ready[1], 8);
     fence_mbar_init();
     s.bad = 0;
   }
@@ -212,10 +215,34 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
   __syncthreads();
   fence_after();
   PESlot sl[2] = {make_slot(s, 0, s.tmem), make_slot(s, 1, s.tmem)};
+  PEBars B;
+  B.ready[0] = &s.ready[0];
+  B.ready[1] = &s.ready[1];
+  B.done[0] = &s.bar[0];
+  B.done[1] = &s.bar[1];
+  B.ready_phase[0] = B.ready_phase[1] = B.done_phase[0] = B.done_phase[1] = 0;
   PROF_INIT
-
-  float Sv[2][32], Wv[2][32];
   const long total = (long)K.nchains * nch;
+  const int npair = P.ns_steps > 0 ? 2 : 1;
+
+  // Register split (launch: 384 threads x 168 = 64512): the two epilogue
+  // warpgroups take 240 each, the producer warpgroup keeps 24:
+  // 2 * 128 * 240 + 128 * 24 = 64512.
+  if (w >= 8) {  // ---- producer warpgroup: warp 8 issues every MMA; all four mirror the cluster barriers ----
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 24;");
+    for (long k = cluster; k < total; k += nclusters) {
+      cluster_sync();
+      cluster_sync();
+      for (int r0 = 0; r0 < cs; r0 += npair) {
+        const int n = min(npair, cs - r0);
+        if (w == 8 && P.ns_steps > 0) pe_produce(sl, B, n, P.ns_steps, &s.bad);
+        for (int j = 0; j < n; ++j) cluster_sync();
+      }
+      cluster_sync();
+    }
+  } else {  // ---- 8 epilogue warps ----
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
+  float Sv[2][32], Wv[2][32];
   for (long k = cluster; k < total; k += nclusters) {
     const int q = (int)(k % K.nchains), c = (int)(k / K.nchains);
     const int b = q / H, hh = q % H;
@@ -231,7 +258,7 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
         }
       }
     }
-    __syncthreads();
+    epi_sync();
     float* slot = carry_slot(a, K.carries, q, c, nch);
     float* mine = slot + 2 * rank * DE;  // [W, S] of this CTA's matrix
     if (c == 0) {  // initial carry: caller's state or the LM init (model.py:251-264)
@@ -264,7 +291,6 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
     }
     cluster_sync();  // both CTAs are done reading the carry slot
 
-    const int npair = P.ns_steps > 0 ? 2 : 1;
     for (int r0 = 0; r0 < cs; r0 += npair) {
       PROF_T(tpair)
       const int n = min(npair, cs - r0);
@@ -303,7 +329,7 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
         float ss = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
-        ss = block_sum(ss, s.red);
+        ss = block_sum_epi(ss, s.red);
         const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
         inv0 = inv;
         if (P.ns_steps > 0) {
@@ -318,7 +344,7 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
         PROF_ADD(3, tnorm)
       }
       // ---- Polar Express (memory_layer.py:43-71) for the pair, interleaved ----
-      if (P.ns_steps > 0 && !pe_forward_multi(sl, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
+      if (P.ns_steps > 0 && !pe_consume(sl, B, n, P.ns_steps, &s.bad) && !s.bad) {
         set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
         s.bad = 1;
       }
@@ -345,7 +371,7 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
         }
         // ---- read-out y = q + W1 gelu(W2 q)  (memory_layer.py:592-595) ----
         if (tid < D) s.qv[tid] = t < T ? ld_act((const TA*)a.q, (((size_t)b * T + t) * H + hh) * D + tid) : 0.f;
-        __syncthreads();
+        epi_sync();
         if (rank == 1) {
           float z0 = 0.f, z1 = 0.f;
 #pragma unroll
@@ -355,7 +381,7 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
           }
           s.zbuf[ch][e0] = z0;
           s.zbuf[ch][e1] = z1;
-          __syncthreads();
+          epi_sync();
           const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
           st_remote_f32(&s.pbuf[r & 1][tid], 0, gelu_tanh(z));
           cluster_sync();
@@ -367,13 +393,13 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
           for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(Wv[0][jj], p0, Wv[1][jj] * p1);
           float part = warp_reduce_scatter32(yv);
           s.ybuf[qd][dc + l] = part;
-          __syncthreads();
+          epi_sync();
           if (tid < D && t < T) {
             float y = s.qv[tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
             st_act((TA*)a.y, (((size_t)b * T + t) * H + hh) * D + tid, y);
           }
         }
-        __syncthreads();
+        epi_sync();
         PROF_ADD(6, tro)
       }
       PROF_ADD(4, tpair)
@@ -408,6 +434,7 @@ __global__ void __launch_bounds__(NT, 1) fwd_kernel(KArgs K) {
     cluster_sync();
     if (rank == 0 && tid == 0) st_release(&K.flags[q], c + 1);
   }
+  }  // epilogue warps
   fence_before();
   __syncthreads();
   if (w == 0) tmem_dealloc(s.tmem, TMEM_COLS);
@@ -450,7 +477,7 @@ static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) 
   cudaError_t e = cudaFuncSetAttribute(fwd_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(NT);
+  cfg.blockDim = dim3(NT + 128);  // 8 epilogue warps + a producer warpgroup (1 MMA warp, 3 idle)
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -85,6 +85,19 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
+// Same, over the 8 epilogue warps only (kernels with a dedicated MMA warp).
+__device__ __forceinline__ float block_sum_epi(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+  float s = 0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  return s;
+}
+
 // Reduce-scatter of 32 per-lane values over a warp: afterwards lane l holds the
 // warp-wide sum of element l in v[0].
 __device__ __forceinline__ float warp_reduce_scatter32(float* v) {
@@ -287,7 +300,7 @@ __device__ __noinline__ static bool pe_forward_multi(PESlot* sl, int nslots, int
         store_split32(q.Xh, q.Xl, e0, dc, D, x0);
         store_split32(q.Xh, q.Xl, e1, dc, D, x1);
       }
-      if (prof && tid == 0) prof[8] += clock64() - te;
+      if (prof && tid == 0) prof[12] += clock64() - te;
       if (p + 1 < P) {
         long long t1 = prof ? clock64() : 0;
         fence_async_smem();
@@ -300,12 +313,127 @@ __device__ __noinline__ static bool pe_forward_multi(PESlot* sl, int nslots, int
           fence_after();
           pe_issue(q, (p + 1) % 3);
           mma_commit(q.bar);
-          if (prof && l == 0) prof[7] += clock64() - ti;
+          if (prof && l == 0) prof[11] += clock64() - ti;
         }
       }
     }
   }
   if (tid == 0) bulk_wait0();  // saved tiles globally visible before anyone reads them back
+  return ok;
+}
+
+}  // namespace tc
+}  // namespace atlas
+
+namespace atlas {
+namespace tc {
+
+// ---------------------------------------------------------------------------
+// Producer / consumer form of the interleaved Polar Express (dedicated MMA warp).
+// The 8 epilogue warps (consumers) and one MMA warp (producer) hand off through
+// per-slot mbarriers: ready[s] (8 arrivals: one per epilogue warp after its tile
+// stores) and done[s] (tcgen05.commit).  No CTA-wide barrier inside the loop.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// named barrier over the 8 epilogue warps only
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+struct PEBars {
+  uint64_t* ready[2];
+  uint64_t* done[2];
+  uint32_t ready_phase[2];  // used by the producer
+  uint32_t done_phase[2];   // used by the consumers
+};
+
+// Epilogue warp: publish this warp's tile stores of slot s to the producer.
+__device__ __forceinline__ void pe_publish(PEBars& B, int s) {
+  fence_async_smem();
+  fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(B.ready[s]);
+}
+
+// Consumers (threads 0..255).  X0 of every slot is already stored by these threads.
+// On return each slot's final X~ is in TMEM (tm + TM_X, + 64).
+static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad) {
+  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
+  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
+  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
+  const int P = 3 * steps;
+  bool ok = true;
+  for (int s = 0; s < nslots; ++s) pe_publish(B, s);
+  for (int p = 0; p < P; ++p) {
+    const int type = p % 3, st = p / 3;
+    for (int s = 0; s < nslots; ++s) {
+      PESlot& q = sl[s];
+      if (!*bad && !mbar_wait(B.done[s], B.done_phase[s])) ok = false;
+      B.done_phase[s] ^= 1;
+      fence_after();
+      if (type == 0) {
+        float av[32];
+        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
+        tmem_wait_ld();
+        if (l < 16) store_split32(q.Ah, q.Al, ra, dc, D, av);
+      } else if (type == 1) {
+        const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
+        float av[32], a2[32];
+        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
+        tmem_ld32(q.tm + lane_off + TM_A2 + dc, a2);
+        tmem_wait_ld();
+        if (l < 16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
+          store_split32(q.Bh, q.Bl, ra, dc, D, a2);  // B'[ra][c]
+        }
+      } else if (st + 1 < steps) {
+        float x0[32], x1[32];
+        tmem_ld32(q.tm + lane_off + TM_X + dc, x0);
+        tmem_ld32(q.tm + lane_off + TM_X + 64 + dc, x1);
+        tmem_wait_ld();
+        store_split32(q.Xh, q.Xl, e0, dc, D, x0);
+        store_split32(q.Xh, q.Xl, e1, dc, D, x1);
+      }
+      if (p + 1 < P) pe_publish(B, s);
+    }
+  }
+  return ok;
+}
+
+// Producer (one whole warp).  Mirrors pe_consume's schedule; saves the freshly
+// published tiles (when q.ns is set) before issuing the next MMAs.
+static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad) {
+  const int P = 3 * steps;
+  const bool lead = (threadIdx.x & 31) == 0;
+  bool ok = true;
+  for (int p = 0; p < P; ++p) {
+    const int type = p % 3, st = p / 3;
+    for (int s = 0; s < nslots; ++s) {
+      PESlot& q = sl[s];
+      if (!*bad && !mbar_wait(B.ready[s], B.ready_phase[s])) ok = false;
+      B.ready_phase[s] ^= 1;
+      fence_after();
+      if (q.ns && lead) {  // tile published for this phase: X_st (type 0), A_st (1), B'_st (2)
+        if (type == 0) {
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          uint8_t* o = q.ns + (size_t)st * NS_TILE_BYTES;
+          bulk_s2g(o, q.Xh, XT_BYTES);
+          bulk_s2g(o + XT_BYTES, q.Xl, XT_BYTES);
+          bulk_commit();
+        } else {
+          pe_save(q, type - 1, st);
+        }
+      }
+      __syncwarp();
+      if (!*bad) {
+        pe_issue(q, type);
+        mma_commit(B.done[s]);
+      }
+    }
+  }
+  if (lead) bulk_wait0();
+  __syncwarp();
   return ok;
 }
 
