@@ -99,7 +99,9 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
   float* actb = (float*)s.slot[0];                     // cs x E  (64 KB)
   float* kbuf = (float*)s.slot[1];                     // cs x D  (16 KB)
   float* errb = (float*)(s.slot[1] + MAXCS * D * 4);   // cs x D  (16 KB)
+  float* W1s = (float*)(s.slot[1] + 2 * MAXCS * D * 4); // W1^T staged (64 KB)
   const int tid = threadIdx.x;
+  for (int i = tid; i < DE / 4; i += NT) ((float4*)W1s)[i] = ((const float4*)W1t)[i];
   for (int i = tid; i < cs * D; i += NT) {
     int r = i / D, d = i % D, t = c * cs + r;
     kbuf[i] = t < T ? ld_act(kp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
@@ -134,7 +136,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
 #pragma unroll
     for (int j = 0; j < MAXCS / 4; ++j) acc[j] = 0.f;
     for (int e = 0; e < E; ++e) {
-      float w = W1t[e * D + d];
+      float w = W1s[e * D + d];
 #pragma unroll
       for (int j = 0; j < MAXCS / 4; ++j) {
         int r = grp * per + j;
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
         PROF_ADD(3, tnorm)
       }
       // ---- Polar Express (memory_layer.py:43-71) for the pair, interleaved ----
-      if (P.ns_steps > 0 && !pe_consume(sl, B, n, P.ns_steps, &s.bad) && !s.bad) {
+      if (P.ns_steps > 0 && !pe_consume(sl, B, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
         set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
         s.bad = 1;
       }

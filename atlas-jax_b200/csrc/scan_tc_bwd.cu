@@ -65,6 +65,7 @@ struct __align__(1024) Smem {
   uint64_t bar;
   uint64_t bar2;         // completion barrier of the second in-flight Polar Express
   uint64_t bar_ld;       // bulk loads of saved Newton-Schulz tiles
+  uint64_t ready[2];     // operand tiles of slot s published by the 8 epilogue warps
   uint32_t tmem;
   int bad;
 };
@@ -164,7 +165,7 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
       kb[i] = kv;
       w.k[i] = kv;
     }
-    __syncthreads();
+    epi_sync();
     {
       const int e = tid;
       float wr[D];
@@ -175,11 +176,15 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
 #pragma unroll
         for (int d = 0; d < D; ++d) hv = fmaf(wr[d], kb[r * D + d], hv);
         w.h[r * E + e] = hv;
-        w.act[r * E + e] = gelu_tanh(hv);
+        const float av = gelu_tanh(hv);
+        w.act[r * E + e] = av;
+        ((float*)s.Gh)[r * E + e] = av;  // smem copy for the err pass (G~ tiles' 64 KB are free here)
       }
     }
+    float* W1s = (float*)s.Xh;  // W1^T staged in the X~ tiles' 64 KB (free in this phase)
+    for (int i = tid; i < DE / 4; i += NT) ((float4*)W1s)[i] = ((const float4*)W1t)[i];
     __threadfence_block();
-    __syncthreads();
+    epi_sync();
     {
       const TA* vp = (const TA*)a.v;
       const int d = tid % D, grp = tid / D;
@@ -188,11 +193,11 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
 #pragma unroll
       for (int j = 0; j < MAXCS / 4; ++j) acc[j] = 0.f;
       for (int e = 0; e < E; ++e) {
-        float wv = W1t[e * D + d];
+        float wv = W1s[e * D + d];
 #pragma unroll
         for (int j = 0; j < MAXCS / 4; ++j) {
           int r = grp * per + j;
-          if (j < per && r < cs) acc[j] = fmaf(wv, w.act[r * E + e], acc[j]);
+          if (j < per && r < cs) acc[j] = fmaf(wv, ((const float*)s.Gh)[r * E + e], acc[j]);
         }
       }
 #pragma unroll
@@ -232,12 +237,46 @@ namespace atlas {
 namespace tc {
 namespace bwd {
 
+
+// One MMA group issued by epilogue warp 0 itself (single problem in flight, so a
+// hand-off to the producer warp would only add latency): publish the operand
+// tiles to the tensor core, issue, wait.  g: 0 = P = G~^T X~, 1 = Ps A + A Ps,
+// 2 = (G~ B' issued with group 0) + X~ Sym.
+__device__ __forceinline__ bool vjp_mma(Smem& s, PEBars& B, uint32_t tm, int g, volatile int* bad) {
+  fence_async_smem();
+  fence_before();
+  epi_sync();
+  if (*bad) return false;
+  if (threadIdx.x < 32) {
+    fence_after();
+    if (g == 0) {
+      mma3<E>(tm + TM_GRAM, s.Gh, s.Gl, true, s.Xh, s.Xl, true, 64, 0, false);
+      mma_commit(B.done[0]);
+      // G~ B' does not depend on Sym: start it now so it overlaps the P epilogue
+      // (later commits cover it; MMAs into one accumulator execute in order)
+      for (int h2 = 0; h2 < 2; ++h2)
+        mma3<D>(tm + TM_X + 64 * h2, s.Gh, s.Gl, false, s.Bh, s.Bl, true, 128, 16384 * h2, false);
+    } else if (g == 1) {
+      mma3<D>(tm + TM_A2, s.Ph, s.Pl, false, s.Ah, s.Al, true, 64, 0, false);
+      mma3<D>(tm + TM_A2, s.Ah, s.Al, false, s.Ph, s.Pl, true, 64, 0, true);
+    } else {
+      for (int h2 = 0; h2 < 2; ++h2)
+        mma3<D>(tm + TM_X + 64 * h2, s.Xh, s.Xl, false, s.Yh, s.Yl, true, 128, 16384 * h2, true);
+    }
+    if (g != 0) mma_commit(B.done[0]);
+  }
+  const bool ok = mbar_wait(B.done[0], B.done_phase[0]);
+  B.done_phase[0] ^= 1;
+  fence_after();
+  return ok;
+}
+
 #ifdef ATLAS_PHASE_PROF
 __device__ unsigned long long g_prof_bwd[16];
 #endif
 
 template <typename TA>
-__global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
+__global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   PROF_DECL
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -267,6 +306,8 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
     mbar_init(&s.bar, 1);
     mbar_init(&s.bar_ld, 1);
     mbar_init(&s.bar2, 1);
+    mbar_init(&s.ready[0], 8);
+    mbar_init(&s.ready[1], 8);
     fence_mbar_init();
     s.bad = 0;
   }
@@ -279,8 +320,37 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
   PESlot sl[2];
   sl[0] = PESlot{s.Xh, s.Xl, s.Ah, s.Al, s.Bh, s.Bl, &s.bar, tm, 0, nullptr, 0};
   sl[1] = PESlot{s.Gh, s.Gl, s.Ph, s.Pl, s.Yh, s.Yl, &s.bar2, tm + 256, 0, nullptr, 0};
+  PEBars B;
+  B.ready[0] = &s.ready[0];
+  B.ready[1] = &s.ready[1];
+  B.done[0] = &s.bar;
+  B.done[1] = &s.bar2;
+  B.ready_phase[0] = B.ready_phase[1] = B.done_phase[0] = B.done_phase[1] = 0;
 
   const long total = (long)K.nchains * nch;
+  const int npair = P.ns_steps > 0 ? 2 : 1;
+  // Register split (launch: 384 threads x 168 = 64512): the two epilogue
+  // warpgroups take 240 each, the producer warpgroup keeps 24:
+  // 2 * 128 * 240 + 128 * 24 = 64512.
+  if (wp >= 8) {  // ---- producer warpgroup: warp 8 issues every MMA; all four mirror the cluster barriers ----
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 24;");
+    for (long kk = cluster; kk < total; kk += nclusters) {
+      cluster_sync();  // frozen pass (rank 0 done)
+      cluster_sync();  // frozen pass (rank 1 done)
+      for (int r0 = 0; r0 < cs; r0 += npair) {
+        const int n = min(npair, cs - r0);
+        if (wp == 8 && P.ns_steps > 0) {
+          sl[0].ns = P.pe_ste ? nullptr : w.ns[rank] + (size_t)r0 * 5 * NS_STEP_BYTES;
+          sl[1].ns = P.pe_ste ? nullptr : sl[0].ns + 5 * NS_STEP_BYTES;
+          pe_produce(sl, B, n, P.ns_steps, &s.bad);
+        }
+        for (int jp = 0; jp < n; ++jp) cluster_sync();  // read-out exchange
+      }
+      cluster_sync();  // phase D start
+      cluster_sync();  // item end
+    }
+  } else {  // ---- 8 epilogue warps ----
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
   for (long kk = cluster; kk < total; kk += nclusters) {
     const int q = (int)(kk % K.nchains), j = (int)(kk / K.nchains), c = nch - 1 - j;
     const int b = q / H, hh = q % H;
@@ -295,7 +365,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         }
       }
     }
-    __syncthreads();
+    epi_sync();
     const float* slot = (const float*)a.saved + ((size_t)q * nch + c) * 4 * DE;
     const float* mine = slot + 2 * rank * DE;
     // zero the accumulators of this cluster (rank 0: dF, rank 1: dG and scalars)
@@ -313,7 +383,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
       s.gate[2][r] = gg.t;
       s.gate[3][r] = gg.g;
     }
-    __syncthreads();
+    epi_sync();
     PROF_ADD(2, tA)
     PROF_T(tB)
 
@@ -327,7 +397,6 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
     ld32(mine + DE + e1 * D + dc, Sv[1]);
     st32(Ssave + e0 * D + dc, Sv[0]);
     st32(Ssave + e1 * D + dc, Sv[1]);
-    const int npair = P.ns_steps > 0 ? 2 : 1;
     for (int r0 = 0; r0 < cs; r0 += npair) {
       const int n = min(npair, cs - r0);
       float inv0 = 0.f;
@@ -356,7 +425,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         float ss = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
-        ss = block_sum(ss, s.red);
+        ss = block_sum_epi(ss, s.red);
         const float nrm_r = sqrtf(ss + 1e-12f);
         const float inv = 1.0f / (nrm_r * 1.01f + 1e-6f);
         if (tid == 0) s.nrm[r] = nrm_r;
@@ -376,7 +445,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         sl[0].ns = w.ns[rank] + (size_t)r0 * 5 * NS_STEP_BYTES;
         sl[1].ns = sl[0].ns + 5 * NS_STEP_BYTES;
         if (P.pe_ste) sl[0].ns = sl[1].ns = nullptr;
-        if (!pe_forward_multi(sl, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
+        if (!pe_consume(sl, B, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
           set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
           s.bad = 1;
         }
@@ -409,7 +478,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
           s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
         }
-        __syncthreads();
+        epi_sync();
         {
           const float* xv = rank ? s.qv : s.dyv;  // rank 1: z = W2 q ; rank 0: dp = W1^T dy
           float z0 = 0.f, z1 = 0.f;
@@ -420,7 +489,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           }
           s.zbuf[ch][e0] = z0;
           s.zbuf[ch][e1] = z1;
-          __syncthreads();
+          epi_sync();
           const float z = s.zbuf[0][tid] + s.zbuf[1][tid];
           // rank 1 sends p = gelu(z) to rank 0; rank 0 sends dp to rank 1
           st_remote_f32(&s.xbuf[r & 1][tid], rank ^ 1u, rank ? gelu_tanh(z) : z);
@@ -431,21 +500,21 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
             const float dz = s.xbuf[r & 1][tid] * gelu_tanh_grad(z);
             vec[r * E + tid] = dz;
             s.zbuf[0][tid] = dz;
-            __syncthreads();
+            epi_sync();
             const float dz0 = s.zbuf[0][e0], dz1 = s.zbuf[0][e1];
             float yv[32];
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(Wv[0][jj], dz0, Wv[1][jj] * dz1);
             float part = warp_reduce_scatter32(yv);
             s.ybuf[qd][dc + l] = part;
-            __syncthreads();
+            epi_sync();
             if (tid < D && t < T) {
               const float dq = s.dyv[tid] + s.ybuf[0][tid] + s.ybuf[1][tid] + s.ybuf[2][tid] + s.ybuf[3][tid];
               st_act((TA*)a.dq, (((size_t)b * T + t) * H + hh) * D + tid, dq);
             }
           }
         }
-        __syncthreads();
+        epi_sync();
       }
     }
 
@@ -486,7 +555,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
       }
       if (tid < MAXCS) s.ipacc[tid] = 0.f;
-      __syncthreads();
+      epi_sync();
       {  // read-out: rank 0 dW1 += dy p^T (tile: p[e] dy[d]); rank 1 dW2 += dz q^T
         const float v0 = vec[r * E + e0], v1 = vec[r * E + e1];
         const float* xv = rank ? s.qv : s.dyv;
@@ -495,6 +564,14 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           dW[0][jj] = fmaf(v0, xv[dc + jj], dW[0][jj]);
           dW[1][jj] = fmaf(v1, xv[dc + jj], dW[1][jj]);
         }
+      }
+      if (r > 0) {  // pull the next token's saved rows into L2 while this token's VJP runs
+        const float* nw = Wsave + (size_t)(r - 1) * DE;
+        const float* ns_ = Ssave + (size_t)(r - 1) * DE;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e0 * D + dc));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e1 * D + dc));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(ns_ + e0 * D + dc));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(ns_ + e1 * D + dc));
       }
       float dal = 0.f;
       {
@@ -526,7 +603,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           bool ok = true;
           uint8_t* nscur = w.ns[rank] + (size_t)r * 5 * NS_STEP_BYTES;
           if (!s.bad) {  // last step's tiles of token r (saved in phase B)
-            __syncthreads();
+            epi_sync();
             if (tid == 0) {
               const uint8_t* o = nscur + (size_t)(P.ns_steps - 1) * NS_STEP_BYTES;
               mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
@@ -554,7 +631,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
             PROF_T(tcp)
             PROF_ADD(9, tcp)
             // P = G~^T X~
-            ok = mma_sync_run(&s.bar, &s.bad, sl[0].phase, [&] { mma3<E>(tm + TM_GRAM, s.Gh, s.Gl, true, s.Xh, s.Xl, true, 64, 0, false); }, PROF_PTR) && ok;
+            ok = vjp_mma(s, B, tm, 0, &s.bad) && ok;  // P = G~^T X~
             float pv[32];
             tmem_ld32(tm + lane_off + TM_GRAM + dc, pv);
             tmem_wait_ld();
@@ -564,17 +641,14 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
               for (int m = 0; m < 8; ++m)
                 *(float4*)&Pf[pf_idx(ra, dc + 4 * m)] = make_float4(pv[4 * m], pv[4 * m + 1], pv[4 * m + 2], pv[4 * m + 3]);
             }
-            __syncthreads();
+            epi_sync();
             if (l < 16) {
 #pragma unroll
               for (int jj = 0; jj < 32; ++jj) pv[jj] += Pf[pf_idx(dc + jj, ra)];  // Ps = P + P^T
               store_split32(s.Ph, s.Pl, ra, dc, D, pv);
             }
             // Sym = b Ps + c (Ps A + A Ps)
-            ok = mma_sync_run(&s.bar, &s.bad, sl[0].phase, [&] {
-                   mma3<D>(tm + TM_A2, s.Ph, s.Pl, false, s.Ah, s.Al, true, 64, 0, false);
-                   mma3<D>(tm + TM_A2, s.Ah, s.Al, false, s.Ph, s.Pl, true, 64, 0, true);
-                 }, PROF_PTR) && ok;
+            ok = vjp_mma(s, B, tm, 1, &s.bad) && ok;  // Ps A + A Ps
             float yv[32];
             tmem_ld32(tm + lane_off + TM_A2 + dc, yv);
             tmem_wait_ld();
@@ -584,12 +658,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
               store_split32(s.Yh, s.Yl, ra, dc, D, yv);
             }
             // dX~ = G~ B' + X~ Sym
-            ok = mma_sync_run(&s.bar, &s.bad, sl[0].phase, [&] {
-                   for (int h2 = 0; h2 < 2; ++h2) {
-                     mma3<D>(tm + TM_X + 64 * h2, s.Gh, s.Gl, false, s.Bh, s.Bl, true, 128, 16384 * h2, false);
-                     mma3<D>(tm + TM_X + 64 * h2, s.Xh, s.Xl, false, s.Yh, s.Yl, true, 128, 16384 * h2, true);
-                   }
-                 }, PROF_PTR) && ok;
+            ok = vjp_mma(s, B, tm, 2, &s.bad) && ok;  // G~ B' + X~ Sym
             if (st > 0 && tid == 0 && !s.bad) {  // prefetch step st-1's tiles; X, A, B' are free now
               const uint8_t* o = nscur + (size_t)(st - 1) * NS_STEP_BYTES;
               mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
@@ -626,7 +695,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
         float dot = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dot = fmaf(gx[0][jj], xo[0][jj], fmaf(gx[1][jj], xo[1][jj], dot));
-        dot = block_sum(dot, s.red);
+        dot = block_sum_epi(dot, s.red);
         const float coef = dot / (kap * kap) * 1.01f / nrm;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -647,31 +716,43 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
       }
       PROF_T(twin)
       const int i0 = win ? max(0, r - P.omega + 1) : r;
-      for (int i = i0; i <= r; ++i) {
-        const float gi = win ? s.gate[3][i] : 1.f;
-        const float cf = -g.e * sc * gi;
-        const float f0 = Fm[i * E + e0], f1 = Fm[i * E + e1];
-        float gv[32], cv[32];
-        ld32(&s.Gc[i * D + dc], gv);
-        float rv0 = 0.f, rv1 = 0.f;
+      for (int ib = i0; ib <= r; ib += 8) {
+        float fa[8], fb[8];  // this block's row factors, loaded together (one L2 round trip)
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          rv0 = fmaf(dS[0][jj], gv[jj], rv0);
-          rv1 = fmaf(dS[1][jj], gv[jj], rv1);
-          cv[jj] = fmaf(dS[0][jj], f0, dS[1][jj] * f1);
+        for (int k8 = 0; k8 < 8; ++k8) {
+          const int i = ib + k8;
+          fa[k8] = i <= r ? Fm[i * E + e0] : 0.f;
+          fb[k8] = i <= r ? Fm[i * E + e1] : 0.f;
         }
-        float ip = fmaf(f0, rv0, f1 * rv1);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ip += __shfl_xor_sync(0xffffffffu, ip, o);
-        if (l == 0) atomicAdd(&s.ipacc[i], ip);
-        red_add(&w.dF[rank][i * E + e0], cf * rv0);
-        red_add(&w.dF[rank][i * E + e1], cf * rv1);
-        const float part = warp_reduce_scatter32(cv);
-        red_add(&w.dG[rank][i * D + dc + l], cf * part);
+        for (int k8 = 0; k8 < 8; ++k8) {
+          const int i = ib + k8;
+          if (i > r) break;
+          const float gi = win ? s.gate[3][i] : 1.f;
+          const float cf = -g.e * sc * gi;
+          const float f0 = fa[k8], f1 = fb[k8];
+          float gv[32], cv[32];
+          ld32(&s.Gc[i * D + dc], gv);
+          float rv0 = 0.f, rv1 = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            rv0 = fmaf(dS[0][jj], gv[jj], rv0);
+            rv1 = fmaf(dS[1][jj], gv[jj], rv1);
+            cv[jj] = fmaf(dS[0][jj], f0, dS[1][jj] * f1);
+          }
+          float ip = fmaf(f0, rv0, f1 * rv1);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ip += __shfl_xor_sync(0xffffffffu, ip, o);
+          if (l == 0) atomicAdd(&s.ipacc[i], ip);
+          red_add(&w.dF[rank][i * E + e0], cf * rv0);
+          red_add(&w.dF[rank][i * E + e1], cf * rv1);
+          const float part = warp_reduce_scatter32(cv);
+          red_add(&w.dG[rank][i * D + dc + l], cf * part);
+        }
       }
       PROF_ADD(7, twin)
-      dal = block_sum(dal, s.red);
-      dth = block_sum(dth, s.red);  // also orders the ipacc atomics before the reads below
+      dal = block_sum_epi(dal, s.red);
+      dth = block_sum_epi(dth, s.red);  // also orders the ipacc atomics before the reads below
       if (tid >= i0 && tid <= r) {
         const float ip = s.ipacc[tid];
         const float gi = win ? s.gate[3][tid] : 1.f;
@@ -697,11 +778,14 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
     __threadfence();
     cluster_sync();  // both ranks' window accumulations are complete
     {
-      const float* W1t = slot;
-      const float* W2 = slot + 2 * DE;
+      // W1^T, then W2, staged in the 64 KB of A/B'/Ps/Sym tiles (free in this phase)
+      float* Wst = (float*)s.Ah;
+      for (int i = tid; i < DE / 4; i += NT) ((float4*)Wst)[i] = ((const float4*)slot)[i];
+      const float* W1t = Wst;
+      const float* W2 = Wst;
       float* dw1t = (float*)s.Xh;  // cs x E
       float* dhb = (float*)s.Gh;   // cs x E
-      float* derr = pf_base(s);    // cs x D
+      float* derr = s.Gc;          // cs x D
       {  // thread e: d(W1^T err) = dchain * gelu'(h); dh = dchain * r * gelu''(h)
         const int e = tid;
         for (int i = 0; i < cs; ++i) {
@@ -710,7 +794,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           dhb[i * E + e] = dcv * w.r[i * E + e] * gelu_erf_second(hv);
         }
       }
-      __syncthreads();
+      epi_sync();
       const int d = tid % D, grp = tid / D, per = (cs + 3) / 4;
       {  // derr = derr_window + W1 d(W1^T err)
         float acc[MAXCS / 4];
@@ -730,7 +814,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           if (jj < per && i < cs) derr[i * D + d] = w.dG[0][i * D + d] + acc[jj];
         }
       }
-      __syncthreads();
+      epi_sync();
       {  // thread e: dact = dact_window + W1^T derr ; dh += dact * gelu_tanh'(h)
         const int e = tid;
         float wr[D];
@@ -743,7 +827,9 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
           dhb[i * E + e] += da * gelu_tanh_grad(w.h[i * E + e]);
         }
       }
-      __syncthreads();
+      epi_sync();
+      for (int i = tid; i < DE / 4; i += NT) ((float4*)Wst)[i] = ((const float4*)(slot + 2 * DE))[i];
+      epi_sync();
       if (rank == 0) {  // dk = dk_window + derr + W2^T dh ; dv = -derr
         float acc[MAXCS / 4];
 #pragma unroll
@@ -828,6 +914,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(KArgs K) {
     cluster_sync();
     if (rank == 0 && tid == 0) st_release(&K.flags[q], j + 1);
   }
+  }  // epilogue warps
   fence_before();
   __syncthreads();
   if (wp == 0) tmem_dealloc(tm, TMEM_COLS);
@@ -855,7 +942,7 @@ static cudaError_t launch_bwd_t(const bwd::KArgs& k, int nclusters, cudaStream_t
       cudaFuncSetAttribute(bwd::bwd_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(NT);
+  cfg.blockDim = dim3(NT + 128);  // 8 epilogue warps + a producer warpgroup (1 MMA warp, 3 idle)
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -357,7 +357,8 @@ __device__ __forceinline__ void pe_publish(PEBars& B, int s) {
 
 // Consumers (threads 0..255).  X0 of every slot is already stored by these threads.
 // On return each slot's final X~ is in TMEM (tm + TM_X, + 64).
-static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad) {
+static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad,
+                                                  unsigned long long* prof = nullptr) {
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
   const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
   const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
@@ -368,9 +369,12 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
     const int type = p % 3, st = p / 3;
     for (int s = 0; s < nslots; ++s) {
       PESlot& q = sl[s];
+      long long tw = prof ? clock64() : 0;
       if (!*bad && !mbar_wait(B.done[s], B.done_phase[s])) ok = false;
       B.done_phase[s] ^= 1;
       fence_after();
+      long long te = prof ? clock64() : 0;
+      if (prof && threadIdx.x == 0) prof[11] += te - tw;
       if (type == 0) {
         float av[32];
         tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
@@ -396,6 +400,7 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
         store_split32(q.Xh, q.Xl, e1, dc, D, x1);
       }
       if (p + 1 < P) pe_publish(B, s);
+      if (prof && threadIdx.x == 0) prof[12] += clock64() - te;
     }
   }
   return ok;
