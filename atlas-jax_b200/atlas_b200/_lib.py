@@ -65,6 +65,8 @@ def load():
     lib.atlas_polar_express_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                                         ctypes.c_int32, ctypes.c_int32]
     lib.atlas_scan_status.restype = ctypes.c_int
+    lib.atlas_debug_set_wait_hooks.restype = ctypes.c_int
+    lib.atlas_debug_set_wait_hooks.argtypes = [ctypes.c_int32, ctypes.c_int32]
     lib.atlas_scan_fwd_noalloc.restype = ctypes.c_int
     lib.atlas_scan_fwd_noalloc.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 4 + [_P] + [_F] * 4 + [_P]
     if lib.atlas_abi_version() != ATLAS_ABI_VERSION:
@@ -78,7 +80,7 @@ def check(code):
         raise AtlasError(code, load().atlas_last_error_string().decode())
 
 
-def header_functions():
-    """Names of the functions include/atlas_scan.h declares."""
-    txt = open(HEADER).read()
+def header_functions(header=HEADER):
+    """Names of the functions a header in include/ declares."""
+    txt = open(header).read()
     return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(atlas_\w+)\s*\(", txt, re.M)))

@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "scan_internal.h"
+#include "atlas_selftest.h"
 
 namespace atlas {
 __device__ int g_status = 0;
@@ -15,6 +16,12 @@ int* device_status_ptr() {
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
   return (int*)p;
+}
+static WaitHooks g_hooks = {0, 50000000};
+WaitHooks wait_hooks() { return g_hooks; }
+void set_wait_hooks(int bias, int limit) {
+  g_hooks.flag_bias = bias;
+  g_hooks.spin_limit = limit > 0 ? limit : 50000000;
 }
 }  // namespace atlas
 
@@ -156,6 +163,11 @@ int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t
   return cuda_result(atlas::exact::launch_pe(X, Y, batch, rows, cols, ns_steps, eps_in_sqrt, workspace,
                                              (cudaStream_t)stream),
                      "atlas_polar_express_batched launch");
+}
+
+int atlas_debug_set_wait_hooks(int32_t flag_bias, int32_t spin_limit) {
+  atlas::set_wait_hooks(flag_bias, spin_limit);
+  return ATLAS_OK;
 }
 
 int atlas_scan_status(void) {

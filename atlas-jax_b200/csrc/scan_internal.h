@@ -47,6 +47,14 @@ size_t pe_workspace_bytes(int64_t batch, int rows, int cols, int steps);
 }  // namespace exact
 
 int* device_status_ptr();
+// Test hooks for the bounded inter-cluster waits (set through
+// atlas_debug_set_wait_hooks): the ordering-flag threshold is raised by
+// flag_bias (0 in normal use) and the wait gives up after spin_limit polls.
+struct WaitHooks {
+  int flag_bias;
+  int spin_limit;
+};
+WaitHooks wait_hooks();
 int report_error(int code, const char* msg);  // sets atlas_last_error_string(), returns code  // address of the status word on the current device
 
 namespace tc {

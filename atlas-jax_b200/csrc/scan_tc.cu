@@ -176,6 +176,7 @@ struct KArgs {
   int nchains, nch;
   float* carries;  // used when a.saved == nullptr: one slot per chain
   int* flags;      // chunks completed per chain (zeroed before launch)
+  WaitHooks hooks;
   float* fscr;     // per cluster, per rank: the chunk's row factors (MAXCS x E)
 };
 
@@ -251,9 +252,9 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
     // ---- wait for the previous chunk of this chain ----
     if (c > 0 && tid == 0 && !s.bad) {
       int spins = 0;
-      while (ld_acquire(&K.flags[q]) < c) {
+      while (ld_acquire(&K.flags[q]) < c + K.hooks.flag_bias) {
         __nanosleep(200);
-        if (++spins > 50000000) {
+        if (++spins > K.hooks.spin_limit) {
           set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
           s.bad = 1;
           break;
@@ -504,6 +505,7 @@ cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
   k.a = a;
   k.nchains = a.p.B * a.p.H;
   k.nch = n_chunks(a.p);
+  k.hooks = wait_hooks();
   uint8_t* ws = (uint8_t*)a.ws;
   k.flags = (int*)ws;
   k.carries = (float*)(ws + flags_bytes(a.p));

@@ -114,6 +114,7 @@ struct KArgs {
   BwdArgs a;
   int nchains, nch;
   int* flags;        // chunks finished per chain, counted from the end
+  WaitHooks hooks;
   float* cot;        // per chain: carry cotangent [m][W, S][E x D]
   float* cws;        // per cluster scratch
 };
@@ -356,9 +357,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     const int b = q / H, hh = q % H;
     if (j > 0 && tid == 0 && !s.bad) {
       int spins = 0;
-      while (ld_acquire(&K.flags[q]) < j) {
+      while (ld_acquire(&K.flags[q]) < j + K.hooks.flag_bias) {
         __nanosleep(200);
-        if (++spins > 50000000) {
+        if (++spins > K.hooks.spin_limit) {
           set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
           s.bad = 1;
           break;
@@ -967,6 +968,7 @@ cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t st) {
   k.a = a;
   k.nchains = a.p.B * a.p.H;
   k.nch = n_chunks(a.p);
+  k.hooks = wait_hooks();
   uint8_t* ws = (uint8_t*)a.ws;
   k.flags = (int*)ws;
   k.cot = (float*)(ws + align256((size_t)k.nchains * sizeof(int)));

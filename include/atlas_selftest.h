@@ -18,6 +18,15 @@ extern "C" {
 int atlas_selftest_tc_gemm(const float* A, const float* B, float* D, int32_t M, int32_t N, int32_t K,
                            int32_t a_mn_major, int32_t b_mn_major, void* stream);
 
+/* Failure-detection test hook for the bounded device-side waits of the tensor
+ * path: every chunk-ordering wait requires its counter to exceed the normal
+ * threshold by `flag_bias` (a value nothing ever reaches when > 0) and gives up
+ * after `spin_limit` polls (<= 0 restores the default).  A forward or backward
+ * launched with flag_bias > 0 therefore reports ATLAS_ERR_DEVICE_TIMEOUT through
+ * atlas_scan_status() instead of hanging.  Affects later launches from this
+ * process; reset with (0, 0). */
+int atlas_debug_set_wait_hooks(int32_t flag_bias, int32_t spin_limit);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,6 +14,9 @@ def test_library_exports_every_header_function():
     for n in names:
         assert hasattr(lib, n), n
     assert lib.atlas_abi_version() == L.ATLAS_ABI_VERSION
+    import os
+    for n in L.header_functions(os.path.join(os.path.dirname(L.HEADER), "atlas_selftest.h")):
+        assert hasattr(lib, n), n
 
 
 def _p(**kw):

@@ -59,3 +59,25 @@ def test_tc_backward(T, omega, ste, sg, act, xav):
             errs[n] = rel(to_np(res[7][i]), dst[i])
     print({k_: f"{v_:.2e}" for k_, v_ in errs.items()})
     assert max(errs.values()) < TOL, errs
+
+
+@pytest.mark.parametrize("T,chunk,omega,ns", [(40, 32, 64, 5), (64, 64, 16, 2), (1, 64, 16, 5)])
+def test_tc_backward_edge_cases(T, chunk, omega, ns):
+    from atlas_b200 import ScanConfig, ATLAS_PREC_TENSOR, scan_forward, scan_backward
+    B, H, D, E = 1, 2, 64, 256
+    ins = O.make_inputs(B, T, H, D, seed=40 + T, gamma_mode="random")
+    st = O.make_xavier_state(B, H, D, E, seed=41)
+    st = (st[0], st[1], 0.05 * st[0], 0.05 * st[1])
+    cfg = ScanConfig(chunk=chunk, omega=omega, ns_steps=ns, precision=ATLAS_PREC_TENSOR)
+    q, k, v, a, e, t, g = ins
+    dev = [to_dev(x) for x in ins]
+    y, out, saved = scan_forward(*dev, tuple(to_dev(x) for x in st), cfg)
+    dy = np.random.default_rng(3).standard_normal((B, T, H, D)).astype(np.float32)
+    res = scan_backward(*dev, saved, to_dev(dy), None, cfg, E)
+    torch.cuda.synchronize()
+    grads, dst = O.scan_backward(*ins, st, dy, None, chunk, omega, ns)
+    errs = {n: rel(to_np(v_), grads[n]) for n, v_ in zip(("q", "k", "v", "alpha", "eta", "theta", "gamma"), res[:7])}
+    for i, n in enumerate(("dW1", "dW2", "dS1", "dS2")):
+        if np.abs(dst[i]).max() > 0:
+            errs[n] = rel(to_np(res[7][i]), dst[i])
+    assert max(errs.values()) < TOL, errs

@@ -71,3 +71,35 @@ def test_tc_forward_many_chains_migrate_between_clusters():
     errs = [rel(y, y_o)] + [rel(a, b) for a, b in zip(out, fin)]
     print("rel errors:", errs)
     assert max(errs) < TOL, errs
+
+
+@pytest.mark.parametrize("T,chunk,omega,ns", [(1, 64, 16, 5), (96, 32, 8, 5), (128, 32, 64, 5), (70, 64, 16, 1),
+                                              (64, 64, 16, 3), (130, 16, 4, 5)])
+def test_tc_forward_edge_cases(T, chunk, omega, ns):
+    """single token, chunk 32 / 16 (BASELINE sweep chunks), Omega >= chunk (full
+    in-chunk cumsum, memory_layer.py:247-248), fewer Newton-Schulz steps."""
+    from atlas_b200 import ScanConfig, ATLAS_PREC_TENSOR, scan_forward
+    B, H = 1, 2
+    ins = O.make_inputs(B, T, H, 64, seed=T + chunk, gamma_mode="random")
+    st = O.make_xavier_state(B, H, 64, 256, seed=5)
+    st = (st[0], st[1], 0.05 * st[0], 0.05 * st[1])
+    cfg = ScanConfig(chunk=chunk, omega=omega, ns_steps=ns, precision=ATLAS_PREC_TENSOR)
+    q, k, v, a, e, t, g = ins
+    y, out, _ = scan_forward(to_dev(q), to_dev(k), to_dev(v), to_dev(a), to_dev(e), to_dev(t), to_dev(g),
+                             tuple(to_dev(x) for x in st), cfg)
+    torch.cuda.synchronize()
+    y_o, fin = O.scan_forward(*ins, st, chunk, omega, ns, dtype=np.float64)
+    errs = [rel(to_np(y), y_o)] + [rel(to_np(a_), b_) for a_, b_ in zip(out, fin) if np.abs(b_).max() > 0]
+    assert max(errs) < TOL, errs
+
+
+def test_tc_forward_sweep_384_chains():
+    """BASELINE config 4's largest B*H (384 (b,h) pairs) in one launch: four chains
+    per resident cluster, chunks migrating between clusters."""
+    B, T, H = 32, 64, 12
+    ins = O.make_inputs(B, T, H, 64, seed=9)
+    ins = tuple(_bf(x) for x in ins[:3]) + tuple(ins[3:])
+    y, out = _run(ins, None, torch.bfloat16)
+    y_o, fin = O.scan_forward(*ins, O.lm_initial_state(B, H, 64, 256), 64, 16, 5, dtype=np.float64)
+    errs = [rel(y, y_o)] + [rel(a, b) for a, b in zip(out[:2], fin[:2])]
+    assert max(errs) < TOL, errs
