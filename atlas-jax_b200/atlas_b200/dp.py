@@ -44,7 +44,11 @@ def init(backend="nccl"):
     if int(os.environ.get("WORLD_SIZE", "1")) <= 1:
         return 0, 1
     if not dist.is_initialized():
-        dist.init_process_group(backend=backend)
+        if backend == "nccl":
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+            dist.init_process_group(backend=backend, device_id=dev)
+        else:
+            dist.init_process_group(backend=backend)
     return dist.get_rank(), dist.get_world_size()
 
 

@@ -94,7 +94,7 @@ def scan(q, k, v, a, e, t, g, state, cs, w, ns, ste=False, stop_grad=False):
             return x
         shape = list(x.shape)
         shape[1] = pad
-        return torch.cat([x, torch.full(shape, val, dtype=x.dtype)], 1)
+        return torch.cat([x, torch.full(shape, val, dtype=x.dtype, device=x.device)], 1)
     q, k, v = p(q, 0.0), p(k, 0.0), p(v, 0.0)
     a, e, t, g = p(a, 1.0), p(e, 0.0), p(t, 0.0), p(g, 0.0)
     ys = []
