@@ -22,8 +22,10 @@
 //     the tensor cores; W <- alpha W + X5; read-out y = q + W1 gelu(W2 q) with the
 //     gelu(W2 q) vector exchanged through distributed shared memory.
 //   * tokens go through Polar Express in pairs: two operand-tile sets and two TMEM
-//     regions let one token's epilogue overlap the other token's MMAs
-//     (pe_forward_multi); the momentum / memory recurrences stay in token order.
+//     regions let one token's epilogue overlap the other token's MMAs.  A
+//     dedicated producer warp issues every MMA (pe_produce); the 8 epilogue warps
+//     (pe_consume) hand tiles to it through mbarriers.  The momentum / memory
+//     recurrences stay in token order.
 //
 // Numerics: every Polar Express product runs as three bf16 MMAs
 // (hi*hi + hi*lo + lo*hi, float32 accumulation in TMEM), i.e. ~16 mantissa bits

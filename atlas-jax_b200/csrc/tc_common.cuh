@@ -160,29 +160,6 @@ __device__ __forceinline__ void mma3(uint32_t tmd, const uint8_t* ah, const uint
 #define PROF_FLUSH(g)
 #endif
 
-template <typename F>
-__device__ __forceinline__ bool mma_sync_run(uint64_t* bar, volatile int* bad, uint32_t& phase, F issue,
-                                             unsigned long long* prof = nullptr) {
-  long long t0 = prof ? clock64() : 0;
-  fence_async_smem();
-  fence_before();
-  __syncthreads();
-  if (*bad) return false;
-  long long t1 = prof ? clock64() : 0;
-  if (threadIdx.x < 32) {  // warp 0 issues (one elected lane)
-    fence_after();
-    issue();
-    mma_commit(bar);
-  }
-  bool ok = mbar_wait(bar, phase);
-  phase ^= 1;
-  fence_after();
-  if (prof && threadIdx.x == 0) {
-    prof[0] += t1 - t0;
-    prof[1] += clock64() - t1;
-  }
-  return ok;
-}
 
 }  // namespace tc
 }  // namespace atlas
@@ -239,87 +216,6 @@ __device__ __forceinline__ void pe_save(const PESlot& q, int type, int st) {
     bulk_s2g(o + AT_BYTES, type == 0 ? q.Al : q.Bl, AT_BYTES);
   }
   bulk_commit();
-}
-
-// Up to two independent Polar Express forwards, interleaved so that one slot's
-// epilogue (TMEM read-out, bf16 split, tile stores) overlaps the other slot's
-// MMAs.  The caller has stored X0 into each slot's X tiles.  On return each
-// slot's final X~ (float32) is in TMEM at tm + TM_X (+64 for rows 128-255).
-// Returns false if a bounded wait expired.
-__device__ __noinline__ static bool pe_forward_multi(PESlot* sl, int nslots, int steps, volatile int* bad,
-                                 unsigned long long* prof = nullptr) {
-  const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
-  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
-  const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
-  const int P = 3 * steps;
-  bool ok = true;
-  fence_async_smem();
-  fence_before();
-  __syncthreads();
-  if (*bad) return false;
-  if (tid == 0)
-    for (int s = 0; s < nslots; ++s)
-      if (sl[s].ns) pe_save(sl[s], 2, -1);  // X0
-  for (int s = 0; s < nslots; ++s)
-    if (w == 4 * s) {  // slot s is issued by warp 4s (one elected lane)
-      fence_after();
-      pe_issue(sl[s], 0);
-      mma_commit(sl[s].bar);
-    }
-  for (int p = 0; p < P; ++p) {
-    const int type = p % 3, st = p / 3;
-    for (int s = 0; s < nslots; ++s) {
-      PESlot& q = sl[s];
-      long long t0 = prof ? clock64() : 0;
-      if (!*bad && !mbar_wait(q.bar, q.phase)) ok = false;
-      q.phase ^= 1;
-      fence_after();
-      if (prof && tid == 0) prof[1] += clock64() - t0;
-      long long te = prof ? clock64() : 0;
-      if (type == 0) {
-        float av[32];
-        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
-        tmem_wait_ld();
-        if (l < 16) store_split32(q.Ah, q.Al, ra, dc, D, av);
-      } else if (type == 1) {
-        const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
-        float av[32], a2[32];
-        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
-        tmem_ld32(q.tm + lane_off + TM_A2 + dc, a2);
-        tmem_wait_ld();
-        if (l < 16) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
-          store_split32(q.Bh, q.Bl, ra, dc, D, a2);  // B'[ra][c]
-        }
-      } else if (st + 1 < steps) {
-        float x0[32], x1[32];
-        tmem_ld32(q.tm + lane_off + TM_X + dc, x0);
-        tmem_ld32(q.tm + lane_off + TM_X + 64 + dc, x1);
-        tmem_wait_ld();
-        store_split32(q.Xh, q.Xl, e0, dc, D, x0);
-        store_split32(q.Xh, q.Xl, e1, dc, D, x1);
-      }
-      if (prof && tid == 0) prof[12] += clock64() - te;
-      if (p + 1 < P) {
-        long long t1 = prof ? clock64() : 0;
-        fence_async_smem();
-        fence_before();
-        __syncthreads();
-        if (prof && tid == 0) prof[0] += clock64() - t1;
-        if (q.ns && tid == 0) pe_save(q, type, st);
-        if (w == 4 * s && !*bad) {
-          long long ti = prof ? clock64() : 0;
-          fence_after();
-          pe_issue(q, (p + 1) % 3);
-          mma_commit(q.bar);
-          if (prof && l == 0) prof[11] += clock64() - ti;
-        }
-      }
-    }
-  }
-  if (tid == 0) bulk_wait0();  // saved tiles globally visible before anyone reads them back
-  return ok;
 }
 
 }  // namespace tc
