@@ -50,7 +50,7 @@ namespace tc {
 using namespace tcx;
 
 struct __align__(1024) Smem {
-  uint8_t slot[2][NS_TILE_BYTES];  // per in-flight token: X~ hi/lo, A hi/lo, B' hi/lo (frozen pass: scratch)
+  uint8_t slot[2][NS_TILE_BYTES];  // per in-flight token: stacked X~, stacked A, B' hi/lo (frozen pass: scratch)
   float G[MAXCS * D];              // per-token column factor: err (rank 0) or k (rank 1)
   float gate[4][MAXCS];            // alpha, eta, theta, gamma
   float qv[D];
@@ -68,10 +68,10 @@ __device__ __forceinline__ PESlot make_slot(Smem& s, int j, uint32_t tmem) {
   PESlot p;
   uint8_t* b = s.slot[j];
   p.Xh = b;
-  p.Xl = b + XT_BYTES;
+  p.Xl = b + XLO;
   p.Ah = b + 2 * XT_BYTES;
-  p.Al = p.Ah + AT_BYTES;
-  p.Bh = p.Al + AT_BYTES;
+  p.Al = p.Ah + XLO;
+  p.Bh = p.Ah + 2 * AT_BYTES;
   p.Bl = p.Bh + AT_BYTES;
   p.bar = &s.bar[j];
   p.tm = tmem + 256u * j;
@@ -341,10 +341,10 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
           float xv[32];
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[0][jj] * inv;
-          store_split32(sl[j].Xh, sl[j].Xl, e0, dc, D, xv);
+          store_stk<32>(sl[j].Xh, e0, dc, xv);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[1][jj] * inv;
-          store_split32(sl[j].Xh, sl[j].Xl, e1, dc, D, xv);
+          store_stk<32>(sl[j].Xh, e1, dc, xv);
         }
         PROF_ADD(3, tnorm)
       }

@@ -239,6 +239,11 @@ namespace tc {
 namespace bwd {
 
 
+// TMEM column map of the Polar Express VJP (phase C uses all 512 columns)
+constexpr uint32_t VJ_P = 0;    // P = G~^T X~ stack (128 cols)
+constexpr uint32_t VJ_S = 128;  // Ps A + A Ps stack (128 cols)
+constexpr uint32_t VJ_X = 256;  // dX~ = G~ B' + X~ Sym, two 128-row halves (128 cols)
+
 // One MMA group issued by epilogue warp 0 itself (single problem in flight, so a
 // hand-off to the producer warp would only add latency): publish the operand
 // tiles to the tensor core, issue, wait.  g: 0 = P = G~^T X~, 1 = Ps A + A Ps,
@@ -250,19 +255,22 @@ __device__ __forceinline__ bool vjp_mma(Smem& s, PEBars& B, uint32_t tm, int g, 
   if (*bad) return false;
   if (threadIdx.x < 32) {
     fence_after();
+    // X~, A, G~ and Ps are stacked tiles; B' and Sym are plain tiles
     if (g == 0) {
-      mma3<E>(tm + TM_GRAM, s.Gh, s.Gl, true, s.Xh, s.Xl, true, 64, 0, false);
+      mma_stack<E>(tm + VJ_P, s.Gh, s.Xh, false);  // P = G~^T X~
       mma_commit(B.done[0]);
       // G~ B' does not depend on Sym: start it now so it overlaps the P epilogue
       // (later commits cover it; MMAs into one accumulator execute in order)
       for (int h2 = 0; h2 < 2; ++h2)
-        mma3<D>(tm + TM_X + 64 * h2, s.Gh, s.Gl, false, s.Bh, s.Bl, true, 128, 16384 * h2, false);
-    } else if (g == 1) {
-      mma3<D>(tm + TM_A2, s.Ph, s.Pl, false, s.Ah, s.Al, true, 64, 0, false);
-      mma3<D>(tm + TM_A2, s.Ah, s.Al, false, s.Ph, s.Pl, true, 64, 0, true);
+        mma3<D>(tm + VJ_X + 64 * h2, s.Gh, s.Gh + XLO, false, XC, s.Bh, s.Bl, true, 64, 128, 16 * 16 * XC * h2,
+                false);
+    } else if (g == 1) {  // Ps A + A Ps  (Ps, A symmetric: Ps^T A + A^T Ps)
+      mma_stack<D>(tm + VJ_S, s.Ph, s.Ah, false);
+      mma_stack<D>(tm + VJ_S, s.Ah, s.Ph, true);
     } else {
       for (int h2 = 0; h2 < 2; ++h2)
-        mma3<D>(tm + TM_X + 64 * h2, s.Xh, s.Xl, false, s.Yh, s.Yl, true, 128, 16384 * h2, true);
+        mma3<D>(tm + VJ_X + 64 * h2, s.Xh, s.Xh + XLO, false, XC, s.Yh, s.Yl, true, 64, 128, 16 * 16 * XC * h2,
+                true);
     }
     if (g != 0) mma_commit(B.done[0]);
   }
@@ -285,7 +293,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   const AtlasScanParams& P = a.p;
   const int tid = threadIdx.x, wp = tid >> 5, l = tid & 31;
   const int qd = wp & 3, ch = wp >> 2;
-  const int e0 = 32 * qd + l, e1 = e0 + 128, dc = 32 * ch, ra = 16 * qd + l;
+  const int e0 = 32 * qd + l, e1 = e0 + 128, dc = 32 * ch;
+  const int rr = 16 * qd + (l & 15), d0 = dc + (l & 16);  // stack_finish row / columns of this lane
   const uint32_t rank = cluster_rank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
   const int cs = P.chunk, T = P.T, H = P.H, nch = K.nch;
@@ -319,8 +328,10 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   uint32_t phase_ld = 0;
   PROF_INIT
   PESlot sl[2];
-  sl[0] = PESlot{s.Xh, s.Xl, s.Ah, s.Al, s.Bh, s.Bl, &s.bar, tm, 0, nullptr, 0};
-  sl[1] = PESlot{s.Gh, s.Gl, s.Ph, s.Pl, s.Yh, s.Yl, &s.bar2, tm + 256, 0, nullptr, 0};
+  // stacked X~ / A tiles: the lo part sits XLO bytes after the hi part (the
+  // Xh..Xl and Ah..Al byte ranges of the struct hold one stacked tile each)
+  sl[0] = PESlot{s.Xh, s.Xh + XLO, s.Ah, s.Ah + XLO, s.Bh, s.Bl, &s.bar, tm, 0, nullptr, 0};
+  sl[1] = PESlot{s.Gh, s.Gh + XLO, s.Ph, s.Ph + XLO, s.Yh, s.Yl, &s.bar2, tm + 256, 0, nullptr, 0};
   PEBars B;
   B.ready[0] = &s.ready[0];
   B.ready[1] = &s.ready[1];
@@ -435,10 +446,10 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           float xv[32];
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[0][jj] * inv;
-          store_split32(sl[jp].Xh, sl[jp].Xl, e0, dc, D, xv);
+          store_stk<32>(sl[jp].Xh, e0, dc, xv);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) xv[jj] = Sv[1][jj] * inv;
-          store_split32(sl[jp].Xh, sl[jp].Xl, e1, dc, D, xv);
+          store_stk<32>(sl[jp].Xh, e1, dc, xv);
         }
       }
       if (P.ns_steps > 0) {
@@ -620,8 +631,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           }
           PROF_ADD(5, tns)
           PROF_T(tvjp)
-          store_split32(s.Gh, s.Gl, e0, dc, D, dW[0]);
-          store_split32(s.Gh, s.Gl, e1, dc, D, dW[1]);
+          store_stk<32>(s.Gh, e0, dc, dW[0]);
+          store_stk<32>(s.Gh, e1, dc, dW[1]);
           const int steps_ = P.ns_steps;
           for (int st = steps_ - 1; st >= 0; --st) {
             const float cb = (float)kPE[st][1], cc = (float)kPE[st][2];
@@ -631,34 +642,36 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             }
             PROF_T(tcp)
             PROF_ADD(9, tcp)
-            // P = G~^T X~
-            ok = vjp_mma(s, B, tm, 0, &s.bad) && ok;  // P = G~^T X~
-            float pv[32];
-            tmem_ld32(tm + lane_off + TM_GRAM + dc, pv);
-            tmem_wait_ld();
+            // P = G~^T X~ (stack), this lane's 16 entries P[rr][d0 + j]
+            ok = vjp_mma(s, B, tm, 0, &s.bad) && ok;
+            float pv[16];
+            {
+              float v[64];
+              tmem_ld64(tm + lane_off + VJ_P + 2 * dc, v);
+              tmem_wait_ld();
+              stack_finish(v, pv);
+            }
             float* Pf = pf_base(s);
-            if (l < 16) {
 #pragma unroll
-              for (int m = 0; m < 8; ++m)
-                *(float4*)&Pf[pf_idx(ra, dc + 4 * m)] = make_float4(pv[4 * m], pv[4 * m + 1], pv[4 * m + 2], pv[4 * m + 3]);
-            }
+            for (int m = 0; m < 4; ++m)
+              *(float4*)&Pf[pf_idx(rr, d0 + 4 * m)] = make_float4(pv[4 * m], pv[4 * m + 1], pv[4 * m + 2], pv[4 * m + 3]);
             epi_sync();
-            if (l < 16) {
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) pv[jj] += Pf[pf_idx(dc + jj, ra)];  // Ps = P + P^T
-              store_split32(s.Ph, s.Pl, ra, dc, D, pv);
-            }
+            for (int jj = 0; jj < 16; ++jj) pv[jj] += Pf[pf_idx(d0 + jj, rr)];  // Ps = P + P^T
+            store_stk<16>(s.Ph, rr, d0, pv);
             // Sym = b Ps + c (Ps A + A Ps)
-            ok = vjp_mma(s, B, tm, 1, &s.bad) && ok;  // Ps A + A Ps
-            float yv[32];
-            tmem_ld32(tm + lane_off + TM_A2 + dc, yv);
-            tmem_wait_ld();
-            if (l < 16) {
+            ok = vjp_mma(s, B, tm, 1, &s.bad) && ok;  // Ps A + A Ps (stack)
+            {
+              float v[64], yv[16];
+              tmem_ld64(tm + lane_off + VJ_S + 2 * dc, v);
+              tmem_wait_ld();
+              stack_finish(v, yv);
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) yv[jj] = fmaf(cc, yv[jj], cb * pv[jj]);
-              store_split32(s.Yh, s.Yl, ra, dc, D, yv);
+              for (int jj = 0; jj < 16; ++jj) yv[jj] = fmaf(cc, yv[jj], cb * pv[jj]);
+              store_split8(s.Yh, s.Yl, cm_off(rr, d0, D), yv);
+              store_split8(s.Yh, s.Yl, cm_off(rr, d0 + 8, D), yv + 8);
             }
-            // dX~ = G~ B' + X~ Sym
+          // dX~ = G~ B' + X~ Sym
             ok = vjp_mma(s, B, tm, 2, &s.bad) && ok;  // G~ B' + X~ Sym
             if (st > 0 && tid == 0 && !s.bad) {  // prefetch step st-1's tiles; X, A, B' are free now
               const uint8_t* o = nscur + (size_t)(st - 1) * NS_STEP_BYTES;
@@ -670,12 +683,12 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
               bulk_g2s(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES, &s.bar_ld);
               bulk_g2s(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES, &s.bar_ld);
             }
-            tmem_ld32(tm + lane_off + TM_X + dc, gx[0]);
-            tmem_ld32(tm + lane_off + TM_X + 64 + dc, gx[1]);
+            tmem_ld32(tm + lane_off + VJ_X + dc, gx[0]);
+            tmem_ld32(tm + lane_off + VJ_X + 64 + dc, gx[1]);
             tmem_wait_ld();
             if (st > 0) {
-              store_split32(s.Gh, s.Gl, e0, dc, D, gx[0]);
-              store_split32(s.Gh, s.Gl, e1, dc, D, gx[1]);
+              store_stk<32>(s.Gh, e0, dc, gx[0]);
+              store_stk<32>(s.Gh, e1, dc, gx[1]);
             }
           }
           PROF_ADD(6, tvjp)

@@ -16,11 +16,20 @@ constexpr int MAXCS = 64;
 constexpr int DE = D * E;
 constexpr int XT_BYTES = E * D * 2;  // bf16 E x D tile
 constexpr int AT_BYTES = D * D * 2;  // bf16 D x D tile
+// X~, A, G~ and Ps live in "stacked" tiles of 128 columns: logical column d is
+// stored as its bf16 hi part at stacked column stk(d) = 32 * (d / 16) + d % 16 and
+// its lo part 16 columns later (XLO bytes on), i.e. blocks of 16 hi columns
+// alternate with blocks of 16 lo columns.  One M=128 x N=128 MMA over two stacked
+// tiles (both MN-major) then yields every hi/lo product pair Zx^T Yy, with the hi
+// row and the lo row of logical row i in lanes 32 * (i / 16) + i % 16 and that + 16.
+constexpr int XC = 128;
+constexpr uint32_t XLO = 256;
+__host__ __device__ constexpr int stk(int d) { return ((d >> 4) << 5) | (d & 15); }
 constexpr int TMEM_COLS = 512;  // two in-flight problems of 256 columns each
-// TMEM column map
-constexpr uint32_t TM_X = 0;      // X~ update: rows 0-127 in cols [0,64), rows 128-255 in [64,128)
-constexpr uint32_t TM_GRAM = 128; // Gram A (M=64 layout)
-constexpr uint32_t TM_A2 = 192;   // A*A    (M=64 layout)
+// TMEM column map of one in-flight Polar Express problem (256 columns):
+constexpr uint32_t TM_GRAM = 0;   // Gram stack (128 cols); then A (16 cols per lane) for the A*A epilogue
+constexpr uint32_t TM_X = 0;      // X~ B'^T: rows 0-127 in cols [0,64), rows 128-255 in [64,128) (after the Gram is read)
+constexpr uint32_t TM_A2 = 128;   // A*A stack (128 cols)
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -67,10 +76,54 @@ __device__ __forceinline__ void store_split32(uint8_t* th, uint8_t* tl, int r, i
 #pragma unroll
   for (int k = 0; k < 4; ++k) store_split8(th, tl, cm_off(r, c0 + 8 * k, C), v + 8 * k);
 }
+// Logical columns [c0, c0+n) (c0 a multiple of 8) of row r of a stacked tile.
+template <int n>
+__device__ __forceinline__ void store_stk(uint8_t* t, int r, int c0, const float* v) {
+#pragma unroll
+  for (int k = 0; k < n / 8; ++k) store_split8(t, t + XLO, cm_off(r, stk(c0 + 8 * k), XC), v + 8 * k);
+}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   tmem_ld16(taddr, v);
   tmem_ld16(taddr + 16, v + 16);
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  tmem_st16(taddr, v);
+  tmem_st16(taddr + 16, v + 16);
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Finishes one row of a stacked product whose 128 TMEM columns [64 ch, 64 ch + 64)
+// the lane loaded into v (hi parts of logical columns 32ch..+15, their lo parts,
+// then the same for 32ch+16..+31).  Lanes l < 16 hold the hi row i (Zh^T Yh | Zh^T Yl),
+// lanes l >= 16 the lo row i (Zl^T Yh | unused).  Afterwards lane l < 16 holds
+// columns 32ch..32ch+15 of  Zh^T Yh + Zh^T Yl + Zl^T Yh  in r[0..15], lane l + 16
+// columns 32ch+16..32ch+31.
+__device__ __forceinline__ void stack_finish(const float* v, float* r) {
+  const bool hi = (threadIdx.x & 16) == 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float keep = hi ? v[j] + v[16 + j] : v[32 + j];
+    const float send = hi ? v[32 + j] + v[48 + j] : v[j];
+    r[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+}
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  tmem_ld16(taddr, v);
+  tmem_ld16(taddr + 16, v + 16);
+  tmem_ld16(taddr + 32, v + 32);
+  tmem_ld16(taddr + 48, v + 48);
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -117,29 +170,43 @@ __device__ __forceinline__ float warp_reduce_scatter32(float* v) {
 
 // Three-term split product into TMEM column `tmd`:
 //   D (+)= Ah*Bh + Ah*Bl + Al*Bh   (M x 64, contraction length K)
-// Operand tiles have 64 columns (core-matrix tiles of C = 64).  amn / bmn pick
-// the MN-major view (rows = K index) instead of the K-major view (rows = M/N).
-// a_off is a byte offset into the A tiles (selects the 128-row half for M = 128).
-// Descriptors are built once per term; stepping K by 16 adds to the 14-bit
-// start-address field (shared-memory addresses < 256 KB never carry out of it).
+// ca / cb are the column counts of the A / B core-matrix tiles: 64 for plain
+// tiles, XC for a stacked A tile (K-major only; al = ah + XLO).  amn / bmn pick the MN-major view (rows = K index)
+// instead of the K-major view (rows = M/N).  a_off is a byte offset into the A
+// tiles (selects the 128-row half for M = 128).  Descriptors are built once per
+// term; stepping K by 16 adds to the 14-bit start-address field (shared-memory
+// addresses < 256 KB never carry out of it).
 template <int K>
-__device__ __forceinline__ void mma3(uint32_t tmd, const uint8_t* ah, const uint8_t* al, bool amn,
-                                     const uint8_t* bh, const uint8_t* bl, bool bmn, int M, uint32_t a_off,
+__device__ __forceinline__ void mma3(uint32_t tmd, const uint8_t* ah, const uint8_t* al, bool amn, int ca,
+                                     const uint8_t* bh, const uint8_t* bl, bool bmn, int cb, int M, uint32_t a_off,
                                      bool accumulate) {
   const uint32_t id = idesc_bf16(M, 64, amn, bmn);
-  const uint64_t sa = amn ? (2048 >> 4) : (256 >> 4);
-  const uint64_t sb = bmn ? (2048 >> 4) : (256 >> 4);
+  // K-major stacked tiles hold 16 hi columns per 32 stacked columns: 512 bytes per 16 of K
+  const uint64_t sa = amn ? (uint64_t)(2 * 16 * ca) >> 4 : (ca == XC ? (512 >> 4) : (256 >> 4));
+  const uint64_t sb = bmn ? (uint64_t)(2 * 16 * cb) >> 4 : (256 >> 4);
   const uint8_t* ta[3] = {ah, ah, al};
   const uint8_t* tb[3] = {bh, bl, bh};
 #pragma unroll
   for (int t = 0; t < 3; ++t) {
     const uint32_t aa = smem_u32(ta[t]) + a_off, bb = smem_u32(tb[t]);
-    const uint64_t da = amn ? desc_mnmajor(aa, 64) : desc_kmajor(aa, 64);
-    const uint64_t db = bmn ? desc_mnmajor(bb, 64) : desc_kmajor(bb, 64);
+    const uint64_t da = amn ? desc_mnmajor(aa, ca) : desc_kmajor(aa, ca);
+    const uint64_t db = bmn ? desc_mnmajor(bb, cb) : desc_kmajor(bb, cb);
 #pragma unroll
     for (int ks = 0; ks < K / 16; ++ks)
       mma_bf16(tmd, da + ks * sa, db + ks * sb, id, (accumulate || t || ks) ? 1u : 0u);
   }
+}
+
+// D (+)= Z^T Y over two stacked tiles (K x 64 logical, MN-major): one
+// M=128 x N=128 MMA per 16 of K; see stack_finish for the result layout.
+template <int K>
+__device__ __forceinline__ void mma_stack(uint32_t tmd, const uint8_t* z, const uint8_t* y, bool accumulate) {
+  const uint32_t id = idesc_bf16(128, 128, true, true);
+  const uint64_t dz = desc_mnmajor(smem_u32(z), XC), dy = desc_mnmajor(smem_u32(y), XC);
+  constexpr uint64_t step = (uint64_t)(2 * 16 * XC) >> 4;
+#pragma unroll
+  for (int ks = 0; ks < K / 16; ++ks)
+    mma_bf16(tmd, dz + ks * step, dy + ks * step, id, (accumulate || ks) ? 1u : 0u);
 }
 
 // Optional phase timers (build with -DATLAS_PHASE_PROF; thread 0 accumulates
@@ -177,6 +244,8 @@ inline int max_clusters_bound() {
 
 // One Polar Express problem in flight: its operand tiles, TMEM base column,
 // completion barrier, and (optionally) where to save each step's operand tiles.
+// X~ (E x 64) and A (64 x 64) are stacked tiles (Xl = Xh + XLO, Al = Ah + XLO);
+// B' is two plain 64-column tiles (Bl = Bh + AT_BYTES).
 struct PESlot {
   uint8_t *Xh, *Xl, *Ah, *Al, *Bh, *Bl;
   uint64_t* bar;
@@ -185,37 +254,18 @@ struct PESlot {
   uint8_t* ns;       // global destination of step k's tiles at ns + k * NS_TILE_BYTES, or null
   int save_last;     // unused (every step is saved when ns is set)
 };
+// Saved per step: stacked X~ (2 * XT_BYTES), stacked A (2 * AT_BYTES), B' hi, B' lo.
 constexpr size_t NS_TILE_BYTES = 2 * XT_BYTES + 4 * AT_BYTES;
 
 __device__ __forceinline__ void pe_issue(const PESlot& p, int type) {
-  if (type == 0) {         // Gram A = X~^T X~
-    mma3<E>(p.tm + TM_GRAM, p.Xh, p.Xl, true, p.Xh, p.Xl, true, 64, 0, false);
-  } else if (type == 1) {  // A * A
-    mma3<D>(p.tm + TM_A2, p.Ah, p.Al, false, p.Ah, p.Al, true, 64, 0, false);
+  if (type == 0) {         // Gram stack: X~^T X~ over the hi/lo pairs
+    mma_stack<E>(p.tm + TM_GRAM, p.Xh, p.Xh, false);
+  } else if (type == 1) {  // A A = A^T A (A symmetric)
+    mma_stack<D>(p.tm + TM_A2, p.Ah, p.Ah, false);
   } else {                 // X~ B'^T, two 128-row halves
-    mma3<D>(p.tm + TM_X, p.Xh, p.Xl, false, p.Bh, p.Bl, false, 128, 0, false);
-    mma3<D>(p.tm + TM_X + 64, p.Xh, p.Xl, false, p.Bh, p.Bl, false, 128, 16384, false);
+    mma3<D>(p.tm + TM_X, p.Xh, p.Xl, false, XC, p.Bh, p.Bl, false, 64, 128, 0, false);
+    mma3<D>(p.tm + TM_X + 64, p.Xh, p.Xl, false, XC, p.Bh, p.Bl, false, 64, 128, 16 * 16 * XC, false);
   }
-}
-
-// Thread 0: copy the tile the epilogue of phase `type` of step `st` just produced
-// to the slot's scratch (step k at ns + k * NS_TILE_BYTES: X hi, X lo, A hi, A lo,
-// B' hi, B' lo).  type 0 -> A_st, 1 -> B'_st, 2 -> X_{st+1}.  Bulk copies are
-// asynchronous; before issuing, all but the most recent earlier copy must have
-// finished reading shared memory -- a tile is rewritten three phases after it was
-// produced, so this never stalls on a copy whose source is still needed.
-__device__ __forceinline__ void pe_save(const PESlot& q, int type, int st) {
-  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-  if (type == 2) {
-    uint8_t* o = q.ns + (size_t)(st + 1) * NS_TILE_BYTES;
-    bulk_s2g(o, q.Xh, XT_BYTES);
-    bulk_s2g(o + XT_BYTES, q.Xl, XT_BYTES);
-  } else {
-    uint8_t* o = q.ns + (size_t)st * NS_TILE_BYTES + 2 * XT_BYTES + (type == 0 ? 0 : 2 * AT_BYTES);
-    bulk_s2g(o, type == 0 ? q.Ah : q.Bh, AT_BYTES);
-    bulk_s2g(o + AT_BYTES, type == 0 ? q.Al : q.Bl, AT_BYTES);
-  }
-  bulk_commit();
 }
 
 }  // namespace tc
@@ -253,10 +303,17 @@ __device__ __forceinline__ void pe_publish(PEBars& B, int s) {
 
 // Consumers (threads 0..255).  X0 of every slot is already stored by these threads.
 // On return each slot's final X~ is in TMEM (tm + TM_X, + 64).
+//
+// Gram and A*A come back as hi/lo stacks (see stack_finish): warp w reads the
+// 64 columns of column half w / 4 of its lane quadrant, and each lane finishes 16
+// entries (row rr, columns d0..d0+15) of the symmetric product with one shuffle
+// per entry.  The lane writes its 16 entries of A back over its own TMEM lane for
+// the A*A epilogue (B' = a I + b A + c A A), which uses the same lane/column map.
 static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad,
                                                   unsigned long long* prof = nullptr) {
   const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, qd = w & 3, ch = w >> 2;
-  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128, ra = 16 * qd + l;
+  const int dc = 32 * ch, e0 = 32 * qd + l, e1 = e0 + 128;
+  const int rr = 16 * qd + (l & 15), d0 = dc + (l & 16);
   const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
   const int P = 3 * steps;
   bool ok = true;
@@ -272,38 +329,49 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
       long long te = prof ? clock64() : 0;
       if (prof && threadIdx.x == 0) prof[11] += te - tw;
       if (type == 0) {
-        float av[32];
-        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
+        float v[64], a[16];
+        tmem_ld64(q.tm + lane_off + TM_GRAM + 2 * dc, v);
         tmem_wait_ld();
-        if (l < 16) store_split32(q.Ah, q.Al, ra, dc, D, av);
+        stack_finish(v, a);  // A[rr][d0 + j]
+        store_stk<16>(q.Ah, rr, d0, a);
+        tmem_st16(q.tm + lane_off + TM_GRAM + 2 * dc, a);
+        tmem_wait_st();
       } else if (type == 1) {
         const float ca = (float)kPE[st][0], cb = (float)kPE[st][1], cc = (float)kPE[st][2];
-        float av[32], a2[32];
-        tmem_ld32(q.tm + lane_off + TM_GRAM + dc, av);
-        tmem_ld32(q.tm + lane_off + TM_A2 + dc, a2);
+        float v[64], av[16], b2[16];
+        tmem_ld64(q.tm + lane_off + TM_A2 + 2 * dc, v);
+        tmem_ld16(q.tm + lane_off + TM_GRAM + 2 * dc, av);
         tmem_wait_ld();
-        if (l < 16) {
+        stack_finish(v, b2);  // (A A)[rr][d0 + j]
 #pragma unroll
-          for (int j = 0; j < 32; ++j) a2[j] = fmaf(cc, a2[j], cb * av[j]) + (ra == dc + j ? ca : 0.f);
-          store_split32(q.Bh, q.Bl, ra, dc, D, a2);  // B'[ra][c]
-        }
+        for (int j = 0; j < 16; ++j) b2[j] = fmaf(cc, b2[j], cb * av[j]) + (rr == d0 + j ? ca : 0.f);
+        store_split8(q.Bh, q.Bl, cm_off(rr, d0, D), b2);  // B'[rr][d0..d0+15]
+        store_split8(q.Bh, q.Bl, cm_off(rr, d0 + 8, D), b2 + 8);
       } else if (st + 1 < steps) {
         float x0[32], x1[32];
         tmem_ld32(q.tm + lane_off + TM_X + dc, x0);
         tmem_ld32(q.tm + lane_off + TM_X + 64 + dc, x1);
         tmem_wait_ld();
-        store_split32(q.Xh, q.Xl, e0, dc, D, x0);
-        store_split32(q.Xh, q.Xl, e1, dc, D, x1);
+        store_stk<32>(q.Xh, e0, dc, x0);
+        store_stk<32>(q.Xh, e1, dc, x1);
       }
       if (p + 1 < P) pe_publish(B, s);
       if (prof && threadIdx.x == 0) prof[12] += clock64() - te;
+#ifdef ATLAS_PHASE_PROF_EPI
+      if (prof && threadIdx.x == 0) prof[7 + type] += clock64() - te;
+#endif
     }
   }
   return ok;
 }
 
-// Producer (one whole warp).  Mirrors pe_consume's schedule; saves the freshly
-// published tiles (when q.ns is set) before issuing the next MMAs.
+// Producer (one whole warp).  Mirrors pe_consume's schedule; when q.ns is set it
+// saves the tile just published (X_st before the Gram, A_st before A*A, B'_st
+// before X~ B'^T) with a bulk copy.  A tile is rewritten by the epilogue two or
+// three phases after it was saved, so before committing the Gram and A*A groups
+// the producer lets all but its newest copy finish reading shared memory: the
+// copies of X_st (rewritten by the X~ B'^T epilogue), A_{st-1} and B'_{st-1}
+// are then complete before their tiles change.
 static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad) {
   const int P = 3 * steps;
   const bool lead = (threadIdx.x & 31) == 0;
@@ -315,20 +383,21 @@ static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nsl
       if (!*bad && !mbar_wait(B.ready[s], B.ready_phase[s])) ok = false;
       B.ready_phase[s] ^= 1;
       fence_after();
-      if (q.ns && lead) {  // tile published for this phase: X_st (type 0), A_st (1), B'_st (2)
-        if (type == 0) {
-          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          uint8_t* o = q.ns + (size_t)st * NS_TILE_BYTES;
-          bulk_s2g(o, q.Xh, XT_BYTES);
-          bulk_s2g(o + XT_BYTES, q.Xl, XT_BYTES);
-          bulk_commit();
-        } else {
-          pe_save(q, type - 1, st);
-        }
+      if (q.ns && lead) {
+        uint8_t* o = q.ns + (size_t)st * NS_TILE_BYTES;
+        if (type == 0)
+          bulk_s2g(o, q.Xh, 2 * XT_BYTES);
+        else if (type == 1)
+          bulk_s2g(o + 2 * XT_BYTES, q.Ah, 2 * AT_BYTES);
+        else
+          bulk_s2g(o + 2 * XT_BYTES + 2 * AT_BYTES, q.Bh, 2 * AT_BYTES);
+        bulk_commit();
       }
       __syncwarp();
       if (!*bad) {
         pe_issue(q, type);
+        if (q.ns && lead && type < 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
         mma_commit(B.done[s]);
       }
     }

@@ -29,6 +29,12 @@ METRIC = "Atlas scan tokens/s fwd+bwd (170M cfg)"
 # algorithmic FLOPs per token-head-layer (m = D, n = E = 4D, ns steps); recompute not counted
 F_FWD = lambda D, ns: ns * 36 * D ** 3 + 40 * D ** 2   # noqa: E731
 F_BWD = lambda D, ns: ns * 56 * D ** 3 + 80 * D ** 2   # noqa: E731
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from an ncu
+# capture of the small case (1 layer, B=8, H=12, T=256).  Both kernels' traffic is
+# per token-head (the backward's Newton-Schulz operand scratch, S_t and W_{t-1}; the
+# forward's saved carries and outputs), so a full launch scales by token-heads.
+NCU_TRAFFIC = {"tc_bwd_kernel": 77.1e9, "tc_fwd_kernel": 128.3e6}
+NCU_TOKEN_HEADS = 8 * 256 * 12
 
 
 def _peaks():
@@ -269,7 +275,10 @@ def gpu_arm(args, rank, world):
                    "grad_allreduce_params": grad_buf.numel()},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak_tf,
-                     "unit": "TFLOP/s", "frac": achieved / peak_tf, "traffic": None,
+                     "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                     "traffic": NCU_TRAFFIC[dom] * (B * T * H) / NCU_TOKEN_HEADS,
+                     "traffic_unit": "bytes per launch",
+                     "traffic_source": "ncu capture at T=256 scaled by token-heads",
                      "peak_source": f"bf16_tflops_sustained ({peak_kind})",
                      "fwd_ms_per_layer": fwd_ms, "bwd_ms_per_layer": bwd_ms},
         "gpu_launches": 2 * NL * args.steps,
