@@ -16,10 +16,12 @@
 //      (p = gelu(W2 q), dz = (W1^T dy) * gelu'(W2 q), dq = dy + W2^T dz).  S_t,
 //      W_{t-1} and p / dz are saved per token in scratch.
 //   C. reverse over tokens with dW, dS in float32 registers: read-out and memory
-//      scan cotangents, Polar Express VJP on the tensor cores (recomputing the five
-//      Newton-Schulz steps of S_t and keeping their operand tiles in scratch),
-//      momentum scan cotangents, and the Omega-window terms that feed the
-//      rank-1 factors (accumulated with global reductions).
+//      scan cotangents, Polar Express VJP on the tensor cores (from the five
+//      Newton-Schulz steps' operand tiles saved in phase B), then the momentum
+//      scan: the gradients of the rank-1 factors and gates of the Omega window come
+//      from two sliding sums kept in TMEM, R_t = sum_{u in [t, t+Om)} c_u dS_u and
+//      M_t = sum_{i in (t-Om, t]} gamma_i f_i g_i^T, each updated by one term in and
+//      one out per token (dS_u is stored in place of W_{u-1} for the term out).
 //   D. frozen-state pass backward (CUDA cores), carry cotangent out.
 //
 // Polar Express VJP of one step, tile orientation (X~ = X^T, G~ = dX~_{k+1}):
@@ -58,7 +60,6 @@ struct __align__(1024) Smem {
   float xbuf[2][E];      // exchanged vector (p into rank 0, dp into rank 1), double-buffered
   float ybuf[4][D];
   float qv[D], dyv[D];
-  float ipacc[MAXCS];
   float gate[4][MAXCS];  // alpha, eta, theta, gamma of the chunk
   float nrm[MAXCS];      // ||S_t||_F (with the 1e-12) per token, from phase B
   float red[8];
@@ -239,10 +240,36 @@ namespace tc {
 namespace bwd {
 
 
+// Deferred step of the momentum recurrence S_u = theta_u S_{u-1} + ... for u = r + 1:
+// with dS = dS_u (the full cotangent of S_u) and xo = S_{u-1} (= S_r, which the
+// normalisation VJP of token r reads anyway), adds dtheta_u = <dS_u, S_{u-1}>
+// (per-warp reduction) and turns dS into theta_u dS_u, the part of dS_r that comes
+// through S_u.  Nothing to do for r = cs - 1 (dS is then the incoming carry cotangent).
+__device__ __forceinline__ void theta_step(float (*dS)[32], float (*xo)[32], int r, int cs, const float* theta,
+                                           float* scal, int l) {
+  const int u = r + 1;
+  if (u >= cs) return;
+  float dt = 0.f;
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) dt = fmaf(dS[0][jj], xo[0][jj], fmaf(dS[1][jj], xo[1][jj], dt));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dt += __shfl_xor_sync(0xffffffffu, dt, o);
+  if (l == 0) red_add(&scal[2 * MAXCS + u], dt);
+  const float th = theta[u];
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) {
+    dS[0][jj] *= th;
+    dS[1][jj] *= th;
+  }
+}
+
 // TMEM column map of the Polar Express VJP (phase C uses all 512 columns)
 constexpr uint32_t VJ_P = 0;    // P = G~^T X~ stack (128 cols)
-constexpr uint32_t VJ_S = 128;  // Ps A + A Ps stack (128 cols)
-constexpr uint32_t VJ_X = 256;  // dX~ = G~ B' + X~ Sym, two 128-row halves (128 cols)
+constexpr uint32_t VJ_S = 0;    // Ps A + A Ps stack (issued after the P epilogue read VJ_P)
+constexpr uint32_t VJ_X = 128;  // dX~ = G~ B' + X~ Sym, two 128-row halves (128 cols)
+// momentum-scan running sums of the reverse token pass, E x D in the VJ_X layout
+constexpr uint32_t VJ_R = 256;  // R_t = sum_{u in [t, t+Om)} c_u dS_u
+constexpr uint32_t VJ_M = 384;  // M_t = sum_{i in (t-Om, t]} gamma_i f_i g_i^T
 
 // One MMA group issued by epilogue warp 0 itself (single problem in flight, so a
 // hand-off to the producer warp would only add latency): publish the operand
@@ -533,6 +560,24 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     PROF_ADD(3, tB)
     PROF_T(tC)
     // ================= C: reverse over the chunk's tokens =================
+    const int Om = win ? P.omega : 1;
+    {  // R = 0, M = M_{cs-1}
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = h ? e1 : e0;
+        float mv[32], zv[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) mv[jj] = zv[jj] = 0.f;
+        for (int i = max(0, cs - Om); i < cs; ++i) {
+          const float f = (win ? s.gate[3][i] : 1.f) * Fm[i * E + e];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) mv[jj] = fmaf(f, s.Gc[i * D + dc + jj], mv[jj]);
+        }
+        tmem_st32(tm + lane_off + VJ_M + 64 * h + dc, mv);
+        tmem_st32(tm + lane_off + VJ_R + 64 * h + dc, zv);
+      }
+      tmem_wait_st();
+    }
     float dW[2][32], dS[2][32];
     {
       float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
@@ -566,7 +611,6 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
         s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
       }
-      if (tid < MAXCS) s.ipacc[tid] = 0.f;
       epi_sync();
       {  // read-out: rank 0 dW1 += dy p^T (tile: p[e] dy[d]); rank 1 dW2 += dz q^T
         const float v0 = vec[r * E + e0], v1 = vec[r * E + e1];
@@ -577,13 +621,15 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           dW[1][jj] = fmaf(v1, xv[dc + jj], dW[1][jj]);
         }
       }
-      if (r > 0) {  // pull the next token's saved rows into L2 while this token's VJP runs
-        const float* nw = Wsave + (size_t)(r - 1) * DE;
-        const float* ns_ = Ssave + (size_t)(r - 1) * DE;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e0 * D + dc));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e1 * D + dc));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(ns_ + e0 * D + dc));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(ns_ + e1 * D + dc));
+      if (r + Om < cs) {  // dS_{r+Om} (read after this token's VJP) into L2
+        const float* pb = Wsave + (size_t)(r + Om) * DE + dc;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + e0 * D));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + e1 * D));
+      }
+      if (r > 0) {  // W_{r-2} for the next token's dalpha
+        const float* nw = Wsave + (size_t)(r - 1) * DE + dc;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e0 * D));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e1 * D));
       }
       float dal = 0.f;
       {
@@ -594,10 +640,17 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv);
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[1][jj], wv[jj], dal);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dal += __shfl_xor_sync(0xffffffffu, dal, o);
+        if (l == 0) red_add(&w.scal[r], dal);  // dalpha_t = <dW_t, W_{t-1}>
       }
       // ---- Polar Express VJP ----
       if (P.pe_ste || P.ns_steps == 0) {
         if (P.pe_ste) {
+          float xo[2][32];
+          ld32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, xo[0]);
+          ld32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, xo[1]);
+          theta_step(dS, xo, r, cs, s.gate[2], w.scal, l);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             dS[0][jj] += dW[0][jj];
@@ -706,6 +759,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         // X0 = S / kappa, kappa = 1.01 sqrt(sum S^2 + 1e-12) + 1e-6
         ld32(St + e0 * D + dc, xo[0]);
         ld32(St + e1 * D + dc, xo[1]);
+        theta_step(dS, xo, r, cs, s.gate[2], w.scal, l);
         float dot = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dot = fmaf(gx[0][jj], xo[0][jj], fmaf(gx[1][jj], xo[1][jj], dot));
@@ -717,80 +771,104 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           dS[1][jj] += gx[1][jj] * inv - coef * xo[1][jj];
         }
       }
-      // ---- momentum scan: dtheta_t = <dS, S_{t-1}>, Omega-window terms ----
-      float dth = 0.f;
-      {
-        float sv[32];
-        ld32(Ssave + (size_t)r * DE + e0 * D + dc, sv);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dth = fmaf(dS[0][jj], sv[jj], dth);
-        ld32(Ssave + (size_t)r * DE + e1 * D + dc, sv);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dth = fmaf(dS[1][jj], sv[jj], dth);
-      }
+      // dS_t (the full cotangent of S_t) replaces W_{t-1} in scratch for the
+      // momentum-scan pass below; this thread read that row for dalpha above.
+      st32(Wsave + (size_t)r * DE + e0 * D + dc, dS[0]);
+      st32(Wsave + (size_t)r * DE + e1 * D + dc, dS[1]);
       PROF_T(twin)
-      const int i0 = win ? max(0, r - P.omega + 1) : r;
-      for (int ib = i0; ib <= r; ib += 8) {
-        float fa[8], fb[8];  // this block's row factors, loaded together (one L2 round trip)
+      {  // momentum-scan cotangents of token r (memory_layer.py:256-299, Omega window 233-253)
+        const float ci = -g.e * sc;
+        const bool out = r + Om < cs;
+        const float co = out ? s.gate[1][r + Om] * sc : 0.f;
+        const float* pb = Wsave + (size_t)(out ? r + Om : r) * DE + dc;
+        const float gi = win ? g.g : 1.f;
+        const float f0 = Fm[r * E + e0], f1 = Fm[r * E + e1];
+        const int io = r - Om;
+        const float go = io >= 0 ? (win ? s.gate[3][io] : 1.f) : 0.f;
+        const float* gr = &s.Gc[r * D + dc];
+        const float* gq = &s.Gc[max(io, 0) * D + dc];
+        float rg[2], dm = 0.f;
 #pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8) {
-          const int i = ib + k8;
-          fa[k8] = i <= r ? Fm[i * E + e0] : 0.f;
-          fb[k8] = i <= r ? Fm[i * E + e1] : 0.f;
-        }
-#pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8) {
-          const int i = ib + k8;
-          if (i > r) break;
-          const float gi = win ? s.gate[3][i] : 1.f;
-          const float cf = -g.e * sc * gi;
-          const float f0 = fa[k8], f1 = fb[k8];
-          float gv[32], cv[32];
-          ld32(&s.Gc[i * D + dc], gv);
-          float rv0 = 0.f, rv1 = 0.f;
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t cr = tm + lane_off + 64 * h + dc;
+          float rv[32], bv[32];
+          tmem_ld32(cr + VJ_R, rv);
+          ld32(pb + (h ? e1 : e0) * D, bv);
+          tmem_wait_ld();
+          float acc = 0.f;
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
-            rv0 = fmaf(dS[0][jj], gv[jj], rv0);
-            rv1 = fmaf(dS[1][jj], gv[jj], rv1);
-            cv[jj] = fmaf(dS[0][jj], f0, dS[1][jj] * f1);
+            rv[jj] = fmaf(co, bv[jj], fmaf(ci, dS[h][jj], rv[jj]));  // R_r = R_{r+1} + c_r dS_r - c_{r+Om} dS_{r+Om}
+            acc = fmaf(rv[jj], gr[jj], acc);
           }
-          float ip = fmaf(f0, rv0, f1 * rv1);
+          rg[h] = acc;
+          tmem_st32(cr + VJ_R, rv);
+          float mv[32];
+          tmem_ld32(cr + VJ_M, mv);
+          tmem_wait_ld();
+          const float fr = -gi * (h ? f1 : f0), fo = io >= 0 ? go * Fm[io * E + (h ? e1 : e0)] : 0.f;
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ip += __shfl_xor_sync(0xffffffffu, ip, o);
-          if (l == 0) atomicAdd(&s.ipacc[i], ip);
-          red_add(&w.dF[rank][i * E + e0], cf * rv0);
-          red_add(&w.dF[rank][i * E + e1], cf * rv1);
+          for (int jj = 0; jj < 32; ++jj) {
+            dm = fmaf(dS[h][jj], mv[jj], dm);
+            mv[jj] = fmaf(fo, gq[jj], fmaf(fr, gr[jj], mv[jj]));  // M_{r-1}
+          }
+          tmem_st32(cr + VJ_M, mv);
+        }
+        tmem_wait_st();
+        // dF_r = gamma_r R_r g_r ; dG_r = gamma_r R_r^T f_r ; dgamma_r = f_r^T R_r g_r ; deta_r = -2/D <dS_r, M_r>
+        red_add(&w.dF[rank][r * E + e0], gi * rg[0]);
+        red_add(&w.dF[rank][r * E + e1], gi * rg[1]);
+        {
+          float cv[32], rv[32];
+          tmem_ld32(tm + lane_off + VJ_R + dc, cv);
+          tmem_ld32(tm + lane_off + VJ_R + 64 + dc, rv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) cv[jj] = fmaf(cv[jj], f0, rv[jj] * f1);
           const float part = warp_reduce_scatter32(cv);
-          red_add(&w.dG[rank][i * D + dc + l], cf * part);
+          red_add(&w.dG[rank][r * D + dc + l], gi * part);
+        }
+        float ip = fmaf(f0, rg[0], f1 * rg[1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          ip += __shfl_xor_sync(0xffffffffu, ip, o);
+          dm += __shfl_xor_sync(0xffffffffu, dm, o);
+        }
+        if (l == 0) {
+          red_add(&w.scal[MAXCS + r], -sc * dm);
+          if (win) red_add(&w.scal[3 * MAXCS + r], ip);
         }
       }
       PROF_ADD(7, twin)
-      dal = block_sum_epi(dal, s.red);
-      dth = block_sum_epi(dth, s.red);  // also orders the ipacc atomics before the reads below
-      if (tid >= i0 && tid <= r) {
-        const float ip = s.ipacc[tid];
-        const float gi = win ? s.gate[3][tid] : 1.f;
-        red_add(&w.scal[MAXCS + r], -sc * gi * ip);          // deta_t
-        if (win) red_add(&w.scal[3 * MAXCS + tid], -g.e * sc * ip);  // dgamma_i
-      }
-      if (tid == 0) {
-        red_add(&w.scal[r], dal);
-        red_add(&w.scal[2 * MAXCS + r], dth);
-      }
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         dW[0][jj] *= g.a;
         dW[1][jj] *= g.a;
-        dS[0][jj] *= g.t;
-        dS[1][jj] *= g.t;
       }
     }
+    {  // dtheta_0 = <dS_0, S_{-1}>, then the decay by theta_0 that leaves the chunk
+      float xo[2][32];
+      ld32(Ssave + e0 * D + dc, xo[0]);
+      ld32(Ssave + e1 * D + dc, xo[1]);
+      theta_step(dS, xo, -1, cs, s.gate[2], w.scal, l);
+    }
 
+    // carry cotangent of chunk c-1 (before phase D's frozen-pass terms) parked in
+    // this chain's slot; phase D reloads it (same thread, same addresses)
+    float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
+    st32(cq + e0 * D + dc, dW[0]);
+    st32(cq + e1 * D + dc, dW[1]);
+    st32(cq + DE + e0 * D + dc, dS[0]);
+    st32(cq + DE + e1 * D + dc, dS[1]);
     PROF_ADD(4, tC)
     PROF_T(tD)
     // ================= D: frozen-state pass backward =================
     __threadfence();
     cluster_sync();  // both ranks' window accumulations are complete
+    ld32(cq + e0 * D + dc, dW[0]);
+    ld32(cq + e1 * D + dc, dW[1]);
+    ld32(cq + DE + e0 * D + dc, dS[0]);
+    ld32(cq + DE + e1 * D + dc, dS[1]);
     {
       // W1^T, then W2, staged in the 64 KB of A/B'/Ps/Sym tiles (free in this phase)
       float* Wst = (float*)s.Ah;
@@ -903,7 +981,6 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       for (int jj = 0; jj < 32; ++jj) dW[0][jj] = dW[1][jj] = dS[0][jj] = dS[1][jj] = 0.f;
     }
     if (c > 0) {
-      float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
       st32(cq + e0 * D + dc, dW[0]);
       st32(cq + e1 * D + dc, dW[1]);
       st32(cq + DE + e0 * D + dc, dS[0]);
