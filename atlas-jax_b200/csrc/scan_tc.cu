@@ -311,23 +311,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
           Sv[1][jj] *= th;
         }
         const int i0 = win ? max(0, r - P.omega + 1) : r;
-        for (int i = i0; i <= r; ++i) {
-          const float wgt = -et * sc * (win ? s.gate[3][i] : 1.f);
-          const float f0 = wgt * Fg[i * E + e0], f1 = wgt * Fg[i * E + e1];
-          const float4* g4 = (const float4*)&s.G[i * D + dc];
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            float4 g = g4[j4];
-            Sv[0][4 * j4 + 0] = fmaf(f0, g.x, Sv[0][4 * j4 + 0]);
-            Sv[0][4 * j4 + 1] = fmaf(f0, g.y, Sv[0][4 * j4 + 1]);
-            Sv[0][4 * j4 + 2] = fmaf(f0, g.z, Sv[0][4 * j4 + 2]);
-            Sv[0][4 * j4 + 3] = fmaf(f0, g.w, Sv[0][4 * j4 + 3]);
-            Sv[1][4 * j4 + 0] = fmaf(f1, g.x, Sv[1][4 * j4 + 0]);
-            Sv[1][4 * j4 + 1] = fmaf(f1, g.y, Sv[1][4 * j4 + 1]);
-            Sv[1][4 * j4 + 2] = fmaf(f1, g.z, Sv[1][4 * j4 + 2]);
-            Sv[1][4 * j4 + 3] = fmaf(f1, g.w, Sv[1][4 * j4 + 3]);
-          }
-        }
+        momentum_window(Sv, Fg, s.G, s.gate[3], i0, r, -et * sc, win, e0, e1, dc);
         PROF_ADD(2, ttok)
         PROF_T(tnorm)
         // ---- Frobenius normalisation (memory_layer.py:55-56) ----

@@ -240,6 +240,21 @@ namespace tc {
 namespace bwd {
 
 
+// v[j] = scale * (hi + lo) of logical columns [c0, c0+32) of row r of a stacked tile.
+__device__ __forceinline__ void load_stk32(const uint8_t* t, int r, int c0, float scale, float* v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t off = cm_off(r, stk(c0 + 8 * k), XC);
+    const uint4 h = *(const uint4*)(t + off), lo = *(const uint4*)(t + off + XLO);
+    const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      v[8 * k + 2 * m] = scale * (__uint_as_float(hw[m] << 16) + __uint_as_float(lw[m] << 16));
+      v[8 * k + 2 * m + 1] = scale * (__uint_as_float(hw[m] & 0xFFFF0000u) + __uint_as_float(lw[m] & 0xFFFF0000u));
+    }
+  }
+}
+
 // Deferred step of the momentum recurrence S_u = theta_u S_{u-1} + ... for u = r + 1:
 // with dS = dS_u (the full cotangent of S_u) and xo = S_{u-1} (= S_r, which the
 // normalisation VJP of token r reads anyway), adds dtheta_u = <dS_u, S_{u-1}>
@@ -381,6 +396,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         if (wp == 8 && P.ns_steps > 0) {
           sl[0].ns = P.pe_ste ? nullptr : w.ns[rank] + (size_t)r0 * 5 * NS_STEP_BYTES;
           sl[1].ns = P.pe_ste ? nullptr : sl[0].ns + 5 * NS_STEP_BYTES;
+#ifdef ATLAS_PROF_NOSAVE  // profiling builds only: phase B without tile saves
+          sl[0].ns = sl[1].ns = nullptr;
+#endif
           pe_produce(sl, B, n, P.ns_steps, &s.bad);
         }
         for (int jp = 0; jp < n; ++jp) cluster_sync();  // read-out exchange
@@ -448,17 +466,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           Sv[1][jj] *= th;
         }
         const int i0 = win ? max(0, r - P.omega + 1) : r;
-        for (int i = i0; i <= r; ++i) {
-          const float wgt = -et * sc * (win ? s.gate[3][i] : 1.f);
-          const float f0 = wgt * Fm[i * E + e0], f1 = wgt * Fm[i * E + e1];
-          float gv[32];
-          ld32(&s.Gc[i * D + dc], gv);
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            Sv[0][jj] = fmaf(f0, gv[jj], Sv[0][jj]);
-            Sv[1][jj] = fmaf(f1, gv[jj], Sv[1][jj]);
-          }
-        }
+        momentum_window(Sv, Fm, s.Gc, s.gate[3], i0, r, -et * sc, win, e0, e1, dc);
         st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
         st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
         float ss = 0.f;
@@ -483,6 +491,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         // keep every step's operand tiles of these tokens for the VJP in phase C
         sl[0].ns = w.ns[rank] + (size_t)r0 * 5 * NS_STEP_BYTES;
         sl[1].ns = sl[0].ns + 5 * NS_STEP_BYTES;
+#ifdef ATLAS_PROF_NOSAVE  // profiling builds only: phase B without tile saves
+        sl[0].ns = sl[1].ns = nullptr;
+#endif
         if (P.pe_ste) sl[0].ns = sl[1].ns = nullptr;
         if (!pe_consume(sl, B, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
           set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
@@ -603,17 +614,29 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         }
       }
     }
+    // q, dy and p / dz of the next token are loaded one token ahead
+    float nq = 0.f, ndy = 0.f, nv0, nv1;
+    auto load_next = [&](int rn) {
+      const int tn = c * cs + rn;
+      if (tid < D) {
+        const size_t o = (((size_t)b * T + tn) * H + hh) * D + tid;
+        nq = tn < T ? ld_act((const TA*)a.q, o) : 0.f;
+        ndy = tn < T ? ld_act((const TA*)a.dy, o) : 0.f;
+      }
+      nv0 = vec[rn * E + e0];
+      nv1 = vec[rn * E + e1];
+    };
+    load_next(cs - 1);
     for (int r = cs - 1; r >= 0; --r) {
-      const int t = c * cs + r;
       const Gates g = {s.gate[0][r], s.gate[1][r], s.gate[2][r], s.gate[3][r]};
       if (tid < D) {
-        const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
-        s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
-        s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
+        s.qv[tid] = nq;
+        s.dyv[tid] = ndy;
       }
+      const float v0 = nv0, v1 = nv1;
+      if (r > 0) load_next(r - 1);
       epi_sync();
       {  // read-out: rank 0 dW1 += dy p^T (tile: p[e] dy[d]); rank 1 dW2 += dz q^T
-        const float v0 = vec[r * E + e0], v1 = vec[r * E + e1];
         const float* xv = rank ? s.qv : s.dyv;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -667,9 +690,10 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           PROF_T(tns)
           bool ok = true;
           uint8_t* nscur = w.ns[rank] + (size_t)r * 5 * NS_STEP_BYTES;
-          if (!s.bad) {  // last step's tiles of token r (saved in phase B)
+          if (!s.bad) {  // last step's tiles of token r (saved in phase B; issued here for the
+                         // chunk's first token, after the previous token's normalisation otherwise)
             epi_sync();
-            if (tid == 0) {
+            if (tid == 0 && r == cs - 1) {
               const uint8_t* o = nscur + (size_t)(P.ns_steps - 1) * NS_STEP_BYTES;
               mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
               bulk_g2s(s.Xh, o, XT_BYTES, &s.bar_ld);
@@ -696,7 +720,10 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             PROF_T(tcp)
             PROF_ADD(9, tcp)
             // P = G~^T X~ (stack), this lane's 16 entries P[rr][d0 + j]
+            PROF_T(tm0)
             ok = vjp_mma(s, B, tm, 0, &s.bad) && ok;
+            PROF_ADD(10, tm0)
+            PROF_T(tep0)
             float pv[16];
             {
               float v[64];
@@ -712,8 +739,12 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) pv[jj] += Pf[pf_idx(d0 + jj, rr)];  // Ps = P + P^T
             store_stk<16>(s.Ph, rr, d0, pv);
+            PROF_ADD(13, tep0)
             // Sym = b Ps + c (Ps A + A Ps)
+            PROF_T(tm1)
             ok = vjp_mma(s, B, tm, 1, &s.bad) && ok;  // Ps A + A Ps (stack)
+            PROF_ADD(10, tm1)
+            PROF_T(tep1)
             {
               float v[64], yv[16];
               tmem_ld64(tm + lane_off + VJ_S + 2 * dc, v);
@@ -724,8 +755,12 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
               store_split8(s.Yh, s.Yl, cm_off(rr, d0, D), yv);
               store_split8(s.Yh, s.Yl, cm_off(rr, d0 + 8, D), yv + 8);
             }
+            PROF_ADD(14, tep1)
           // dX~ = G~ B' + X~ Sym
+            PROF_T(tm2)
             ok = vjp_mma(s, B, tm, 2, &s.bad) && ok;  // G~ B' + X~ Sym
+            PROF_ADD(10, tm2)
+            PROF_T(tep2)
             if (st > 0 && tid == 0 && !s.bad) {  // prefetch step st-1's tiles; X, A, B' are free now
               const uint8_t* o = nscur + (size_t)(st - 1) * NS_STEP_BYTES;
               mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
@@ -743,6 +778,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
               store_stk<32>(s.Gh, e0, dc, gx[0]);
               store_stk<32>(s.Gh, e1, dc, gx[1]);
             }
+            PROF_ADD(15, tep2)
           }
           PROF_ADD(6, tvjp)
           if (!ok && !s.bad) {
@@ -757,13 +793,25 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           }
         }
         // X0 = S / kappa, kappa = 1.01 sqrt(sum S^2 + 1e-12) + 1e-6
-        ld32(St + e0 * D + dc, xo[0]);
-        ld32(St + e1 * D + dc, xo[1]);
+        if (P.ns_steps > 0) {  // S_t = kappa X0, X0 still resident (stacked hi + lo, ~2^-17 relative)
+          load_stk32(s.Xh, e0, dc, kap, xo[0]);
+          load_stk32(s.Xh, e1, dc, kap, xo[1]);
+        } else {
+          ld32(St + e0 * D + dc, xo[0]);
+          ld32(St + e1 * D + dc, xo[1]);
+        }
         theta_step(dS, xo, r, cs, s.gate[2], w.scal, l);
         float dot = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dot = fmaf(gx[0][jj], xo[0][jj], fmaf(gx[1][jj], xo[1][jj], dot));
-        dot = block_sum_epi(dot, s.red);
+        dot = block_sum_epi(dot, s.red);  // every thread is done reading the X0 tiles
+        if (P.ns_steps > 0 && r > 0 && tid == 0 && !s.bad) {  // next token's last-step tiles
+          const uint8_t* o = w.ns[rank] + ((size_t)(r - 1) * 5 + (P.ns_steps - 1)) * NS_STEP_BYTES;
+          fence_async_smem();
+          mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
+          bulk_g2s(s.Xh, o, 2 * XT_BYTES, &s.bar_ld);
+          bulk_g2s(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld);
+        }
         const float coef = dot / (kap * kap) * 1.01f / nrm;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {

@@ -126,6 +126,41 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
   tmem_ld16(taddr + 48, v + 48);
 }
 
+// Momentum window term of one token (memory_layer.py:233-253, 543-560):
+//   S[e][d] += wgt * sum_{i = i0..r} gamma_i F[i][e] G[i][d]
+// for this thread's rows e0, e1 and columns dc..dc+31.  F (global, L2-resident)
+// is read eight window entries at a time so their loads overlap.
+__device__ __forceinline__ void momentum_window(float (*Sv)[32], const float* F, const float* G, const float* gam,
+                                                int i0, int r, float wgt, bool win, int e0, int e1, int dc) {
+  for (int ib = i0; ib <= r; ib += 8) {
+    float fa[8], fb[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = min(ib + k, r);
+      const float c = ib + k <= r ? wgt * (win ? gam[i] : 1.f) : 0.f;
+      fa[k] = c * F[i * E + e0];
+      fb[k] = c * F[i * E + e1];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (ib + k > r) break;
+      const float4* g4 = (const float4*)&G[(ib + k) * D + dc];
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 g = g4[j4];
+        Sv[0][4 * j4 + 0] = fmaf(fa[k], g.x, Sv[0][4 * j4 + 0]);
+        Sv[0][4 * j4 + 1] = fmaf(fa[k], g.y, Sv[0][4 * j4 + 1]);
+        Sv[0][4 * j4 + 2] = fmaf(fa[k], g.z, Sv[0][4 * j4 + 2]);
+        Sv[0][4 * j4 + 3] = fmaf(fa[k], g.w, Sv[0][4 * j4 + 3]);
+        Sv[1][4 * j4 + 0] = fmaf(fb[k], g.x, Sv[1][4 * j4 + 0]);
+        Sv[1][4 * j4 + 1] = fmaf(fb[k], g.y, Sv[1][4 * j4 + 1]);
+        Sv[1][4 * j4 + 2] = fmaf(fb[k], g.z, Sv[1][4 * j4 + 2]);
+        Sv[1][4 * j4 + 3] = fmaf(fb[k], g.w, Sv[1][4 * j4 + 3]);
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -367,11 +402,13 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
 
 // Producer (one whole warp).  Mirrors pe_consume's schedule; when q.ns is set it
 // saves the tile just published (X_st before the Gram, A_st before A*A, B'_st
-// before X~ B'^T) with a bulk copy.  A tile is rewritten by the epilogue two or
-// three phases after it was saved, so before committing the Gram and A*A groups
-// the producer lets all but its newest copy finish reading shared memory: the
-// copies of X_st (rewritten by the X~ B'^T epilogue), A_{st-1} and B'_{st-1}
-// are then complete before their tiles change.
+// before X~ B'^T) with one bulk copy (one bulk group) per slot and phase.  A saved
+// tile is next rewritten by the epilogue that follows the commit two phases
+// later (X_st by the X~ B'^T epilogue, A_st by the next Gram epilogue, B'_st by
+// the next A*A epilogue).  By that commit the lead lane has issued exactly
+// 2 * nslots newer groups, so waiting until at most 2 * nslots groups are still
+// reading shared memory before every commit keeps each copy ahead of its
+// overwrite with the most slack.
 static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad) {
   const int P = 3 * steps;
   const bool lead = (threadIdx.x & 31) == 0;
@@ -396,7 +433,12 @@ static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nsl
       __syncwarp();
       if (!*bad) {
         pe_issue(q, type);
-        if (q.ns && lead && type < 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        if (q.ns && lead) {
+          if (nslots == 2)
+            asm volatile("cp.async.bulk.wait_group.read 4;" ::: "memory");
+          else
+            asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
+        }
         __syncwarp();
         mma_commit(B.done[s]);
       }
