@@ -183,7 +183,7 @@ struct KArgs {
 };
 
 #ifdef ATLAS_PHASE_PROF
-__device__ unsigned long long g_prof_fwd[16];
+__device__ unsigned long long g_prof_fwd[24];
 #endif
 
 template <typename TA>
@@ -332,6 +332,13 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
         }
         PROF_ADD(3, tnorm)
       }
+      // q of the pair, loaded before Polar Express so the read-out does not wait on it
+      float pq[2] = {0.f, 0.f};
+      if (tid < D)
+        for (int j = 0; j < n; ++j) {
+          const int t = c * cs + r0 + j;
+          if (t < T) pq[j] = ld_act((const TA*)a.q, (((size_t)b * T + t) * H + hh) * D + tid);
+        }
       // ---- Polar Express (memory_layer.py:43-71) for the pair, interleaved ----
       if (P.ns_steps > 0 && !pe_consume(sl, B, n, P.ns_steps, &s.bad, PROF_PTR) && !s.bad) {
         set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
@@ -359,7 +366,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
           }
         }
         // ---- read-out y = q + W1 gelu(W2 q)  (memory_layer.py:592-595) ----
-        if (tid < D) s.qv[tid] = t < T ? ld_act((const TA*)a.q, (((size_t)b * T + t) * H + hh) * D + tid) : 0.f;
+        if (tid < D) s.qv[tid] = j ? pq[1] : pq[0];
         epi_sync();
         if (rank == 1) {
           float z0 = 0.f, z1 = 0.f;
@@ -508,8 +515,8 @@ cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
 #ifdef ATLAS_PHASE_PROF
 // Instrumented builds only: read and clear the forward kernel's phase cycle counters.
 extern "C" int atlas_debug_prof_fwd(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, atlas::tc::g_prof_fwd, 16 * sizeof(unsigned long long));
-  unsigned long long z[16] = {};
+  cudaMemcpyFromSymbol(out, atlas::tc::g_prof_fwd, 24 * sizeof(unsigned long long));
+  unsigned long long z[24] = {};
   return cudaMemcpyToSymbol(atlas::tc::g_prof_fwd, z, sizeof(z)) == cudaSuccess ? 0 : 3;
 }
 #endif

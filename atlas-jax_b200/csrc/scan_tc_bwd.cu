@@ -323,7 +323,7 @@ __device__ __forceinline__ bool vjp_mma(Smem& s, PEBars& B, uint32_t tm, int g, 
 }
 
 #ifdef ATLAS_PHASE_PROF
-__device__ unsigned long long g_prof_bwd[16];
+__device__ unsigned long long g_prof_bwd[24];
 #endif
 
 template <typename TA>
@@ -368,6 +368,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   fence_after();
   const uint32_t tm = s.tmem;
   uint32_t phase_ld = 0;
+  const uint64_t pol_ef = l2_evict_first_policy();  // saved Newton-Schulz tiles: read once
   PROF_INIT
   PESlot sl[2];
   // stacked X~ / A tiles: the lo part sits XLO bytes after the hi part (the
@@ -457,6 +458,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     for (int r0 = 0; r0 < cs; r0 += npair) {
       const int n = min(npair, cs - r0);
       float inv0 = 0.f;
+      PROF_T(tb16)
       for (int jp = 0; jp < n; ++jp) {
         const int r = r0 + jp;
         const float et = s.gate[1][r], th = s.gate[2][r];
@@ -467,8 +469,10 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         }
         const int i0 = win ? max(0, r - P.omega + 1) : r;
         momentum_window(Sv, Fm, s.Gc, s.gate[3], i0, r, -et * sc, win, e0, e1, dc);
-        st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
-        st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
+        if (P.pe_ste || P.ns_steps == 0) {  // otherwise phase C reads S_t from the X0 tiles
+          st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
+          st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
+        }
         float ss = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
@@ -487,6 +491,18 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           store_stk<32>(sl[jp].Xh, e1, dc, xv);
         }
       }
+      PROF_ADD(16, tb16)
+      // q and dy of the pair, loaded before Polar Express so the read-out does not wait on them
+      float pq[2] = {0.f, 0.f}, pdy[2] = {0.f, 0.f};
+      if (tid < D)
+        for (int jp = 0; jp < n; ++jp) {
+          const int t = c * cs + r0 + jp;
+          if (t < T) {
+            const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
+            pq[jp] = ld_act((const TA*)a.q, o);
+            pdy[jp] = ld_act((const TA*)a.dy, o);
+          }
+        }
       if (P.ns_steps > 0) {
         // keep every step's operand tiles of these tokens for the VJP in phase C
         sl[0].ns = w.ns[rank] + (size_t)r0 * 5 * NS_STEP_BYTES;
@@ -500,6 +516,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           s.bad = 1;
         }
       }
+      PROF_T(tb17)
       for (int jp = 0; jp < n; ++jp) {
         const int r = r0 + jp, t = c * cs + r;
         const float al = s.gate[0][r];
@@ -524,9 +541,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         }
         // read-out backward pieces (memory_layer.py:592-595)
         if (tid < D) {
-          const size_t o = (((size_t)b * T + t) * H + hh) * D + tid;
-          s.qv[tid] = t < T ? ld_act((const TA*)a.q, o) : 0.f;
-          s.dyv[tid] = t < T ? ld_act((const TA*)a.dy, o) : 0.f;
+          s.qv[tid] = jp ? pq[1] : pq[0];
+          s.dyv[tid] = jp ? pdy[1] : pdy[0];
         }
         epi_sync();
         {
@@ -566,6 +582,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         }
         epi_sync();
       }
+      PROF_ADD(17, tb17)
     }
 
     PROF_ADD(3, tB)
@@ -628,6 +645,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     };
     load_next(cs - 1);
     for (int r = cs - 1; r >= 0; --r) {
+      PROF_T(tc18)
       const Gates g = {s.gate[0][r], s.gate[1][r], s.gate[2][r], s.gate[3][r]};
       if (tid < D) {
         s.qv[tid] = nq;
@@ -649,24 +667,12 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + e0 * D));
         asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + e1 * D));
       }
-      if (r > 0) {  // W_{r-2} for the next token's dalpha
-        const float* nw = Wsave + (size_t)(r - 1) * DE + dc;
+      {  // W_{t-1} of this token (dalpha, after the VJP) into L2
+        const float* nw = Wsave + (size_t)r * DE + dc;
         asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e0 * D));
         asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e1 * D));
       }
-      float dal = 0.f;
-      {
-        float wv[32];
-        ld32(Wsave + (size_t)r * DE + e0 * D + dc, wv);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[0][jj], wv[jj], dal);
-        ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[1][jj], wv[jj], dal);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dal += __shfl_xor_sync(0xffffffffu, dal, o);
-        if (l == 0) red_add(&w.scal[r], dal);  // dalpha_t = <dW_t, W_{t-1}>
-      }
+      PROF_ADD(18, tc18)
       // ---- Polar Express VJP ----
       if (P.pe_ste || P.ns_steps == 0) {
         if (P.pe_ste) {
@@ -696,12 +702,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             if (tid == 0 && r == cs - 1) {
               const uint8_t* o = nscur + (size_t)(P.ns_steps - 1) * NS_STEP_BYTES;
               mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
-              bulk_g2s(s.Xh, o, XT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Xl, o + XT_BYTES, XT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Ah, o + 2 * XT_BYTES, AT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Al, o + 2 * XT_BYTES + AT_BYTES, AT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES, &s.bar_ld);
+              bulk_g2s_hint(s.Xh, o, 2 * XT_BYTES, &s.bar_ld, pol_ef);
+              bulk_g2s_hint(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld, pol_ef);
             }
             if (!mbar_wait(&s.bar_ld, phase_ld)) ok = false;
             phase_ld ^= 1;
@@ -744,6 +746,13 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             PROF_T(tm1)
             ok = vjp_mma(s, B, tm, 1, &s.bad) && ok;  // Ps A + A Ps (stack)
             PROF_ADD(10, tm1)
+            // A and B' (read by this group and by group 0's G~ B') are free: start
+            // step st-1's tiles with them; X~ follows once group 2 has read it
+            if (st > 0 && tid == 0 && !s.bad) {
+              const uint8_t* o = nscur + (size_t)(st - 1) * NS_STEP_BYTES;
+              mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
+              bulk_g2s_hint(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld, pol_ef);
+            }
             PROF_T(tep1)
             {
               float v[64], yv[16];
@@ -761,16 +770,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             ok = vjp_mma(s, B, tm, 2, &s.bad) && ok;  // G~ B' + X~ Sym
             PROF_ADD(10, tm2)
             PROF_T(tep2)
-            if (st > 0 && tid == 0 && !s.bad) {  // prefetch step st-1's tiles; X, A, B' are free now
-              const uint8_t* o = nscur + (size_t)(st - 1) * NS_STEP_BYTES;
-              mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
-              bulk_g2s(s.Xh, o, XT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Xl, o + XT_BYTES, XT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Ah, o + 2 * XT_BYTES, AT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Al, o + 2 * XT_BYTES + AT_BYTES, AT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Bh, o + 2 * XT_BYTES + 2 * AT_BYTES, AT_BYTES, &s.bar_ld);
-              bulk_g2s(s.Bl, o + 2 * XT_BYTES + 3 * AT_BYTES, AT_BYTES, &s.bar_ld);
-            }
+            if (st > 0 && tid == 0 && !s.bad)  // rest of step st-1's tiles: X~ is free now
+              bulk_g2s_hint(s.Xh, nscur + (size_t)(st - 1) * NS_STEP_BYTES, 2 * XT_BYTES, &s.bar_ld, pol_ef);
             tmem_ld32(tm + lane_off + VJ_X + dc, gx[0]);
             tmem_ld32(tm + lane_off + VJ_X + 64 + dc, gx[1]);
             tmem_wait_ld();
@@ -793,6 +794,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           }
         }
         // X0 = S / kappa, kappa = 1.01 sqrt(sum S^2 + 1e-12) + 1e-6
+        PROF_T(tc19)
         if (P.ns_steps > 0) {  // S_t = kappa X0, X0 still resident (stacked hi + lo, ~2^-17 relative)
           load_stk32(s.Xh, e0, dc, kap, xo[0]);
           load_stk32(s.Xh, e1, dc, kap, xo[1]);
@@ -809,8 +811,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           const uint8_t* o = w.ns[rank] + ((size_t)(r - 1) * 5 + (P.ns_steps - 1)) * NS_STEP_BYTES;
           fence_async_smem();
           mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
-          bulk_g2s(s.Xh, o, 2 * XT_BYTES, &s.bar_ld);
-          bulk_g2s(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld);
+          bulk_g2s_hint(s.Xh, o, 2 * XT_BYTES, &s.bar_ld, pol_ef);
+          bulk_g2s_hint(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld, pol_ef);
         }
         const float coef = dot / (kap * kap) * 1.01f / nrm;
 #pragma unroll
@@ -818,6 +820,19 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           dS[0][jj] += gx[0][jj] * inv - coef * xo[0][jj];
           dS[1][jj] += gx[1][jj] * inv - coef * xo[1][jj];
         }
+        PROF_ADD(19, tc19)
+      }
+      {  // dalpha_t = <dW_t, W_{t-1}>  (dW_t is unchanged by the VJP above)
+        float dal = 0.f, wv[32];
+        ld32(Wsave + (size_t)r * DE + e0 * D + dc, wv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[0][jj], wv[jj], dal);
+        ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[1][jj], wv[jj], dal);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dal += __shfl_xor_sync(0xffffffffu, dal, o);
+        if (l == 0) red_add(&w.scal[r], dal);
       }
       // dS_t (the full cotangent of S_t) replaces W_{t-1} in scratch for the
       // momentum-scan pass below; this thread read that row for dalpha above.
@@ -1123,8 +1138,8 @@ cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t st) {
 #ifdef ATLAS_PHASE_PROF
 // Instrumented builds only: read and clear the backward kernel's phase cycle counters.
 extern "C" int atlas_debug_prof_bwd(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, atlas::tc::bwd::g_prof_bwd, 16 * sizeof(unsigned long long));
-  unsigned long long z[16] = {};
+  cudaMemcpyFromSymbol(out, atlas::tc::bwd::g_prof_bwd, 24 * sizeof(unsigned long long));
+  unsigned long long z[24] = {};
   return cudaMemcpyToSymbol(atlas::tc::bwd::g_prof_bwd, z, sizeof(z)) == cudaSuccess ? 0 : 3;
 }
 #endif

@@ -247,12 +247,12 @@ __device__ __forceinline__ void mma_stack(uint32_t tmd, const uint8_t* z, const 
 // Optional phase timers (build with -DATLAS_PHASE_PROF; thread 0 accumulates
 // clock64() deltas into a shared array; off in the product build).
 #ifdef ATLAS_PHASE_PROF
-#define PROF_DECL __shared__ unsigned long long s_prof[16];
-#define PROF_INIT if (threadIdx.x < 16) s_prof[threadIdx.x] = 0;
+#define PROF_DECL __shared__ unsigned long long s_prof[24];
+#define PROF_INIT if (threadIdx.x < 24) s_prof[threadIdx.x] = 0;
 #define PROF_T(v) long long v = clock64();
 #define PROF_ADD(slot, v) if (threadIdx.x == 0) s_prof[slot] += clock64() - v;
 #define PROF_PTR s_prof
-#define PROF_FLUSH(g) if (threadIdx.x < 16) atomicAdd(&g[threadIdx.x], s_prof[threadIdx.x]);
+#define PROF_FLUSH(g) if (threadIdx.x < 24) atomicAdd(&g[threadIdx.x], s_prof[threadIdx.x]);
 #else
 #define PROF_DECL
 #define PROF_INIT
@@ -412,6 +412,7 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
 static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nslots, int steps, volatile int* bad) {
   const int P = 3 * steps;
   const bool lead = (threadIdx.x & 31) == 0;
+  const uint64_t pol = l2_evict_first_policy();  // saved tiles are read once, much later
   bool ok = true;
   for (int p = 0; p < P; ++p) {
     const int type = p % 3, st = p / 3;
@@ -423,11 +424,11 @@ static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nsl
       if (q.ns && lead) {
         uint8_t* o = q.ns + (size_t)st * NS_TILE_BYTES;
         if (type == 0)
-          bulk_s2g(o, q.Xh, 2 * XT_BYTES);
+          bulk_s2g_hint(o, q.Xh, 2 * XT_BYTES, pol);
         else if (type == 1)
-          bulk_s2g(o + 2 * XT_BYTES, q.Ah, 2 * AT_BYTES);
+          bulk_s2g_hint(o + 2 * XT_BYTES, q.Ah, 2 * AT_BYTES, pol);
         else
-          bulk_s2g(o + 2 * XT_BYTES + 2 * AT_BYTES, q.Bh, 2 * AT_BYTES);
+          bulk_s2g_hint(o + 2 * XT_BYTES + 2 * AT_BYTES, q.Bh, 2 * AT_BYTES, pol);
         bulk_commit();
       }
       __syncwarp();
