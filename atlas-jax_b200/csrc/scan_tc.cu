@@ -103,6 +103,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
   float* errb = (float*)(s.slot[1] + MAXCS * D * 4);   // cs x D  (16 KB)
   float* W1s = (float*)(s.slot[1] + 2 * MAXCS * D * 4); // W1^T staged (64 KB)
   const int tid = threadIdx.x;
+  const uint64_t pol = l2_evict_last_policy();  // Fg is re-read by every token of the chunk
   for (int i = tid; i < DE / 4; i += NT) ((float4*)W1s)[i] = ((const float4*)W1t)[i];
   for (int i = tid; i < cs * D; i += NT) {
     int r = i / D, d = i % D, t = c * cs + r;
@@ -127,7 +128,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
       for (int d = 0; d < D; ++d) hv = fmaf(w[d], kbuf[r * D + d], hv);
       const float av = gelu_tanh(hv);
       actb[r * E + e] = av;
-      Fg[r * E + e] = rank ? hv : av;  // rank 1 keeps h for gelu'(h)
+      st_hint(&Fg[r * E + e], rank ? hv : av, pol);  // rank 1 keeps h for gelu'(h)
     }
   }
   epi_sync();
@@ -164,7 +165,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
       float rv = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) rv = fmaf(w[d], errb[r * D + d], rv);
-      Fg[r * E + e] = rv * gelu_erf_prime(Fg[r * E + e]);
+      st_hint(&Fg[r * E + e], rv * gelu_erf_prime(Fg[r * E + e]), pol);
     }
   }
   for (int i = tid; i < cs * D; i += NT) s.G[i] = rank ? kbuf[i] : errb[i];

@@ -159,13 +159,15 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
   const float* W1t = slot;
   const float* W2 = slot + 2 * DE;
   float* kb = pf_base(s);  // cs x D
+  // the frozen-pass arrays are re-read by every token of phases B and C: keep them in L2
+  const uint64_t pol = l2_evict_last_policy();
   if (rank == 0) {
     const TA* kp = (const TA*)a.k;
     for (int i = tid; i < cs * D; i += NT) {
       int r = i / D, d = i % D, t = c * cs + r;
       float kv = t < T ? ld_act(kp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
       kb[i] = kv;
-      w.k[i] = kv;
+      st_hint(&w.k[i], kv, pol);
     }
     epi_sync();
     {
@@ -177,9 +179,9 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
         float hv = 0.f;
 #pragma unroll
         for (int d = 0; d < D; ++d) hv = fmaf(wr[d], kb[r * D + d], hv);
-        w.h[r * E + e] = hv;
+        st_hint(&w.h[r * E + e], hv, pol);
         const float av = gelu_tanh(hv);
-        w.act[r * E + e] = av;
+        st_hint(&w.act[r * E + e], av, pol);
         ((float*)s.Gh)[r * E + e] = av;  // smem copy for the err pass (G~ tiles' 64 KB are free here)
       }
     }
@@ -207,7 +209,7 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
         int r = grp * per + j, t = c * cs + r;
         if (j < per && r < cs) {
           float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
-          w.err[r * D + d] = kb[r * D + d] + acc[j] - vv;
+          st_hint(&w.err[r * D + d], kb[r * D + d] + acc[j] - vv, pol);
         }
       }
     }
@@ -223,8 +225,8 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
       float rv = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) rv = fmaf(wr[d], w.err[r * D + d], rv);
-      w.r[r * E + e] = rv;
-      w.chain[r * E + e] = rv * gelu_erf_prime(w.h[r * E + e]);
+      st_hint(&w.r[r * E + e], rv, pol);
+      st_hint(&w.chain[r * E + e], rv * gelu_erf_prime(w.h[r * E + e]), pol);
     }
   }
   __threadfence();
@@ -369,6 +371,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   const uint32_t tm = s.tmem;
   uint32_t phase_ld = 0;
   const uint64_t pol_ef = l2_evict_first_policy();  // saved Newton-Schulz tiles: read once
+  const uint64_t pol_el = l2_evict_last_policy();   // per-chunk arrays re-read every token
   PROF_INIT
   PESlot sl[2];
   // stacked X~ / A tiles: the lo part sits XLO bytes after the hi part (the
@@ -520,6 +523,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       for (int jp = 0; jp < n; ++jp) {
         const int r = r0 + jp, t = c * cs + r;
         const float al = s.gate[0][r];
+        PROF_T(tb23)
         st32(Wsave + (size_t)r * DE + e0 * D + dc, Wv[0]);  // W_{t-1}
         st32(Wsave + (size_t)r * DE + e1 * D + dc, Wv[1]);
         if (P.ns_steps > 0) {
@@ -539,6 +543,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             Wv[1][jj] = al * Wv[1][jj] + Sv[1][jj] * inv0;
           }
         }
+        PROF_ADD(23, tb23)
         // read-out backward pieces (memory_layer.py:592-595)
         if (tid < D) {
           s.qv[tid] = jp ? pq[1] : pq[0];
@@ -561,10 +566,10 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           st_remote_f32(&s.xbuf[r & 1][tid], rank ^ 1u, rank ? gelu_tanh(z) : z);
           cluster_sync();
           if (rank == 0) {
-            vec[r * E + tid] = s.xbuf[r & 1][tid];  // p_t
+            st_hint(&vec[r * E + tid], s.xbuf[r & 1][tid], pol_el);  // p_t
           } else {
             const float dz = s.xbuf[r & 1][tid] * gelu_tanh_grad(z);
-            vec[r * E + tid] = dz;
+            st_hint(&vec[r * E + tid], dz, pol_el);
             s.zbuf[0][tid] = dz;
             epi_sync();
             const float dz0 = s.zbuf[0][e0], dz1 = s.zbuf[0][e1];
@@ -597,7 +602,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) mv[jj] = zv[jj] = 0.f;
         for (int i = max(0, cs - Om); i < cs; ++i) {
-          const float f = (win ? s.gate[3][i] : 1.f) * Fm[i * E + e];
+          const float f = (win ? s.gate[3][i] : 1.f) * ld_hint(Fm + i * E + e, pol_el);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) mv[jj] = fmaf(f, s.Gc[i * D + dc + jj], mv[jj]);
         }
@@ -640,8 +645,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         nq = tn < T ? ld_act((const TA*)a.q, o) : 0.f;
         ndy = tn < T ? ld_act((const TA*)a.dy, o) : 0.f;
       }
-      nv0 = vec[rn * E + e0];
-      nv1 = vec[rn * E + e1];
+      nv0 = ld_hint(vec + rn * E + e0, pol_el);
+      nv1 = ld_hint(vec + rn * E + e1, pol_el);
     };
     load_next(cs - 1);
     for (int r = cs - 1; r >= 0; --r) {
@@ -662,15 +667,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           dW[1][jj] = fmaf(v1, xv[dc + jj], dW[1][jj]);
         }
       }
-      if (r + Om < cs) {  // dS_{r+Om} (read after this token's VJP) into L2
-        const float* pb = Wsave + (size_t)(r + Om) * DE + dc;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + e0 * D));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + e1 * D));
-      }
-      {  // W_{t-1} of this token (dalpha, after the VJP) into L2
-        const float* nw = Wsave + (size_t)r * DE + dc;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e0 * D));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(nw + e1 * D));
+      if (tid == 0) {  // W_{t-1} (dalpha) and dS_{r+Om} (window), both read after this token's VJP, into L2
+        bulk_prefetch_l2(Wsave + (size_t)r * DE, DE * sizeof(float));
+        if (r + Om < cs) bulk_prefetch_l2(Wsave + (size_t)(r + Om) * DE, DE * sizeof(float));
       }
       PROF_ADD(18, tc18)
       // ---- Polar Express VJP ----
@@ -807,13 +806,6 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dot = fmaf(gx[0][jj], xo[0][jj], fmaf(gx[1][jj], xo[1][jj], dot));
         dot = block_sum_epi(dot, s.red);  // every thread is done reading the X0 tiles
-        if (P.ns_steps > 0 && r > 0 && tid == 0 && !s.bad) {  // next token's last-step tiles
-          const uint8_t* o = w.ns[rank] + ((size_t)(r - 1) * 5 + (P.ns_steps - 1)) * NS_STEP_BYTES;
-          fence_async_smem();
-          mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
-          bulk_g2s_hint(s.Xh, o, 2 * XT_BYTES, &s.bar_ld, pol_ef);
-          bulk_g2s_hint(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld, pol_ef);
-        }
         const float coef = dot / (kap * kap) * 1.01f / nrm;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -822,22 +814,35 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         }
         PROF_ADD(19, tc19)
       }
+      PROF_T(tc20)
       {  // dalpha_t = <dW_t, W_{t-1}>  (dW_t is unchanged by the VJP above)
-        float dal = 0.f, wv[32];
-        ld32(Wsave + (size_t)r * DE + e0 * D + dc, wv);
+        float wv[2][32];
+        ld32(Wsave + (size_t)r * DE + e0 * D + dc, wv[0]);
+        ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv[1]);
+        float dal = 0.f;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[0][jj], wv[jj], dal);
-        ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[1][jj], wv[jj], dal);
+        for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[0][jj], wv[0][jj], fmaf(dW[1][jj], wv[1][jj], dal));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dal += __shfl_xor_sync(0xffffffffu, dal, o);
         if (l == 0) red_add(&w.scal[r], dal);
       }
+      // next token's last-step tiles (every thread finished reading the X0 tiles in
+      // the normalisation VJP's block reduction); issued after the dalpha loads so
+      // those do not queue behind 96 KB of tile data
+      if (P.ns_steps > 0 && !P.pe_ste && r > 0 && tid == 0 && !s.bad) {
+        const uint8_t* o = w.ns[rank] + ((size_t)(r - 1) * 5 + (P.ns_steps - 1)) * NS_STEP_BYTES;
+        fence_async_smem();
+        mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
+        bulk_g2s_hint(s.Xh, o, 2 * XT_BYTES, &s.bar_ld, pol_ef);
+        bulk_g2s_hint(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld, pol_ef);
+      }
+      PROF_ADD(20, tc20)
+      PROF_T(tc21)
       // dS_t (the full cotangent of S_t) replaces W_{t-1} in scratch for the
       // momentum-scan pass below; this thread read that row for dalpha above.
       st32(Wsave + (size_t)r * DE + e0 * D + dc, dS[0]);
       st32(Wsave + (size_t)r * DE + e1 * D + dc, dS[1]);
+      PROF_ADD(21, tc21)
       PROF_T(twin)
       {  // momentum-scan cotangents of token r (memory_layer.py:256-299, Omega window 233-253)
         const float ci = -g.e * sc;
@@ -943,10 +948,23 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       float* derr = s.Gc;          // cs x D
       {  // thread e: d(W1^T err) = dchain * gelu'(h); dh = dchain * r * gelu''(h)
         const int e = tid;
-        for (int i = 0; i < cs; ++i) {
-          const float dcv = w.dF[1][i * E + e], hv = w.h[i * E + e];
-          dw1t[i * E + e] = dcv * gelu_erf_prime(hv);
-          dhb[i * E + e] = dcv * w.r[i * E + e] * gelu_erf_second(hv);
+        for (int i0 = 0; i0 < cs; i0 += 8) {  // 8 tokens' loads in flight
+          float dcv[8], hv[8], rv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = min(i0 + u, cs - 1);
+            dcv[u] = w.dF[1][i * E + e];
+            hv[u] = ld_hint(w.h + i * E + e, pol_el);
+            rv[u] = ld_hint(w.r + i * E + e, pol_el);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u;
+            if (i < cs) {
+              dw1t[i * E + e] = dcv[u] * gelu_erf_prime(hv[u]);
+              dhb[i * E + e] = dcv[u] * rv[u] * gelu_erf_second(hv[u]);
+            }
+          }
         }
       }
       epi_sync();
@@ -975,11 +993,25 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         float wr[D];
 #pragma unroll
         for (int dd = 0; dd < D; ++dd) wr[dd] = W1t[e * D + dd];
-        for (int i = 0; i < cs; ++i) {
-          float da = w.dF[0][i * E + e];
+        for (int i0 = 0; i0 < cs; i0 += 4) {  // 4 tokens per pass: loads and FMA chains overlap
+          float da[4], hv[4];
 #pragma unroll
-          for (int dd = 0; dd < D; ++dd) da = fmaf(wr[dd], derr[i * D + dd], da);
-          dhb[i * E + e] += da * gelu_tanh_grad(w.h[i * E + e]);
+          for (int u = 0; u < 4; ++u) {
+            const int i = min(i0 + u, cs - 1);
+            da[u] = w.dF[0][i * E + e];
+            hv[u] = ld_hint(w.h + i * E + e, pol_el);
+          }
+#pragma unroll
+          for (int dd = 0; dd < D; dd += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float4 dv = *(const float4*)&derr[min(i0 + u, cs - 1) * D + dd];
+              da[u] = fmaf(wr[dd], dv.x, fmaf(wr[dd + 1], dv.y, fmaf(wr[dd + 2], dv.z, fmaf(wr[dd + 3], dv.w, da[u]))));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (i0 + u < cs) dhb[(i0 + u) * E + e] += da[u] * gelu_tanh_grad(hv[u]);
         }
       }
       epi_sync();
@@ -1014,21 +1046,33 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           if (a.dgamma) a.dgamma[o] = win ? w.scal[3 * MAXCS + tid] : 0.f;
         }
       }
-      // chunk-start weight cotangents of the frozen pass
+      // chunk-start weight cotangents of the frozen pass; their global operands (err and
+      // act on rank 0, k on rank 1) are first staged in shared memory: the W tile area
+      // (free after dk) and, on rank 0, the dh area (rank 0 no longer needs dh)
+      epi_sync();
+      float* gst = Wst;   // err or k: cs x D
+      float* ast = dhb;   // act (rank 0): cs x E
+      {
+        const float* gsrc = rank ? w.k : w.err;
+        for (int i = tid; i < cs * D / 4; i += NT) ((float4*)gst)[i] = ld4_hint(gsrc + 4 * i, pol_el);
+        if (rank == 0)
+          for (int i = tid; i < cs * E / 4; i += NT) ((float4*)ast)[i] = ld4_hint(w.act + 4 * i, pol_el);
+      }
+      epi_sync();
       for (int i = 0; i < cs; ++i) {
         float gv[32], hv2[32];
         if (rank == 0) {  // dW1^T[e][d] += dw1t[e] err[d] + act[e] derr[d]
-          ld32(w.err + i * D + dc, gv);
+          ld32(gst + i * D + dc, gv);
           ld32(derr + i * D + dc, hv2);
           const float a0 = dw1t[i * E + e0], a1 = dw1t[i * E + e1];
-          const float b0 = w.act[i * E + e0], b1 = w.act[i * E + e1];
+          const float b0 = ast[i * E + e0], b1 = ast[i * E + e1];
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             dW[0][jj] = fmaf(a0, gv[jj], fmaf(b0, hv2[jj], dW[0][jj]));
             dW[1][jj] = fmaf(a1, gv[jj], fmaf(b1, hv2[jj], dW[1][jj]));
           }
         } else {          // dW2[e][d] += dh[e] k[d]
-          ld32(w.k + i * D + dc, gv);
+          ld32(gst + i * D + dc, gv);
           const float a0 = dhb[i * E + e0], a1 = dhb[i * E + e1];
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {

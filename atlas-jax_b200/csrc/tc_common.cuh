@@ -128,8 +128,9 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
 
 // Momentum window term of one token (memory_layer.py:233-253, 543-560):
 //   S[e][d] += wgt * sum_{i = i0..r} gamma_i F[i][e] G[i][d]
-// for this thread's rows e0, e1 and columns dc..dc+31.  F (global, L2-resident)
-// is read eight window entries at a time so their loads overlap.
+// for this thread's rows e0, e1 and columns dc..dc+31.  F (global; each row is
+// re-read by the next Omega tokens, mostly from L1) is read eight window entries at
+// a time so their loads overlap.
 __device__ __forceinline__ void momentum_window(float (*Sv)[32], const float* F, const float* G, const float* gam,
                                                 int i0, int r, float wgt, bool win, int e0, int e1, int dc) {
   for (int ib = i0; ib <= r; ib += 8) {
