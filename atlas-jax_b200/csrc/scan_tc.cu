@@ -98,7 +98,7 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
   const TA* vp = (const TA*)a.v;
   const float* W1t = slot;            // W1^T: [e][d]
   const float* W2 = slot + 2 * DE;    // W2:   [e][d]
-  float* actb = (float*)s.slot[0];                     // cs x E  (64 KB)
+  float* actb = (float*)s.slot[0];                     // E x MAXCS, tsw layout (64 KB)
   float* kbuf = (float*)s.slot[1];                     // cs x D  (16 KB)
   float* errb = (float*)(s.slot[1] + MAXCS * D * 4);   // cs x D  (16 KB)
   float* W1s = (float*)(s.slot[1] + 2 * MAXCS * D * 4); // W1^T staged (64 KB)
@@ -127,32 +127,25 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
 #pragma unroll
       for (int d = 0; d < D; ++d) hv = fmaf(w[d], kbuf[r * D + d], hv);
       const float av = gelu_tanh(hv);
-      actb[r * E + e] = av;
+      actb[tsw(e, r)] = av;
       st_hint(&Fg[r * E + e], rank ? hv : av, pol);  // rank 1 keeps h for gelu'(h)
     }
   }
   epi_sync();
-  {  // err = k + W1 act - v ; thread (d, token group)
-    const int d = tid % D, grp = tid / D;  // 4 groups
-    const int per = (cs + 3) / 4;
-    float acc[MAXCS / 4];
+  {  // err = k + W1 act - v ; 4 x 4 (token x d) tile per thread
+    const int dq = tid & 15, iq = tid >> 4;
+    float acc[4][4];
+    tile_tok_d(W1s, actb, dq, iq, acc);
 #pragma unroll
-    for (int j = 0; j < MAXCS / 4; ++j) acc[j] = 0.f;
-    for (int e = 0; e < E; ++e) {
-      float w = W1s[e * D + d];
+    for (int u = 0; u < 4; ++u) {
+      const int r = 4 * iq + u, t = c * cs + r;
+      if (r < cs)
 #pragma unroll
-      for (int j = 0; j < MAXCS / 4; ++j) {
-        int r = grp * per + j;
-        if (j < per && r < cs) acc[j] = fmaf(w, actb[r * E + e], acc[j]);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < MAXCS / 4; ++j) {
-      int r = grp * per + j, t = c * cs + r;
-      if (j < per && r < cs) {
-        float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
-        errb[r * D + d] = kbuf[r * D + d] + acc[j] - vv;
-      }
+        for (int v = 0; v < 4; ++v) {
+          const int d = 4 * dq + v;
+          const float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
+          errb[r * D + d] = kbuf[r * D + d] + acc[u][v] - vv;
+        }
     }
   }
   epi_sync();

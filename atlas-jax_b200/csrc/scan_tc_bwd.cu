@@ -182,35 +182,28 @@ __device__ void frozen_to_scratch(const BwdArgs& a, Smem& s, const ClusterWS& w,
         st_hint(&w.h[r * E + e], hv, pol);
         const float av = gelu_tanh(hv);
         st_hint(&w.act[r * E + e], av, pol);
-        ((float*)s.Gh)[r * E + e] = av;  // smem copy for the err pass (G~ tiles' 64 KB are free here)
+        ((float*)s.Gh)[tsw(e, r)] = av;  // smem copy for the err pass (G~ tiles' 64 KB are free here)
       }
     }
     float* W1s = (float*)s.Xh;  // W1^T staged in the X~ tiles' 64 KB (free in this phase)
     for (int i = tid; i < DE / 4; i += NT) ((float4*)W1s)[i] = ((const float4*)W1t)[i];
     __threadfence_block();
     epi_sync();
-    {
+    {  // err = k + W1 act - v ; 4 x 4 (token x d) tile per thread
       const TA* vp = (const TA*)a.v;
-      const int d = tid % D, grp = tid / D;
-      const int per = (cs + 3) / 4;
-      float acc[MAXCS / 4];
+      const int dq = tid & 15, iq = tid >> 4;
+      float acc[4][4];
+      tile_tok_d(W1s, (const float*)s.Gh, dq, iq, acc);
 #pragma unroll
-      for (int j = 0; j < MAXCS / 4; ++j) acc[j] = 0.f;
-      for (int e = 0; e < E; ++e) {
-        float wv = W1s[e * D + d];
+      for (int u = 0; u < 4; ++u) {
+        const int r = 4 * iq + u, t = c * cs + r;
+        if (r < cs)
 #pragma unroll
-        for (int j = 0; j < MAXCS / 4; ++j) {
-          int r = grp * per + j;
-          if (j < per && r < cs) acc[j] = fmaf(wv, ((const float*)s.Gh)[r * E + e], acc[j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < MAXCS / 4; ++j) {
-        int r = grp * per + j, t = c * cs + r;
-        if (j < per && r < cs) {
-          float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
-          st_hint(&w.err[r * D + d], kb[r * D + d] + acc[j] - vv, pol);
-        }
+          for (int v = 0; v < 4; ++v) {
+            const int d = 4 * dq + v;
+            const float vv = t < T ? ld_act(vp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
+            st_hint(&w.err[r * D + d], kb[r * D + d] + acc[u][v] - vv, pol);
+          }
       }
     }
   }
@@ -718,8 +711,6 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
               if (!mbar_wait(&s.bar_ld, phase_ld)) ok = false;
               phase_ld ^= 1;
             }
-            PROF_T(tcp)
-            PROF_ADD(9, tcp)
             // P = G~^T X~ (stack), this lane's 16 entries P[rr][d0 + j]
             PROF_T(tm0)
             ok = vjp_mma(s, B, tm, 0, &s.bad) && ok;
@@ -933,19 +924,16 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     // ================= D: frozen-state pass backward =================
     __threadfence();
     cluster_sync();  // both ranks' window accumulations are complete
-    ld32(cq + e0 * D + dc, dW[0]);
-    ld32(cq + e1 * D + dc, dW[1]);
-    ld32(cq + DE + e0 * D + dc, dS[0]);
-    ld32(cq + DE + e1 * D + dc, dS[1]);
     {
       // W1^T, then W2, staged in the 64 KB of A/B'/Ps/Sym tiles (free in this phase)
       float* Wst = (float*)s.Ah;
       for (int i = tid; i < DE / 4; i += NT) ((float4*)Wst)[i] = ((const float4*)slot)[i];
       const float* W1t = Wst;
       const float* W2 = Wst;
-      float* dw1t = (float*)s.Xh;  // cs x E
-      float* dhb = (float*)s.Gh;   // cs x E
+      float* dw1t = (float*)s.Xh;  // E x MAXCS, tsw layout
+      float* dhb = (float*)s.Gh;   // E x MAXCS, tsw layout
       float* derr = s.Gc;          // cs x D
+      PROF_T(td0)
       {  // thread e: d(W1^T err) = dchain * gelu'(h); dh = dchain * r * gelu''(h)
         const int e = tid;
         for (int i0 = 0; i0 < cs; i0 += 8) {  // 8 tokens' loads in flight
@@ -961,33 +949,32 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           for (int u = 0; u < 8; ++u) {
             const int i = i0 + u;
             if (i < cs) {
-              dw1t[i * E + e] = dcv[u] * gelu_erf_prime(hv[u]);
-              dhb[i * E + e] = dcv[u] * rv[u] * gelu_erf_second(hv[u]);
+              dw1t[tsw(e, i)] = dcv[u] * gelu_erf_prime(hv[u]);
+              dhb[tsw(e, i)] = dcv[u] * rv[u] * gelu_erf_second(hv[u]);
             }
           }
         }
       }
       epi_sync();
-      const int d = tid % D, grp = tid / D, per = (cs + 3) / 4;
+      PROF_ADD(0, td0)
+      PROF_T(td1)
+      // 4 x 4 output tiles of the (token x d) products: thread (dq, iq) owns
+      // d = 4dq..4dq+3 and tokens i = 4iq..4iq+3 (tokens >= cs are computed and dropped)
+      const int dq = tid & 15, iq = tid >> 4;
       {  // derr = derr_window + W1 d(W1^T err)
-        float acc[MAXCS / 4];
+        float acc[4][4];
+        tile_tok_d(W1t, dw1t, dq, iq, acc);
 #pragma unroll
-        for (int jj = 0; jj < MAXCS / 4; ++jj) acc[jj] = 0.f;
-        for (int e = 0; e < E; ++e) {
-          const float wv = W1t[e * D + d];
+        for (int u = 0; u < 4; ++u) {
+          const int i = 4 * iq + u;
+          if (i < cs)
 #pragma unroll
-          for (int jj = 0; jj < MAXCS / 4; ++jj) {
-            const int i = grp * per + jj;
-            if (jj < per && i < cs) acc[jj] = fmaf(wv, dw1t[i * E + e], acc[jj]);
-          }
-        }
-#pragma unroll
-        for (int jj = 0; jj < MAXCS / 4; ++jj) {
-          const int i = grp * per + jj;
-          if (jj < per && i < cs) derr[i * D + d] = w.dG[0][i * D + d] + acc[jj];
+            for (int v = 0; v < 4; ++v) derr[i * D + 4 * dq + v] = w.dG[0][i * D + 4 * dq + v] + acc[u][v];
         }
       }
       epi_sync();
+      PROF_ADD(1, td1)
+      PROF_T(td9)
       {  // thread e: dact = dact_window + W1^T derr ; dh += dact * gelu_tanh'(h)
         const int e = tid;
         float wr[D];
@@ -1011,31 +998,28 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u)
-            if (i0 + u < cs) dhb[(i0 + u) * E + e] += da[u] * gelu_tanh_grad(hv[u]);
+            if (i0 + u < cs) dhb[tsw(e, i0 + u)] += da[u] * gelu_tanh_grad(hv[u]);
         }
       }
       epi_sync();
+      PROF_ADD(9, td9)
+      PROF_T(td22)
       for (int i = tid; i < DE / 4; i += NT) ((float4*)Wst)[i] = ((const float4*)(slot + 2 * DE))[i];
       epi_sync();
       if (rank == 0) {  // dk = dk_window + derr + W2^T dh ; dv = -derr
-        float acc[MAXCS / 4];
+        float acc[4][4];
+        tile_tok_d(W2, dhb, dq, iq, acc);
 #pragma unroll
-        for (int jj = 0; jj < MAXCS / 4; ++jj) acc[jj] = 0.f;
-        for (int e = 0; e < E; ++e) {
-          const float wv = W2[e * D + d];
+        for (int u = 0; u < 4; ++u) {
+          const int i = 4 * iq + u, t = c * cs + i;
+          if (i < cs && t < T) {
 #pragma unroll
-          for (int jj = 0; jj < MAXCS / 4; ++jj) {
-            const int i = grp * per + jj;
-            if (jj < per && i < cs) acc[jj] = fmaf(wv, dhb[i * E + e], acc[jj]);
-          }
-        }
-#pragma unroll
-        for (int jj = 0; jj < MAXCS / 4; ++jj) {
-          const int i = grp * per + jj, t = c * cs + i;
-          if (jj < per && i < cs && t < T) {
-            const size_t o = (((size_t)b * T + t) * H + hh) * D + d;
-            st_act((TA*)a.dk, o, w.dG[1][i * D + d] + derr[i * D + d] + acc[jj]);
-            st_act((TA*)a.dv, o, -derr[i * D + d]);
+            for (int v = 0; v < 4; ++v) {
+              const int d = 4 * dq + v;
+              const size_t o = (((size_t)b * T + t) * H + hh) * D + d;
+              st_act((TA*)a.dk, o, w.dG[1][i * D + d] + derr[i * D + d] + acc[u][v]);
+              st_act((TA*)a.dv, o, -derr[i * D + d]);
+            }
           }
         }
         if (tid < cs && c * cs + tid < T) {
@@ -1046,6 +1030,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           if (a.dgamma) a.dgamma[o] = win ? w.scal[3 * MAXCS + tid] : 0.f;
         }
       }
+      PROF_ADD(22, td22)
       // chunk-start weight cotangents of the frozen pass; their global operands (err and
       // act on rank 0, k on rank 1) are first staged in shared memory: the W tile area
       // (free after dk) and, on rank 0, the dh area (rank 0 no longer needs dh)
@@ -1059,12 +1044,16 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           for (int i = tid; i < cs * E / 4; i += NT) ((float4*)ast)[i] = ld4_hint(w.act + 4 * i, pol_el);
       }
       epi_sync();
+      ld32(cq + e0 * D + dc, dW[0]);  // carry cotangent parked after phase C
+      ld32(cq + e1 * D + dc, dW[1]);
+      ld32(cq + DE + e0 * D + dc, dS[0]);
+      ld32(cq + DE + e1 * D + dc, dS[1]);
       for (int i = 0; i < cs; ++i) {
         float gv[32], hv2[32];
         if (rank == 0) {  // dW1^T[e][d] += dw1t[e] err[d] + act[e] derr[d]
           ld32(gst + i * D + dc, gv);
           ld32(derr + i * D + dc, hv2);
-          const float a0 = dw1t[i * E + e0], a1 = dw1t[i * E + e1];
+          const float a0 = dw1t[tsw(e0, i)], a1 = dw1t[tsw(e1, i)];
           const float b0 = ast[i * E + e0], b1 = ast[i * E + e1];
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
@@ -1073,7 +1062,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           }
         } else {          // dW2[e][d] += dh[e] k[d]
           ld32(gst + i * D + dc, gv);
-          const float a0 = dhb[i * E + e0], a1 = dhb[i * E + e1];
+          const float a0 = dhb[tsw(e0, i)], a1 = dhb[tsw(e1, i)];
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
             dW[0][jj] = fmaf(a0, gv[jj], dW[0][jj]);

@@ -162,6 +162,33 @@ __device__ __forceinline__ void momentum_window(float (*Sv)[32], const float* F,
   }
 }
 
+// Per-token E-vectors of a chunk that feed (token x d) products on CUDA cores (the
+// frozen pass's act, the backward's d(W1^T err) and dh) are kept transposed, [e][i]
+// with i the token of the chunk, so four consecutive tokens of one e are one 16-byte load.  The
+// 16-byte groups of a row are XOR-swizzled by e so the row-per-thread writes spread
+// over the banks.
+__device__ __forceinline__ int tsw(int e, int i) { return e * MAXCS + ((((i >> 2) ^ (e & 15))) << 2) + (i & 3); }
+
+// acc[u][v] = sum_e Wt[e][4dq + v] * V[e][4iq + u]  (Wt: E x D row-major in shared
+// memory, V: tsw layout), the 4 x 4 (token x d) tile of one thread: thread (dq, iq) owns
+// d = 4dq..4dq+3 and tokens i = 4iq..4iq+3.
+__device__ __forceinline__ void tile_tok_d(const float* Wt, const float* V, int dq, int iq, float (*acc)[4]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[u][v] = 0.f;
+#pragma unroll 4
+  for (int e = 0; e < E; ++e) {
+    const float4 wv = *(const float4*)&Wt[e * D + 4 * dq];
+    const float4 av = *(const float4*)&V[tsw(e, 4 * iq)];
+    const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(aa[u], wa[v], acc[u][v]);
+  }
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
