@@ -177,7 +177,7 @@ struct KArgs {
 };
 
 #ifdef ATLAS_PHASE_PROF
-__device__ unsigned long long g_prof_fwd[24];
+__device__ unsigned long long g_prof_fwd[32];
 #endif
 
 template <typename TA>
@@ -509,8 +509,8 @@ cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
 #ifdef ATLAS_PHASE_PROF
 // Instrumented builds only: read and clear the forward kernel's phase cycle counters.
 extern "C" int atlas_debug_prof_fwd(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, atlas::tc::g_prof_fwd, 24 * sizeof(unsigned long long));
-  unsigned long long z[24] = {};
+  cudaMemcpyFromSymbol(out, atlas::tc::g_prof_fwd, 32 * sizeof(unsigned long long));
+  unsigned long long z[32] = {};
   return cudaMemcpyToSymbol(atlas::tc::g_prof_fwd, z, sizeof(z)) == cudaSuccess ? 0 : 3;
 }
 #endif

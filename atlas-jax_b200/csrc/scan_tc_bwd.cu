@@ -136,6 +136,32 @@ __device__ __forceinline__ void st32(float* p, const float* v) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) ((float4*)p)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
+// Per-token E x D scratch private to this kernel (W_{t-1}, dS_t, S_t, the carry
+// cotangent) is kept in thread order: the value a thread holds at row half h,
+// column j lives at float4 (8h + j/4) * NT + tid, so each warp access covers 512
+// contiguous bytes.  (In row-major order the 32 lanes, one row each, would touch 32
+// cache lines per instruction.)  Every access uses the same thread -> (row, column)
+// map, so the layout never leaves the kernel.
+__device__ __forceinline__ void st_tile(float* base, const float (*v)[32]) {
+  float4* p = (float4*)base + threadIdx.x;
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      p[(8 * h + j) * NT] = make_float4(v[h][4 * j], v[h][4 * j + 1], v[h][4 * j + 2], v[h][4 * j + 3]);
+}
+__device__ __forceinline__ void ld_tile_half(const float* base, int h, float* v) {
+  const float4* p = (const float4*)base + threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 x = p[(8 * h + j) * NT];
+    v[4 * j] = x.x; v[4 * j + 1] = x.y; v[4 * j + 2] = x.z; v[4 * j + 3] = x.w;
+  }
+}
+__device__ __forceinline__ void ld_tile(const float* base, float (*v)[32]) {
+  ld_tile_half(base, 0, v[0]);
+  ld_tile_half(base, 1, v[1]);
+}
 // block-wide copy of n bytes (multiple of 16)
 __device__ __forceinline__ void copy16(void* dst, const void* src, int n) {
   for (int i = threadIdx.x; i < n / 16; i += NT) ((uint4*)dst)[i] = ((const uint4*)src)[i];
@@ -318,7 +344,7 @@ __device__ __forceinline__ bool vjp_mma(Smem& s, PEBars& B, uint32_t tm, int g, 
 }
 
 #ifdef ATLAS_PHASE_PROF
-__device__ unsigned long long g_prof_bwd[24];
+__device__ unsigned long long g_prof_bwd[32];
 #endif
 
 template <typename TA>
@@ -449,8 +475,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     ld32(mine + e1 * D + dc, Wv[1]);
     ld32(mine + DE + e0 * D + dc, Sv[0]);
     ld32(mine + DE + e1 * D + dc, Sv[1]);
-    st32(Ssave + e0 * D + dc, Sv[0]);
-    st32(Ssave + e1 * D + dc, Sv[1]);
+    st_tile(Ssave, Sv);
     for (int r0 = 0; r0 < cs; r0 += npair) {
       const int n = min(npair, cs - r0);
       float inv0 = 0.f;
@@ -466,8 +491,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         const int i0 = win ? max(0, r - P.omega + 1) : r;
         momentum_window(Sv, Fm, s.Gc, s.gate[3], i0, r, -et * sc, win, e0, e1, dc);
         if (P.pe_ste || P.ns_steps == 0) {  // otherwise phase C reads S_t from the X0 tiles
-          st32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, Sv[0]);
-          st32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, Sv[1]);
+          st_tile(Ssave + (size_t)(r + 1) * DE, Sv);
         }
         float ss = 0.f;
 #pragma unroll
@@ -517,8 +541,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         const int r = r0 + jp, t = c * cs + r;
         const float al = s.gate[0][r];
         PROF_T(tb23)
-        st32(Wsave + (size_t)r * DE + e0 * D + dc, Wv[0]);  // W_{t-1}
-        st32(Wsave + (size_t)r * DE + e1 * D + dc, Wv[1]);
+        st_tile(Wsave + (size_t)r * DE, Wv);  // W_{t-1}
         if (P.ns_steps > 0) {
           float x0[32], x1[32];
           tmem_ld32(sl[jp].tm + lane_off + TM_X + dc, x0);
@@ -608,10 +631,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     {
       float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
       if (j > 0) {
-        ld32(cq + e0 * D + dc, dW[0]);
-        ld32(cq + e1 * D + dc, dW[1]);
-        ld32(cq + DE + e0 * D + dc, dS[0]);
-        ld32(cq + DE + e1 * D + dc, dS[1]);
+        ld_tile(cq, dW);
+        ld_tile(cq + DE, dS);
       } else {
         const float* gW = rank ? a.dW2_out : a.dW1_out;
         const float* gS = rank ? a.dS2_out : a.dS1_out;
@@ -669,8 +690,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       if (P.pe_ste || P.ns_steps == 0) {
         if (P.pe_ste) {
           float xo[2][32];
-          ld32(Ssave + (size_t)(r + 1) * DE + e0 * D + dc, xo[0]);
-          ld32(Ssave + (size_t)(r + 1) * DE + e1 * D + dc, xo[1]);
+          ld_tile(Ssave + (size_t)(r + 1) * DE, xo);
           theta_step(dS, xo, r, cs, s.gate[2], w.scal, l);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
@@ -682,8 +702,6 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       if (!P.pe_ste) {
         const float* St = Ssave + (size_t)(r + 1) * DE;
         const float nrm = s.nrm[r], kap = nrm * 1.01f + 1e-6f, inv = 1.0f / kap;
-        float xo[2][32];
-        float gx[2][32];
         if (P.ns_steps > 0) {
           PROF_T(tns)
           bool ok = true;
@@ -762,12 +780,14 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             PROF_T(tep2)
             if (st > 0 && tid == 0 && !s.bad)  // rest of step st-1's tiles: X~ is free now
               bulk_g2s_hint(s.Xh, nscur + (size_t)(st - 1) * NS_STEP_BYTES, 2 * XT_BYTES, &s.bar_ld, pol_ef);
-            tmem_ld32(tm + lane_off + VJ_X + dc, gx[0]);
-            tmem_ld32(tm + lane_off + VJ_X + 64 + dc, gx[1]);
-            tmem_wait_ld();
-            if (st > 0) {
-              store_stk<32>(s.Gh, e0, dc, gx[0]);
-              store_stk<32>(s.Gh, e1, dc, gx[1]);
+            if (st > 0) {  // dX~ becomes the next step's G~ (after step 0 it stays in TMEM)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                float gv[32];
+                tmem_ld32(tm + lane_off + VJ_X + 64 * h + dc, gv);
+                tmem_wait_ld();
+                store_stk<32>(s.Gh, h ? e1 : e0, dc, gv);
+              }
             }
             PROF_ADD(15, tep2)
           }
@@ -776,40 +796,72 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             set_status(a.status, ATLAS_ERR_DEVICE_TIMEOUT);
             s.bad = 1;
           }
-        } else {
+        }
+        // Normalisation VJP, X0 = S / kappa, kappa = 1.01 sqrt(sum S^2 + 1e-12) + 1e-6, one
+        // 32-column row half at a time (registers): pass 1 forms <G, S_t> and, for the
+        // deferred momentum step, dtheta_{r+1} = <dS_{r+1}, S_r>; pass 2 updates dS.
+        // G (the VJP's dX~_0, or dW without Newton-Schulz steps) is re-read from TMEM, and
+        // S_t = kappa X0 from the X0 tiles still resident (stacked hi + lo, ~2^-17 relative).
+        PROF_T(tc19)
+        const bool from_tiles = P.ns_steps > 0;
+        auto load_xo = [&](int h, float* xo) {
+          if (from_tiles)
+            load_stk32(s.Xh, h ? e1 : e0, dc, kap, xo);
+          else
+            ld_tile_half(St, h, xo);
+        };
+        auto load_g = [&](int h, float* gv) {
+          if (from_tiles) {
+            tmem_ld32(tm + lane_off + VJ_X + 64 * h + dc, gv);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) gv[jj] = dW[h][jj];
+          }
+        };
+        float dot = 0.f, dt = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float xo[32], gv[32];
+          load_xo(h, xo);
+          load_g(h, gv);
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
-            gx[0][jj] = dW[0][jj];
-            gx[1][jj] = dW[1][jj];
+            dot = fmaf(gv[jj], xo[jj], dot);
+            dt = fmaf(dS[h][jj], xo[jj], dt);
           }
         }
-        // X0 = S / kappa, kappa = 1.01 sqrt(sum S^2 + 1e-12) + 1e-6
-        PROF_T(tc19)
-        if (P.ns_steps > 0) {  // S_t = kappa X0, X0 still resident (stacked hi + lo, ~2^-17 relative)
-          load_stk32(s.Xh, e0, dc, kap, xo[0]);
-          load_stk32(s.Xh, e1, dc, kap, xo[1]);
-        } else {
-          ld32(St + e0 * D + dc, xo[0]);
-          ld32(St + e1 * D + dc, xo[1]);
-        }
-        theta_step(dS, xo, r, cs, s.gate[2], w.scal, l);
-        float dot = 0.f;
+        const bool step = r + 1 < cs;  // theta_{r+1} decay of the incoming dS (none at the chunk end)
+        if (step) {
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dot = fmaf(gx[0][jj], xo[0][jj], fmaf(gx[1][jj], xo[1][jj], dot));
-        dot = block_sum_epi(dot, s.red);  // every thread is done reading the X0 tiles
+          for (int o = 16; o > 0; o >>= 1) dt += __shfl_xor_sync(0xffffffffu, dt, o);
+          if (l == 0) red_add(&w.scal[2 * MAXCS + r + 1], dt);
+        }
+        const float th = step ? s.gate[2][r + 1] : 1.f;
+        dot = block_sum_epi(dot, s.red);
         const float coef = dot / (kap * kap) * 1.01f / nrm;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          dS[0][jj] += gx[0][jj] * inv - coef * xo[0][jj];
-          dS[1][jj] += gx[1][jj] * inv - coef * xo[1][jj];
+        for (int h = 0; h < 2; ++h) {
+          float xo[32], gv[32];
+          load_xo(h, xo);
+          load_g(h, gv);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) dS[h][jj] = fmaf(th, dS[h][jj], gv[jj] * inv - coef * xo[jj]);
+        }
+        // X0 tiles free: warp 0 (whose lane 0 issues the next token's tiles below) waits for
+        // the other warps; they only signal and go on
+        if (from_tiles) {
+          if (wp == 0)
+            asm volatile("bar.sync 2, 256;" ::: "memory");
+          else
+            asm volatile("bar.arrive 2, 256;" ::: "memory");
         }
         PROF_ADD(19, tc19)
       }
       PROF_T(tc20)
       {  // dalpha_t = <dW_t, W_{t-1}>  (dW_t is unchanged by the VJP above)
         float wv[2][32];
-        ld32(Wsave + (size_t)r * DE + e0 * D + dc, wv[0]);
-        ld32(Wsave + (size_t)r * DE + e1 * D + dc, wv[1]);
+        ld_tile(Wsave + (size_t)r * DE, wv);
         float dal = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dal = fmaf(dW[0][jj], wv[0][jj], fmaf(dW[1][jj], wv[1][jj], dal));
@@ -817,29 +869,31 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         for (int o = 16; o > 0; o >>= 1) dal += __shfl_xor_sync(0xffffffffu, dal, o);
         if (l == 0) red_add(&w.scal[r], dal);
       }
-      // next token's last-step tiles (every thread finished reading the X0 tiles in
-      // the normalisation VJP's block reduction); issued after the dalpha loads so
-      // those do not queue behind 96 KB of tile data
+      // next token's last-step tiles (every warp has finished reading the X0 tiles: named
+      // barrier 2 above); issued after the dalpha loads so those do not queue behind
+      // 96 KB of tile data
+      PROF_ADD(20, tc20)
+      PROF_T(tc24)
       if (P.ns_steps > 0 && !P.pe_ste && r > 0 && tid == 0 && !s.bad) {
         const uint8_t* o = w.ns[rank] + ((size_t)(r - 1) * 5 + (P.ns_steps - 1)) * NS_STEP_BYTES;
         fence_async_smem();
+        PROF_ADD(25, tc24)
         mbar_expect_tx(&s.bar_ld, (uint32_t)NS_STEP_BYTES);
         bulk_g2s_hint(s.Xh, o, 2 * XT_BYTES, &s.bar_ld, pol_ef);
         bulk_g2s_hint(s.Ah, o + 2 * XT_BYTES, 4 * AT_BYTES, &s.bar_ld, pol_ef);
       }
-      PROF_ADD(20, tc20)
+      PROF_ADD(24, tc24)
       PROF_T(tc21)
       // dS_t (the full cotangent of S_t) replaces W_{t-1} in scratch for the
       // momentum-scan pass below; this thread read that row for dalpha above.
-      st32(Wsave + (size_t)r * DE + e0 * D + dc, dS[0]);
-      st32(Wsave + (size_t)r * DE + e1 * D + dc, dS[1]);
+      st_tile(Wsave + (size_t)r * DE, dS);
       PROF_ADD(21, tc21)
       PROF_T(twin)
       {  // momentum-scan cotangents of token r (memory_layer.py:256-299, Omega window 233-253)
         const float ci = -g.e * sc;
         const bool out = r + Om < cs;
         const float co = out ? s.gate[1][r + Om] * sc : 0.f;
-        const float* pb = Wsave + (size_t)(out ? r + Om : r) * DE + dc;
+        const float* pb = Wsave + (size_t)(out ? r + Om : r) * DE;
         const float gi = win ? g.g : 1.f;
         const float f0 = Fm[r * E + e0], f1 = Fm[r * E + e1];
         const int io = r - Om;
@@ -852,7 +906,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           const uint32_t cr = tm + lane_off + 64 * h + dc;
           float rv[32], bv[32];
           tmem_ld32(cr + VJ_R, rv);
-          ld32(pb + (h ? e1 : e0) * D, bv);
+          ld_tile_half(pb, h, bv);
           tmem_wait_ld();
           float acc = 0.f;
 #pragma unroll
@@ -907,18 +961,15 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     }
     {  // dtheta_0 = <dS_0, S_{-1}>, then the decay by theta_0 that leaves the chunk
       float xo[2][32];
-      ld32(Ssave + e0 * D + dc, xo[0]);
-      ld32(Ssave + e1 * D + dc, xo[1]);
+      ld_tile(Ssave, xo);
       theta_step(dS, xo, -1, cs, s.gate[2], w.scal, l);
     }
 
     // carry cotangent of chunk c-1 (before phase D's frozen-pass terms) parked in
     // this chain's slot; phase D reloads it (same thread, same addresses)
     float* cq = K.cot + (size_t)q * 4 * DE + 2 * rank * DE;
-    st32(cq + e0 * D + dc, dW[0]);
-    st32(cq + e1 * D + dc, dW[1]);
-    st32(cq + DE + e0 * D + dc, dS[0]);
-    st32(cq + DE + e1 * D + dc, dS[1]);
+    st_tile(cq, dW);
+    st_tile(cq + DE, dS);
     PROF_ADD(4, tC)
     PROF_T(tD)
     // ================= D: frozen-state pass backward =================
@@ -1044,10 +1095,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           for (int i = tid; i < cs * E / 4; i += NT) ((float4*)ast)[i] = ld4_hint(w.act + 4 * i, pol_el);
       }
       epi_sync();
-      ld32(cq + e0 * D + dc, dW[0]);  // carry cotangent parked after phase C
-      ld32(cq + e1 * D + dc, dW[1]);
-      ld32(cq + DE + e0 * D + dc, dS[0]);
-      ld32(cq + DE + e1 * D + dc, dS[1]);
+      ld_tile(cq, dW);  // carry cotangent parked after phase C
+      ld_tile(cq + DE, dS);
       for (int i = 0; i < cs; ++i) {
         float gv[32], hv2[32];
         if (rank == 0) {  // dW1^T[e][d] += dw1t[e] err[d] + act[e] derr[d]
@@ -1077,10 +1126,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       for (int jj = 0; jj < 32; ++jj) dW[0][jj] = dW[1][jj] = dS[0][jj] = dS[1][jj] = 0.f;
     }
     if (c > 0) {
-      st32(cq + e0 * D + dc, dW[0]);
-      st32(cq + e1 * D + dc, dW[1]);
-      st32(cq + DE + e0 * D + dc, dS[0]);
-      st32(cq + DE + e1 * D + dc, dS[1]);
+      st_tile(cq, dW);
+      st_tile(cq + DE, dS);
     } else {
       float* oW = rank ? a.dW2_in : a.dW1_in;
       float* oS = rank ? a.dS2_in : a.dS1_in;
@@ -1171,8 +1218,8 @@ cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t st) {
 #ifdef ATLAS_PHASE_PROF
 // Instrumented builds only: read and clear the backward kernel's phase cycle counters.
 extern "C" int atlas_debug_prof_bwd(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, atlas::tc::bwd::g_prof_bwd, 24 * sizeof(unsigned long long));
-  unsigned long long z[24] = {};
+  cudaMemcpyFromSymbol(out, atlas::tc::bwd::g_prof_bwd, 32 * sizeof(unsigned long long));
+  unsigned long long z[32] = {};
   return cudaMemcpyToSymbol(atlas::tc::bwd::g_prof_bwd, z, sizeof(z)) == cudaSuccess ? 0 : 3;
 }
 #endif

@@ -275,12 +275,12 @@ __device__ __forceinline__ void mma_stack(uint32_t tmd, const uint8_t* z, const 
 // Optional phase timers (build with -DATLAS_PHASE_PROF; thread 0 accumulates
 // clock64() deltas into a shared array; off in the product build).
 #ifdef ATLAS_PHASE_PROF
-#define PROF_DECL __shared__ unsigned long long s_prof[24];
-#define PROF_INIT if (threadIdx.x < 24) s_prof[threadIdx.x] = 0;
+#define PROF_DECL __shared__ unsigned long long s_prof[32];
+#define PROF_INIT if (threadIdx.x < 32) s_prof[threadIdx.x] = 0;
 #define PROF_T(v) long long v = clock64();
 #define PROF_ADD(slot, v) if (threadIdx.x == 0) s_prof[slot] += clock64() - v;
 #define PROF_PTR s_prof
-#define PROF_FLUSH(g) if (threadIdx.x < 24) atomicAdd(&g[threadIdx.x], s_prof[threadIdx.x]);
+#define PROF_FLUSH(g) if (threadIdx.x < 32) atomicAdd(&g[threadIdx.x], s_prof[threadIdx.x]);
 #else
 #define PROF_DECL
 #define PROF_INIT
