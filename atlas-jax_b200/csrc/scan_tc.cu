@@ -294,18 +294,19 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
       PROF_T(tpair)
       const int n = min(npair, cs - r0);
       float inv0 = 0.f;
+      float Gv[2][32];  // Omega-window gradient sum, slid from the pair's first token to its second
       for (int j = 0; j < n; ++j) {
         PROF_T(ttok)
         const int r = r0 + j;
         const float et = s.gate[1][r], th = s.gate[2][r];
         // ---- momentum: S <- theta S - eta * s * sum_i gamma_i f_i g_i^T ----
+        window_sum(Gv, Fg, s.G, s.gate[3], r, P.omega, win, j > 0, e0, e1, dc);
+        const float wg = -et * sc;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
-          Sv[0][jj] *= th;
-          Sv[1][jj] *= th;
+          Sv[0][jj] = fmaf(th, Sv[0][jj], wg * Gv[0][jj]);
+          Sv[1][jj] = fmaf(th, Sv[1][jj], wg * Gv[1][jj]);
         }
-        const int i0 = win ? max(0, r - P.omega + 1) : r;
-        momentum_window(Sv, Fg, s.G, s.gate[3], i0, r, -et * sc, win, e0, e1, dc);
         PROF_ADD(2, ttok)
         PROF_T(tnorm)
         // ---- Frobenius normalisation (memory_layer.py:55-56) ----

@@ -480,16 +480,17 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       const int n = min(npair, cs - r0);
       float inv0 = 0.f;
       PROF_T(tb16)
+      float Gv[2][32];  // Omega-window gradient sum, slid from the pair's first token to its second
       for (int jp = 0; jp < n; ++jp) {
         const int r = r0 + jp;
         const float et = s.gate[1][r], th = s.gate[2][r];
+        window_sum(Gv, Fm, s.Gc, s.gate[3], r, P.omega, win, jp > 0, e0, e1, dc);
+        const float wg = -et * sc;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
-          Sv[0][jj] *= th;
-          Sv[1][jj] *= th;
+          Sv[0][jj] = fmaf(th, Sv[0][jj], wg * Gv[0][jj]);
+          Sv[1][jj] = fmaf(th, Sv[1][jj], wg * Gv[1][jj]);
         }
-        const int i0 = win ? max(0, r - P.omega + 1) : r;
-        momentum_window(Sv, Fm, s.Gc, s.gate[3], i0, r, -et * sc, win, e0, e1, dc);
         if (P.pe_ste || P.ns_steps == 0) {  // otherwise phase C reads S_t from the X0 tiles
           st_tile(Ssave + (size_t)(r + 1) * DE, Sv);
         }

@@ -189,6 +189,43 @@ __device__ __forceinline__ void tile_tok_d(const float* Wt, const float* V, int 
   }
 }
 
+// Gv += c f_i g_i^T for this thread's rows e0, e1 and columns dc..dc+31.
+__device__ __forceinline__ void rank1_add(float (*Gv)[32], const float* F, const float* G, int i, float c, int e0,
+                                          int e1, int dc) {
+  const float fa = c * F[i * E + e0], fb = c * F[i * E + e1];
+  const float4* g4 = (const float4*)&G[i * D + dc];
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    const float4 g = g4[j4];
+    Gv[0][4 * j4 + 0] = fmaf(fa, g.x, Gv[0][4 * j4 + 0]);
+    Gv[0][4 * j4 + 1] = fmaf(fa, g.y, Gv[0][4 * j4 + 1]);
+    Gv[0][4 * j4 + 2] = fmaf(fa, g.z, Gv[0][4 * j4 + 2]);
+    Gv[0][4 * j4 + 3] = fmaf(fa, g.w, Gv[0][4 * j4 + 3]);
+    Gv[1][4 * j4 + 0] = fmaf(fb, g.x, Gv[1][4 * j4 + 0]);
+    Gv[1][4 * j4 + 1] = fmaf(fb, g.y, Gv[1][4 * j4 + 1]);
+    Gv[1][4 * j4 + 2] = fmaf(fb, g.z, Gv[1][4 * j4 + 2]);
+    Gv[1][4 * j4 + 3] = fmaf(fb, g.w, Gv[1][4 * j4 + 3]);
+  }
+}
+
+// Omega-window sum of token r's per-token gradients, G_r = sum_{i in win(r)} c_i f_i g_i^T
+// (c_i = gamma_i; window [max(0, r - omega + 1), r] of the chunk, or just r when the
+// window is off; memory_layer.py:233-253).  The first token of a Polar Express pair
+// builds it from the window; the second (slide) moves the previous token's sum on by
+// one token: add token r, drop token r - omega if it was in the previous window.
+__device__ __forceinline__ void window_sum(float (*Gv)[32], const float* F, const float* G, const float* gam, int r,
+                                           int omega, bool win, bool slide, int e0, int e1, int dc) {
+  if (!slide) {
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) Gv[0][jj] = Gv[1][jj] = 0.f;
+    momentum_window(Gv, F, G, gam, win ? max(0, r - omega + 1) : r, r, 1.f, win, e0, e1, dc);
+  } else {
+    rank1_add(Gv, F, G, r, win ? gam[r] : 1.f, e0, e1, dc);
+    const int io = r - (win ? omega : 1);
+    if (io >= 0) rank1_add(Gv, F, G, io, -(win ? gam[io] : 1.f), e0, e1, dc);
+  }
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
