@@ -143,8 +143,8 @@ int atlas_scan_bwd(const AtlasScanParams* p, const void* q, const void* k, const
 
 size_t atlas_polar_express_workspace_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ns_steps,
                                            int32_t precision) {
-  (void)precision;
   if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  if (precision == ATLAS_PREC_TENSOR) return atlas::tcpe::workspace_bytes(batch, rows, cols);
   return atlas::exact::pe_workspace_bytes(batch, rows, cols, ns_steps);
 }
 
@@ -155,11 +155,15 @@ int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t
   if (!X || !Y) return fail(ATLAS_ERR_INVALID_ARGUMENT, "X and Y must be non-NULL");
   if (batch <= 0 || rows <= 0 || cols <= 0) return fail(ATLAS_ERR_INVALID_ARGUMENT, "empty problem");
   if (ns_steps < 0 || ns_steps > 5) return fail(ATLAS_ERR_INVALID_ARGUMENT, "ns_steps must be in 0..5");
-  if (precision != ATLAS_PREC_EXACT)
-    return fail(ATLAS_ERR_UNSUPPORTED, "batched Polar Express is implemented in ATLAS_PREC_EXACT only");
+  if (precision != ATLAS_PREC_EXACT && precision != ATLAS_PREC_TENSOR)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "precision must be ATLAS_PREC_EXACT or ATLAS_PREC_TENSOR");
   size_t need = atlas_polar_express_workspace_bytes(batch, rows, cols, ns_steps, precision);
   if (!workspace || workspace_bytes < need)
     return fail(ATLAS_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (precision == ATLAS_PREC_TENSOR)
+    return cuda_result(atlas::tcpe::launch(X, Y, batch, rows, cols, ns_steps, eps_in_sqrt, workspace,
+                                           (cudaStream_t)stream),
+                       "atlas_polar_express_batched launch (tensor)");
   return cuda_result(atlas::exact::launch_pe(X, Y, batch, rows, cols, ns_steps, eps_in_sqrt, workspace,
                                              (cudaStream_t)stream),
                      "atlas_polar_express_batched launch");

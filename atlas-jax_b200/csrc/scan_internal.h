@@ -57,6 +57,13 @@ struct WaitHooks {
 WaitHooks wait_hooks();
 int report_error(int code, const char* msg);  // sets atlas_last_error_string(), returns code  // address of the status word on the current device
 
+// tcgen05 batched Polar Express for large matrices (Muon), pe_tc.cu
+namespace tcpe {
+size_t workspace_bytes(int64_t batch, int rows, int cols);
+cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps, void* ws,
+                   cudaStream_t s);
+}  // namespace tcpe
+
 namespace tc {
 bool supported(const AtlasScanParams& p, const char** why);
 size_t saved_bytes(const AtlasScanParams& p);

@@ -141,7 +141,11 @@ int atlas_scan_fwd_noalloc(const AtlasScanParams* p,
  * Replaces fused_polar_express (atlas_jax/kernels/triton_pe.py:26-69, same math
  * as memory_layer.py:43-71) and the Muon orthogonalisation call site
  * (atlas_jax/optim.py:68-83, which omits the 1e-12 inside the square root:
- * pass eps_in_sqrt = 0 for that behaviour, 1e-12 for the memory layer's). */
+ * pass eps_in_sqrt = 0 for that behaviour, 1e-12 for the memory layer's).
+ * precision: ATLAS_PREC_EXACT runs float64 on CUDA cores, one CTA per matrix (small
+ * matrices, parity checks); ATLAS_PREC_TENSOR runs each Newton-Schulz step as three
+ * batched tcgen05 GEMMs with the three-term bf16 split (large matrices such as
+ * Muon's stacked parameter gradients). */
 int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t rows, int32_t cols,
                                 int32_t ns_steps, float eps_in_sqrt, int32_t precision,
                                 void* workspace, size_t workspace_bytes, void* stream);
