@@ -12,7 +12,6 @@ projections) plus ragged sizes that exercise the masked tile edges.  Tolerance
 about 16 mantissa bits per operand, and Polar Express amplifies rounding in the
 small singular directions.
 """
-import numpy as np
 import pytest
 import torch
 
