@@ -13,8 +13,8 @@
 // Polar Express amplifies).  The epilogue fuses alpha * product + beta * addend.
 //
 // GEMM kernel: one CTA of 4 warps per 128 x 128 output tile and batch entry; K in
-// chunks of 32, two shared-memory stages (the next chunk's global loads are in
-// flight while the current chunk's MMAs run); one elected thread issues the MMAs
+// chunks of 32, two shared-memory stages (the next chunk's coalesced global loads are
+// in flight while the current chunk's MMAs run); one elected thread issues the MMAs
 // and commits them to the stage's mbarrier; every wait is bounded and records
 // ATLAS_ERR_DEVICE_TIMEOUT instead of hanging.
 #include <cuda_bf16.h>
@@ -56,23 +56,11 @@ struct GemmArgs {
   int* status;
 };
 
-__device__ __forceinline__ void ld_row32(const float* p, int valid, bool vec, float* v) {
-  if (vec && valid >= 32) {
+// 4 consecutive values -> bf16 hi / lo, 8 bytes into each tile
+__device__ __forceinline__ void split4(uint8_t* th, uint8_t* tl, uint32_t off, const float* v) {
+  uint32_t h[2], l[2];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 x = ((const float4*)p)[j];
-      v[4 * j] = x.x; v[4 * j + 1] = x.y; v[4 * j + 2] = x.z; v[4 * j + 3] = x.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = j < valid ? p[j] : 0.f;
-  }
-}
-
-__device__ __forceinline__ void split8(uint8_t* th, uint8_t* tl, uint32_t off, const float* v) {
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < 2; ++k) {
     __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
     const uint32_t hb = *reinterpret_cast<uint32_t*>(&hv);
     const float r0 = v[2 * k] - __uint_as_float(hb << 16);
@@ -81,8 +69,8 @@ __device__ __forceinline__ void split8(uint8_t* th, uint8_t* tl, uint32_t off, c
     h[k] = hb;
     l[k] = *reinterpret_cast<uint32_t*>(&lv);
   }
-  *(uint4*)(th + off) = make_uint4(h[0], h[1], h[2], h[3]);
-  *(uint4*)(tl + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  *(uint2*)(th + off) = make_uint2(h[0], h[1]);
+  *(uint2*)(tl + off) = make_uint2(l[0], l[1]);
 }
 
 __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
@@ -108,34 +96,47 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
   const uint32_t tm = s.tmem;
   const bool vecA = (g.lda & 3) == 0, vecB = (g.ldb & 3) == 0;
   const int nk = (g.K + TK - 1) / TK;
-  float ra[32], rb[32];
-  auto load = [&](int i) {
-    const int k0 = i * TK;
-    const int m = m0 + t;
-    if (m < g.M)
-      ld_row32(A + (size_t)m * g.lda + k0, g.K - k0, vecA, ra);
-    else
+  // Coalesced staging: per pass, 8 threads cover one 128-byte row segment of a K-major
+  // tile (32 k) and a warp reads 4 whole segments; for the MN-major B tile a warp
+  // reads one 512-byte row of 128 n.  Each thread holds 8 passes x 4 floats; the next
+  // chunk's loads are issued right after this chunk is staged, so they are in flight
+  // while its MMAs run.
+  float ra0[32], rb0[32];
+  auto ld4 = [&](const float* p, int valid, bool vec, float* v) {
+    if (vec && valid >= 4) {
+      const float4 x = *(const float4*)p;
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) ra[j] = 0.f;
-    if (!g.b_kn) {  // row n of B, k0..k0+31
-      const int n = n0 + t;
-      if (n < g.N)
-        ld_row32(Bp + (size_t)n * g.ldb + k0, g.K - k0, vecB, rb);
+      for (int j = 0; j < 4; ++j) v[j] = j < valid ? p[j] : 0.f;
+    }
+  };
+  auto load = [&](int i, float* ra, float* rb) {
+    const int k0 = i * TK, kq = 4 * (t & 7);
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const int m = m0 + 16 * p + (t >> 3);
+      if (m < g.M)
+        ld4(A + (size_t)m * g.lda + k0 + kq, g.K - k0 - kq, vecA, ra + 4 * p);
       else
-#pragma unroll
-        for (int j = 0; j < 32; ++j) rb[j] = 0.f;
-    } else {  // row k of B, 32 columns of n
-      const int k = k0 + (t >> 2), nc = n0 + 32 * (t & 3);
-      if (k < g.K)
-        ld_row32(Bp + (size_t)k * g.ldb + nc, g.N - nc, vecB, rb);
-      else
-#pragma unroll
-        for (int j = 0; j < 32; ++j) rb[j] = 0.f;
+        ra[4 * p] = ra[4 * p + 1] = ra[4 * p + 2] = ra[4 * p + 3] = 0.f;
+      if (!g.b_kn) {
+        const int n = n0 + 16 * p + (t >> 3);
+        if (n < g.N)
+          ld4(Bp + (size_t)n * g.ldb + k0 + kq, g.K - k0 - kq, vecB, rb + 4 * p);
+        else
+          rb[4 * p] = rb[4 * p + 1] = rb[4 * p + 2] = rb[4 * p + 3] = 0.f;
+      } else {
+        const int k = k0 + 4 * p + (t >> 5), nq = 4 * (t & 31);
+        if (k < g.K)
+          ld4(Bp + (size_t)k * g.ldb + n0 + nq, g.N - n0 - nq, vecB, rb + 4 * p);
+        else
+          rb[4 * p] = rb[4 * p + 1] = rb[4 * p + 2] = rb[4 * p + 3] = 0.f;
+      }
     }
   };
   const uint32_t idesc = idesc_bf16(128, 128, false, g.b_kn != 0);
-  load(0);
-  for (int i = 0; i < nk; ++i) {
+  auto chunk = [&](int i, float* ra, float* rb) {
     const int st = i & 1;
     if (i >= 2 && !s.bad && !mbar_wait(&s.bar[st], ((i - 2) >> 1) & 1)) {  // MMAs of chunk i-2 read this stage
       s.bad = 1;
@@ -143,18 +144,17 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
     }
     uint8_t *ah = s.a[st][0], *al = s.a[st][1], *bh = s.b[st][0], *bl = s.b[st][1];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) split8(ah, al, cm_off(t, 8 * j, TK), ra + 8 * j);
-    if (!g.b_kn) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) split8(bh, bl, cm_off(t, 8 * j, TK), rb + 8 * j);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) split8(bh, bl, cm_off(t >> 2, 32 * (t & 3) + 8 * j, TN), rb + 8 * j);
+    for (int p = 0; p < 8; ++p) {
+      split4(ah, al, cm_off(16 * p + (t >> 3), 4 * (t & 7), TK), ra + 4 * p);
+      if (!g.b_kn)
+        split4(bh, bl, cm_off(16 * p + (t >> 3), 4 * (t & 7), TK), rb + 4 * p);
+      else
+        split4(bh, bl, cm_off(4 * p + (t >> 5), 4 * (t & 31), TN), rb + 4 * p);
     }
     fence_async_smem();
     fence_before();
     __syncthreads();
-    if (i + 1 < nk) load(i + 1);  // next chunk's global loads overlap this chunk's MMAs
+    if (i + 1 < nk) load(i + 1, ra, rb);
     if (w == 0 && !__shfl_sync(0xffffffffu, s.bad, 0)) {  // warp-uniform: elect.sync needs the whole warp
       fence_after();
       const uint64_t da[2] = {desc_kmajor(smem_u32(ah), TK), desc_kmajor(smem_u32(al), TK)};
@@ -178,7 +178,9 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
           mma_bf16(tm, da[ta[term]] + ks * sa, db[tb[term]] + ks * sb, idesc, (i || term || ks) ? 1u : 0u);
       mma_commit(&s.bar[st]);
     }
-  }
+  };
+  load(0, ra0, rb0);
+  for (int i = 0; i < nk; ++i) chunk(i, ra0, rb0);
   // the last commit covers every MMA of the tile
   if (!s.bad && !mbar_wait(&s.bar[(nk - 1) & 1], ((nk - 1) >> 1) & 1)) {
     s.bad = 1;
