@@ -49,3 +49,18 @@ def test_polar_express_rejects_empty():
     lib = L.load()
     assert lib.atlas_polar_express_batched(None, None, 0, 4, 4, 5, 1e-12, 0, None, 0, None) \
         == L.ATLAS_ERR_INVALID_ARGUMENT
+
+
+def test_polar_express_precisions():
+    lib = L.load()
+    # tensor path: two wide X buffers and two D x D buffers per matrix, float32
+    assert lib.atlas_polar_express_workspace_bytes(12, 4096, 768, 5, L.ATLAS_PREC_TENSOR) == \
+        12 * (2 * 4096 * 768 + 2 * 768 * 768) * 4
+    assert lib.atlas_polar_express_workspace_bytes(12, 768, 768, 5, L.ATLAS_PREC_EXACT) > 0
+    # an unknown precision is refused before any device work (the pointers are never read)
+    dummy = ctypes.c_void_p(16)
+    rc = lib.atlas_polar_express_batched(dummy, dummy, 1, 8, 8, 5, 0.0, 7, dummy, 1 << 20, None)
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT and b"precision" in lib.atlas_last_error_string()
+    # too small a workspace is refused as well
+    rc = lib.atlas_polar_express_batched(dummy, dummy, 1, 8, 8, 5, 0.0, L.ATLAS_PREC_TENSOR, dummy, 16, None)
+    assert rc == L.ATLAS_ERR_WORKSPACE
