@@ -57,7 +57,7 @@ struct __align__(1024) Smem {
   float zbuf[2][E];
   float pbuf[2][E];                // gelu(W2 q) written by rank 1 into rank 0
   float ybuf[4][D];
-  float red[16];      // two alternating block-reduction buffers
+  float red[8];
   uint64_t bar[2];    // done[s]: MMAs of slot s complete
   uint64_t ready[2];  // ready[s]: slot s operand tiles published by the 8 epilogue warps
   uint32_t tmem;
@@ -241,7 +241,6 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
     }
   } else {  // ---- 8 epilogue warps ----
   asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
-  int rpar = 0;  // block_sum_epi buffer toggle
   float Sv[2][32], Wv[2][32];
   for (long k = cluster; k < total; k += nclusters) {
     const int q = (int)(k % K.nchains), c = (int)(k / K.nchains);
@@ -314,7 +313,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
         float ss = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
-        ss = block_sum_epi(ss, s.red, rpar);
+        ss = block_sum_epi(ss, s.red);
         const float inv = 1.0f / (sqrtf(ss + 1e-12f) * 1.01f + 1e-6f);
         inv0 = inv;
         if (P.ns_steps > 0) {

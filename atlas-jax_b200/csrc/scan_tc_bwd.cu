@@ -62,7 +62,7 @@ struct __align__(1024) Smem {
   float qv[D], dyv[D];
   float gate[4][MAXCS];  // alpha, eta, theta, gamma of the chunk
   float nrm[MAXCS];      // ||S_t||_F (with the 1e-12) per token, from phase B
-  float red[16];      // two alternating block-reduction buffers
+  float red[8];
   uint64_t bar;
   uint64_t bar2;         // completion barrier of the second in-flight Polar Express
   uint64_t bar_ld;       // bulk loads of saved Newton-Schulz tiles
@@ -431,7 +431,6 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     }
   } else {  // ---- 8 epilogue warps ----
   asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
-  int rpar = 0;  // block_sum_epi buffer toggle
   for (long kk = cluster; kk < total; kk += nclusters) {
     const int q = (int)(kk % K.nchains), j = (int)(kk / K.nchains), c = nch - 1 - j;
     const int b = q / H, hh = q % H;
@@ -498,7 +497,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
         float ss = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) ss = fmaf(Sv[0][jj], Sv[0][jj], fmaf(Sv[1][jj], Sv[1][jj], ss));
-        ss = block_sum_epi(ss, s.red, rpar);
+        ss = block_sum_epi(ss, s.red);
         const float nrm_r = sqrtf(ss + 1e-12f);
         const float inv = 1.0f / (nrm_r * 1.01f + 1e-6f);
         if (tid == 0) s.nrm[r] = nrm_r;
@@ -840,7 +839,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           if (l == 0) red_add(&w.scal[2 * MAXCS + r + 1], dt);
         }
         const float th = step ? s.gate[2][r + 1] : 1.f;
-        dot = block_sum_epi(dot, s.red, rpar);
+        dot = block_sum_epi(dot, s.red);
         const float coef = dot / (kap * kap) * 1.01f / nrm;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {

@@ -238,16 +238,11 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-// Same, over the 8 epilogue warps only (kernels with a dedicated MMA warp), with one
-// barrier: red holds two 8-float buffers used alternately (par, the calling thread's
-// toggle, flips every call and flips alike on every epilogue thread).  A buffer is
-// rewritten two calls later, after every thread has passed the barrier of the call in
-// between and so has finished reading it.
-__device__ __forceinline__ float block_sum_epi(float v, float* red2, int& par) {
+// Same, over the 8 epilogue warps only (kernels with a dedicated MMA warp).
+__device__ __forceinline__ float block_sum_epi(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  float* red = red2 + 8 * par;
-  par ^= 1;
+  asm volatile("bar.sync 1, 256;" ::: "memory");
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   asm volatile("bar.sync 1, 256;" ::: "memory");
   float s = 0;
