@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
       for (int term = 0; term < 3; ++term)
 #pragma unroll
         for (int ks = 0; ks < TK / 16; ++ks)
-          mma_bf16(tm, da[ta[term]] + ks * sa, db[tb[term]] + ks * sb, idesc, (i || term || ks) ? 1u : 0u);
+          mma_kf16(tm, da[ta[term]] + ks * sa, db[tb[term]] + ks * sb, idesc, (i || term || ks) ? 1u : 0u);
       mma_commit(&s.bar[st]);
     }
   };
@@ -258,13 +258,10 @@ __global__ void unwide_kernel(const float* X, float* Y, int64_t batch, int rows,
 }
 
 static cudaError_t gemm(const GemmArgs& g, int64_t batch, cudaStream_t s) {
-  static bool attr_set = false;
   const size_t smem = sizeof(Smem) + 1024;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  // per device (and cheap): set on every launch
+  cudaError_t e = cudaFuncSetAttribute(gemm3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
   for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
     const int nz = (int)std::min<int64_t>(65535, batch - z0);
     GemmArgs h = g;

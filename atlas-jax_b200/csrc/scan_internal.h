@@ -4,6 +4,8 @@
 #include <stdint.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "atlas_scan.h"
 
 namespace atlas {
@@ -34,6 +36,24 @@ struct BwdArgs {
   int* status;
 };
 
+// A host-side value computed once per device ordinal (occupancy-derived grid sizes
+// and the like), thread-safe.  Ordinals >= 64 compute it on every call.
+struct DeviceCache {
+  std::mutex mu;
+  int v[64];
+  DeviceCache() {
+    for (int& x : v) x = -1;
+  }
+  template <class F>
+  int get(F compute) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return compute();
+    std::lock_guard<std::mutex> lk(mu);
+    if (v[dev] < 0) v[dev] = compute();
+    return v[dev];
+  }
+};
+
 __host__ __device__ inline int n_chunks(const AtlasScanParams& p) { return (p.T + p.chunk - 1) / p.chunk; }
 
 namespace exact {
@@ -46,7 +66,7 @@ cudaError_t launch_pe(const float* X, float* Y, int64_t batch, int rows, int col
 size_t pe_workspace_bytes(int64_t batch, int rows, int cols, int steps);
 }  // namespace exact
 
-int* device_status_ptr();
+int* device_status_ptr();  // address of the status word on the current device
 // Test hooks for the bounded inter-cluster waits (set through
 // atlas_debug_set_wait_hooks): the ordering-flag threshold is raised by
 // flag_bias (0 in normal use) and the wait gives up after spin_limit polls.
@@ -55,7 +75,9 @@ struct WaitHooks {
   int spin_limit;
 };
 WaitHooks wait_hooks();
-int report_error(int code, const char* msg);  // sets atlas_last_error_string(), returns code  // address of the status word on the current device
+int report_error(int code, const char* msg);  // sets atlas_last_error_string(), returns code
+void clear_error();                           // atlas_last_error_string() -> ""
+int check_scan_params(const AtlasScanParams* p);  // the entry points' parameter checks (sets the message)
 
 // tcgen05 batched Polar Express for large matrices (Muon), pe_tc.cu
 namespace tcpe {

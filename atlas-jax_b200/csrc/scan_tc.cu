@@ -27,10 +27,12 @@
 //     (pe_consume) hand tiles to it through mbarriers.  The momentum / memory
 //     recurrences stay in token order.
 //
-// Numerics: every Polar Express product runs as three bf16 MMAs
-// (hi*hi + hi*lo + lo*hi, float32 accumulation in TMEM), i.e. ~16 mantissa bits
-// per operand.  A single bf16 pass is not enough: Polar Express amplifies noise
-// in the near-null directions of the low-rank momentum by ~1e3.
+// Numerics: every Polar Express product runs on split fp16 operands (hi + lo of
+// 256 x the value, ~22 significant bits; hi*hi + hi*lo + lo*hi, plus lo*lo in the
+// stacked products, float32 accumulation in TMEM).  A single 16-bit pass is not
+// enough: Polar Express amplifies noise in the near-null directions of the
+// low-rank momentum by ~1e3.  With this split the scan's error matches the
+// reference's own float32 arithmetic.
 //
 // Storage: each CTA keeps its matrix in the E x D orientation ("tile"): rank 0
 // holds W1^T and S1^T, rank 1 holds W2 and S2.  Polar Express of the wide D x E
@@ -349,9 +351,9 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
           tmem_ld32(sl[j].tm + lane_off + TM_X + 64 + dc, x1);
           tmem_wait_ld();
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            Wv[0][jj] = fmaf(al, Wv[0][jj], x0[jj]);
-            Wv[1][jj] = fmaf(al, Wv[1][jj], x1[jj]);
+          for (int jj = 0; jj < 32; ++jj) {  // TMEM holds KSPLIT^2 X_ns
+            Wv[0][jj] = fmaf(al, Wv[0][jj], x0[jj] * KUNSC2);
+            Wv[1][jj] = fmaf(al, Wv[1][jj], x1[jj] * KUNSC2);
           }
         } else {  // PE with zero steps is the normalisation alone
 #pragma unroll
@@ -460,7 +462,7 @@ size_t workspace_bytes(const AtlasScanParams& p) {
   return std::max(fwd_workspace_bytes(p), bwd_workspace_bytes(p));
 }
 
-static int g_max_clusters = -1;
+static DeviceCache g_max_clusters;  // resident 2-CTA clusters, per device
 
 template <typename TA>
 static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) {
@@ -478,13 +480,13 @@ static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (g_max_clusters < 0) {
+  const int maxc = g_max_clusters.get([&] {
     int n = 0;
     cfg.gridDim = dim3(2);
     if (cudaOccupancyMaxActiveClusters(&n, fwd_kernel<TA>, &cfg) != cudaSuccess || n <= 0) n = 1;
-    g_max_clusters = n;
-  }
-  cfg.gridDim = dim3(2 * std::min(nclusters, g_max_clusters));
+    return n;
+  });
+  cfg.gridDim = dim3(2 * std::min(nclusters, maxc));
   return cudaLaunchKernelEx(&cfg, fwd_kernel<TA>, k);
 }
 

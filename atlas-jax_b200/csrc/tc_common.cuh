@@ -1,6 +1,7 @@
 // Shared pieces of the tcgen05 scan kernels (forward and backward).
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "tc_ops.cuh"
@@ -14,10 +15,10 @@ constexpr int E = 256;
 constexpr int NT = 256;      // 8 warps: warp w -> TMEM lane quadrant w % 4, column half w / 4
 constexpr int MAXCS = 64;
 constexpr int DE = D * E;
-constexpr int XT_BYTES = E * D * 2;  // bf16 E x D tile
-constexpr int AT_BYTES = D * D * 2;  // bf16 D x D tile
+constexpr int XT_BYTES = E * D * 2;  // 16-bit E x D tile
+constexpr int AT_BYTES = D * D * 2;  // 16-bit D x D tile
 // X~, A, G~ and Ps live in "stacked" tiles of 128 columns: logical column d is
-// stored as its bf16 hi part at stacked column stk(d) = 32 * (d / 16) + d % 16 and
+// stored as its fp16 hi part at stacked column stk(d) = 32 * (d / 16) + d % 16 and
 // its lo part 16 columns later (XLO bytes on), i.e. blocks of 16 hi columns
 // alternate with blocks of 16 lo columns.  One M=128 x N=128 MMA over two stacked
 // tiles (both MN-major) then yields every hi/lo product pair Zx^T Yy, with the hi
@@ -53,34 +54,48 @@ __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Split 8 consecutive float32 values into bf16 hi and lo parts and store them
-// as one 16-byte core-matrix row segment in each tile.
-__device__ __forceinline__ void store_split8(uint8_t* th, uint8_t* tl, uint32_t off, const float* v) {
+// Operand split of every Polar Express product: a float32 value x is stored as two
+// fp16 parts of y = KSPLIT * x, hi = fp16(y) and lo = fp16(y - hi), so hi + lo holds
+// about 22 significant bits (fp16 has 11; the lo part's exponent keeps the residual
+// exact down to the fp16 subnormal floor).  The power-of-two pre-scale keeps the
+// small entries of the normalised iterates out of that floor.  Forward iterates are
+// bounded by the Frobenius normalisation: |X| <= 1.2, |A| <= 1.5, |B'| < 64, so
+// KSPLIT * |x| stays far below the fp16 maximum (65504).  A product of two split
+// operands accumulates KSPLIT^2 times the true value; KUNSC2 undoes that.
+// Compared with a bf16 split (8 + 8 bits) this is what lets B' = a I + b A + c A A
+// carry the a X term: the split's representation error of X, amplified by a <= 8.2
+// and by the five steps, was the tensor path's dominant error term.
+constexpr float KSPLIT = 256.f;
+constexpr float KUNSC2 = 1.f / 65536.f;
+
+// Split 8 consecutive float32 values (times scale) into fp16 hi and lo parts and
+// store them as one 16-byte core-matrix row segment in each tile.
+__device__ __forceinline__ void store_split8(uint8_t* th, uint8_t* tl, uint32_t off, const float* v,
+                                             float scale = KSPLIT) {
   uint32_t h[4], l[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    // packed conversions (one cvt.rn.bf16x2.f32 per pair); bf16 -> f32 is a bit shift
-    __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
-    uint32_t hb = *reinterpret_cast<uint32_t*>(&hv);
-    float r0 = v[2 * k] - __uint_as_float(hb << 16);
-    float r1 = v[2 * k + 1] - __uint_as_float(hb & 0xFFFF0000u);
-    __nv_bfloat162 lv = __floats2bfloat162_rn(r0, r1);
-    h[k] = hb;
-    l[k] = *reinterpret_cast<uint32_t*>(&lv);
+    const float y0 = v[2 * k] * scale, y1 = v[2 * k + 1] * scale;
+    const __half2 hv = __floats2half2_rn(y0, y1);  // .x (low half) = y0
+    const float2 hf = __half22float2(hv);
+    const __half2 lv = __floats2half2_rn(y0 - hf.x, y1 - hf.y);
+    h[k] = *reinterpret_cast<const uint32_t*>(&hv);
+    l[k] = *reinterpret_cast<const uint32_t*>(&lv);
   }
   *(uint4*)(th + off) = make_uint4(h[0], h[1], h[2], h[3]);
   *(uint4*)(tl + off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 // 32 consecutive columns [c0, c0+32) of row r of a tile with C columns.
-__device__ __forceinline__ void store_split32(uint8_t* th, uint8_t* tl, int r, int c0, int C, const float* v) {
+__device__ __forceinline__ void store_split32(uint8_t* th, uint8_t* tl, int r, int c0, int C, const float* v,
+                                              float scale = KSPLIT) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) store_split8(th, tl, cm_off(r, c0 + 8 * k, C), v + 8 * k);
+  for (int k = 0; k < 4; ++k) store_split8(th, tl, cm_off(r, c0 + 8 * k, C), v + 8 * k, scale);
 }
 // Logical columns [c0, c0+n) (c0 a multiple of 8) of row r of a stacked tile.
 template <int n>
-__device__ __forceinline__ void store_stk(uint8_t* t, int r, int c0, const float* v) {
+__device__ __forceinline__ void store_stk(uint8_t* t, int r, int c0, const float* v, float scale = KSPLIT) {
 #pragma unroll
-  for (int k = 0; k < n / 8; ++k) store_split8(t, t + XLO, cm_off(r, stk(c0 + 8 * k), XC), v + 8 * k);
+  for (int k = 0; k < n / 8; ++k) store_split8(t, t + XLO, cm_off(r, stk(c0 + 8 * k), XC), v + 8 * k, scale);
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
@@ -107,16 +122,16 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // Finishes one row of a stacked product whose 128 TMEM columns [64 ch, 64 ch + 64)
 // the lane loaded into v (hi parts of logical columns 32ch..+15, their lo parts,
 // then the same for 32ch+16..+31).  Lanes l < 16 hold the hi row i (Zh^T Yh | Zh^T Yl),
-// lanes l >= 16 the lo row i (Zl^T Yh | unused).  Afterwards lane l < 16 holds
-// columns 32ch..32ch+15 of  Zh^T Yh + Zh^T Yl + Zl^T Yh  in r[0..15], lane l + 16
-// columns 32ch+16..32ch+31.
-__device__ __forceinline__ void stack_finish(const float* v, float* r) {
+// lanes l >= 16 the lo row i (Zl^T Yh | Zl^T Yl).  Afterwards lane l < 16 holds
+// columns 32ch..32ch+15 of  unscale * (Zh^T Yh + Zh^T Yl + Zl^T Yh + Zl^T Yl)  in
+// r[0..15], lane l + 16 columns 32ch+16..32ch+31.
+__device__ __forceinline__ void stack_finish(const float* v, float* r, float unscale = KUNSC2) {
   const bool hi = (threadIdx.x & 16) == 0;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const float keep = hi ? v[j] + v[16 + j] : v[32 + j];
-    const float send = hi ? v[32 + j] + v[48 + j] : v[j];
-    r[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    const float keep = hi ? v[j] + v[16 + j] : v[32 + j] + v[48 + j];
+    const float send = hi ? v[32 + j] + v[48 + j] : v[j] + v[16 + j];
+    r[j] = unscale * (keep + __shfl_xor_sync(0xffffffffu, send, 16));
   }
 }
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
@@ -268,7 +283,7 @@ __device__ __forceinline__ float warp_reduce_scatter32(float* v) {
   return v[0];
 }
 
-// Three-term split product into TMEM column `tmd`:
+// Three-term split product (fp16 parts) into TMEM column `tmd`:
 //   D (+)= Ah*Bh + Ah*Bl + Al*Bh   (M x 64, contraction length K)
 // ca / cb are the column counts of the A / B core-matrix tiles: 64 for plain
 // tiles, XC for a stacked A tile (K-major only; al = ah + XLO).  amn / bmn pick the MN-major view (rows = K index)
@@ -276,24 +291,24 @@ __device__ __forceinline__ float warp_reduce_scatter32(float* v) {
 // tiles (selects the 128-row half for M = 128).  Descriptors are built once per
 // term; stepping K by 16 adds to the 14-bit start-address field (shared-memory
 // addresses < 256 KB never carry out of it).
-template <int K>
+template <int K, int NTERM = 3>
 __device__ __forceinline__ void mma3(uint32_t tmd, const uint8_t* ah, const uint8_t* al, bool amn, int ca,
                                      const uint8_t* bh, const uint8_t* bl, bool bmn, int cb, int M, uint32_t a_off,
                                      bool accumulate) {
-  const uint32_t id = idesc_bf16(M, 64, amn, bmn);
+  const uint32_t id = idesc_f16(M, 64, amn, bmn);
   // K-major stacked tiles hold 16 hi columns per 32 stacked columns: 512 bytes per 16 of K
   const uint64_t sa = amn ? (uint64_t)(2 * 16 * ca) >> 4 : (ca == XC ? (512 >> 4) : (256 >> 4));
   const uint64_t sb = bmn ? (uint64_t)(2 * 16 * cb) >> 4 : (256 >> 4);
-  const uint8_t* ta[3] = {ah, ah, al};
-  const uint8_t* tb[3] = {bh, bl, bh};
+  const uint8_t* ta[4] = {ah, ah, al, al};
+  const uint8_t* tb[4] = {bh, bl, bh, bl};
 #pragma unroll
-  for (int t = 0; t < 3; ++t) {
+  for (int t = 0; t < NTERM; ++t) {
     const uint32_t aa = smem_u32(ta[t]) + a_off, bb = smem_u32(tb[t]);
     const uint64_t da = amn ? desc_mnmajor(aa, ca) : desc_kmajor(aa, ca);
     const uint64_t db = bmn ? desc_mnmajor(bb, cb) : desc_kmajor(bb, cb);
 #pragma unroll
     for (int ks = 0; ks < K / 16; ++ks)
-      mma_bf16(tmd, da + ks * sa, db + ks * sb, id, (accumulate || t || ks) ? 1u : 0u);
+      mma_kf16(tmd, da + ks * sa, db + ks * sb, id, (accumulate || t || ks) ? 1u : 0u);
   }
 }
 
@@ -301,12 +316,12 @@ __device__ __forceinline__ void mma3(uint32_t tmd, const uint8_t* ah, const uint
 // M=128 x N=128 MMA per 16 of K; see stack_finish for the result layout.
 template <int K>
 __device__ __forceinline__ void mma_stack(uint32_t tmd, const uint8_t* z, const uint8_t* y, bool accumulate) {
-  const uint32_t id = idesc_bf16(128, 128, true, true);
+  const uint32_t id = idesc_f16(128, 128, true, true);
   const uint64_t dz = desc_mnmajor(smem_u32(z), XC), dy = desc_mnmajor(smem_u32(y), XC);
   constexpr uint64_t step = (uint64_t)(2 * 16 * XC) >> 4;
 #pragma unroll
   for (int ks = 0; ks < K / 16; ++ks)
-    mma_bf16(tmd, dz + ks * step, dy + ks * step, id, (accumulate || ks) ? 1u : 0u);
+    mma_kf16(tmd, dz + ks * step, dy + ks * step, id, (accumulate || ks) ? 1u : 0u);
 }
 
 // Optional phase timers (build with -DATLAS_PHASE_PROF; thread 0 accumulates
@@ -402,7 +417,7 @@ __device__ __forceinline__ void pe_publish(PEBars& B, int s) {
 }
 
 // Consumers (threads 0..255).  X0 of every slot is already stored by these threads.
-// On return each slot's final X~ is in TMEM (tm + TM_X, + 64).
+// On return each slot's final X~ is in TMEM (tm + TM_X, + 64), KSPLIT^2 times its value.
 //
 // Gram and A*A come back as hi/lo stacks (see stack_finish): warp w reads the
 // 64 columns of column half w / 4 of its lane quadrant, and each lane finishes 16
@@ -452,8 +467,8 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
         tmem_ld32(q.tm + lane_off + TM_X + dc, x0);
         tmem_ld32(q.tm + lane_off + TM_X + 64 + dc, x1);
         tmem_wait_ld();
-        store_stk<32>(q.Xh, e0, dc, x0);
-        store_stk<32>(q.Xh, e1, dc, x1);
+        store_stk<32>(q.Xh, e0, dc, x0, KSPLIT * KUNSC2);
+        store_stk<32>(q.Xh, e1, dc, x1, KSPLIT * KUNSC2);
       }
       if (p + 1 < P) pe_publish(B, s);
       if (prof && threadIdx.x == 0) prof[12] += clock64() - te;

@@ -56,10 +56,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor: kind::f16, A = B = fp16, D = f32.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                 // D format f32 (A and B format 0 = f16)
+         | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // MMA and commit are executed by a whole (converged) warp; one elected lane
 // issues.  Issuing from a full warp keeps the operands warp-uniform, which
 // measured ~38 cycles per small (64x64x16) MMA against ~60-70 from one thread.
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_kf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"

@@ -46,7 +46,7 @@ __global__ void selftest_gemm(const float* A, const float* B, float* D, int M, i
       uint32_t boff = bmn ? (uint32_t)(kb * 2) * (N * 16) : (uint32_t)kb * 256;
       uint64_t da = amn ? desc_mnmajor(smem_u32(sA) + aoff, M) : desc_kmajor(smem_u32(sA) + aoff, K);
       uint64_t db = bmn ? desc_mnmajor(smem_u32(sB) + boff, N) : desc_kmajor(smem_u32(sB) + boff, K);
-      mma_bf16(tm, da, db, id, kb > 0);
+      mma_kf16(tm, da, db, id, kb > 0);
     }
     mma_commit(&bar);
   }

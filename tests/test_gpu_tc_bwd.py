@@ -1,15 +1,17 @@
 """GPU parity of the tcgen05 backward scan against the oracle's float64 VJP.
 
-Tolerance 2e-2 relative (Frobenius) per gradient tensor (the bf16-activation
-bound of the north star); inputs are rounded to bf16 for both sides when the
-activations are bf16.
+Tolerance per gradient tensor: 2e-2 relative (Frobenius) with bf16 activations
+(inputs rounded to bf16 for both sides); with float32 activations
+max(2e-4, 2 x the float32 oracle VJP's own distance from the float64 one)
+(gpu_util.f32_bound_bwd): the reference's float32 accuracy up to the summation
+order of the scalar gate gradients.
 """
 import numpy as np
 import pytest
 import torch
 
 from oracle import atlas_oracle as O
-from gpu_util import rel, to_dev, to_np
+from gpu_util import check_errs, f32_bound_bwd, rel, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-2
@@ -51,14 +53,18 @@ def test_tc_backward(T, omega, ste, sg, act, xav):
     torch.cuda.synchronize()
     device_status()
     grads, dst = O.scan_backward(*ins, st, dy, dfin, cs, omega, 5, pe_ste=ste, stop_grad_chunks=sg)
-    errs = {}
+    if act == torch.float32:
+        g32, d32 = O.scan_backward(*ins, st, dy, dfin, cs, omega, 5, pe_ste=ste, stop_grad_chunks=sg,
+                                   dtype=np.float32)
+    errs, bounds = {}, {}
     for name, val in zip(("q", "k", "v", "alpha", "eta", "theta", "gamma"), res[:7]):
         errs[name] = rel(to_np(val), grads[name])
+        bounds[name] = TOL if act == torch.bfloat16 else f32_bound_bwd(g32[name], grads[name])
     for i, n in enumerate(("dW1", "dW2", "dS1", "dS2")):
         if np.abs(dst[i]).max() > 0:
             errs[n] = rel(to_np(res[7][i]), dst[i])
-    print({k_: f"{v_:.2e}" for k_, v_ in errs.items()})
-    assert max(errs.values()) < TOL, errs
+            bounds[n] = TOL if act == torch.bfloat16 else f32_bound_bwd(d32[i], dst[i])
+    check_errs(errs, bounds)
 
 
 @pytest.mark.parametrize("T,chunk,omega,ns", [(40, 32, 64, 5), (64, 64, 16, 2), (1, 64, 16, 5)])
@@ -76,8 +82,11 @@ def test_tc_backward_edge_cases(T, chunk, omega, ns):
     res = scan_backward(*dev, saved, to_dev(dy), None, cfg, E)
     torch.cuda.synchronize()
     grads, dst = O.scan_backward(*ins, st, dy, None, chunk, omega, ns)
-    errs = {n: rel(to_np(v_), grads[n]) for n, v_ in zip(("q", "k", "v", "alpha", "eta", "theta", "gamma"), res[:7])}
+    g32, d32 = O.scan_backward(*ins, st, dy, None, chunk, omega, ns, dtype=np.float32)
+    names = ("q", "k", "v", "alpha", "eta", "theta", "gamma")
+    errs = {n: rel(to_np(v_), grads[n]) for n, v_ in zip(names, res[:7])}
+    bounds = {n: f32_bound_bwd(g32[n], grads[n]) for n in names}
     for i, n in enumerate(("dW1", "dW2", "dS1", "dS2")):
         if np.abs(dst[i]).max() > 0:
-            errs[n] = rel(to_np(res[7][i]), dst[i])
-    assert max(errs.values()) < TOL, errs
+            errs[n], bounds[n] = rel(to_np(res[7][i]), dst[i]), f32_bound_bwd(d32[i], dst[i])
+    check_errs(errs, bounds)

@@ -1,16 +1,17 @@
 """GPU parity of the tcgen05 forward scan against the oracle.
 
-Tolerance (north_star): 2e-2 relative (Frobenius) with bf16 activations; the
-float32-activation runs are held to the same bound because the tensor path's
-three-term bf16 split is the accuracy limit, not the activation dtype.  The
-oracle runs in float64 on the same (bf16-rounded where applicable) inputs.
+Tolerances (north_star): 2e-2 relative (Frobenius) with bf16 activations; with
+float32 activations every output must be as close to the float64 oracle as
+max(1e-4, 1.5 x the float32 oracle's own distance from it) -- the accuracy of the
+reference's float32 arithmetic (gpu_util.f32_bound).  The oracle runs on the same
+(bf16-rounded where applicable) inputs.
 """
 import numpy as np
 import pytest
 import torch
 
 from oracle import atlas_oracle as O
-from gpu_util import rel, to_dev, to_np
+from gpu_util import check_errs, f32_bound, rel, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-2
@@ -41,10 +42,16 @@ def test_tc_forward_lm_init(act):
     if act == torch.bfloat16:
         ins = tuple(_bf(x) for x in ins[:3]) + tuple(ins[3:])
     y, out = _run(ins, None, act)
-    y_o, fin = O.scan_forward(*ins, O.lm_initial_state(B, H, 64, 256), 64, 16, 5, dtype=np.float64)
-    errs = [rel(y, y_o)] + [rel(a, b) for a, b in zip(out, fin)]
-    print("rel errors y,W1,W2,S1,S2:", errs)
-    assert max(errs) < TOL, errs
+    st0 = O.lm_initial_state(B, H, 64, 256)
+    y_o, fin = O.scan_forward(*ins, st0, 64, 16, 5, dtype=np.float64)
+    names = ("y", "W1", "W2", "S1", "S2")
+    errs = dict(zip(names, [rel(y, y_o)] + [rel(a, b) for a, b in zip(out, fin)]))
+    if act == torch.bfloat16:
+        bounds = dict.fromkeys(names, TOL)
+    else:
+        y32, fin32 = O.scan_forward(*ins, st0, 64, 16, 5, dtype=np.float32)
+        bounds = dict(zip(names, [f32_bound(y32, y_o)] + [f32_bound(a, b) for a, b in zip(fin32, fin)]))
+    check_errs(errs, bounds)
 
 
 def test_tc_forward_padding_xavier_random_gamma():
@@ -54,9 +61,10 @@ def test_tc_forward_padding_xavier_random_gamma():
     st = (st[0], st[1], 0.05 * st[0], 0.05 * st[1])
     y, out = _run(ins, st, torch.float32, omega=4)
     y_o, fin = O.scan_forward(*ins, st, 64, 4, 5, dtype=np.float64)
-    errs = [rel(y, y_o)] + [rel(a, b) for a, b in zip(out[:2], fin[:2])]
-    print("rel errors:", errs)
-    assert max(errs) < TOL, errs
+    y32, fin32 = O.scan_forward(*ins, st, 64, 4, 5, dtype=np.float32)
+    errs = {"y": rel(y, y_o), "W1": rel(out[0], fin[0]), "W2": rel(out[1], fin[1])}
+    check_errs(errs, {"y": f32_bound(y32, y_o), "W1": f32_bound(fin32[0], fin[0]),
+                      "W2": f32_bound(fin32[1], fin[1])})
     assert np.all(out[2] == 0) and np.all(out[3] == 0)  # padded tail zeroes S (memory_layer.py:657)
 
 
@@ -89,8 +97,12 @@ def test_tc_forward_edge_cases(T, chunk, omega, ns):
                              tuple(to_dev(x) for x in st), cfg)
     torch.cuda.synchronize()
     y_o, fin = O.scan_forward(*ins, st, chunk, omega, ns, dtype=np.float64)
-    errs = [rel(to_np(y), y_o)] + [rel(to_np(a_), b_) for a_, b_ in zip(out, fin) if np.abs(b_).max() > 0]
-    assert max(errs) < TOL, errs
+    y32, fin32 = O.scan_forward(*ins, st, chunk, omega, ns, dtype=np.float32)
+    errs, bounds = {"y": rel(to_np(y), y_o)}, {"y": f32_bound(y32, y_o)}
+    for i, (a_, b_, c_) in enumerate(zip(out, fin, fin32)):
+        if np.abs(b_).max() > 0:
+            errs[f"state{i}"], bounds[f"state{i}"] = rel(to_np(a_), b_), f32_bound(c_, b_)
+    check_errs(errs, bounds)
 
 
 def test_tc_forward_sweep_384_chains():
