@@ -9,7 +9,7 @@ import os
 import re
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libatlas_scan.so")
+LIB_PATH = os.environ.get("ATLAS_LIB_PATH") or os.path.join(_HERE, "libatlas_scan.so")
 HEADER = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "include", "atlas_scan.h")
 
 ATLAS_ABI_VERSION = 1
@@ -69,6 +69,11 @@ def load():
     lib.atlas_debug_set_wait_hooks.argtypes = [ctypes.c_int32, ctypes.c_int32]
     lib.atlas_scan_fwd_noalloc.restype = ctypes.c_int
     lib.atlas_scan_fwd_noalloc.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 4 + [_P] + [_F] * 4 + [_P]
+    lib.atlas_xla_opaque_bytes.restype = ctypes.c_size_t
+    lib.atlas_xla_pe_opaque_bytes.restype = ctypes.c_size_t
+    for n in ("atlas_xla_fwd", "atlas_xla_bwd", "atlas_xla_polar_express"):
+        getattr(lib, n).restype = None
+        getattr(lib, n).argtypes = [_P, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p, ctypes.c_size_t, _P]
     if lib.atlas_abi_version() != ATLAS_ABI_VERSION:
         raise OSError(f"libatlas_scan ABI {lib.atlas_abi_version()} != {ATLAS_ABI_VERSION}")
     _lib = lib

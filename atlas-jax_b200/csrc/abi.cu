@@ -1,5 +1,6 @@
 // C ABI entry points (include/atlas_scan.h): argument checks, dispatch to the
 // exact or the tcgen05 implementation, error reporting.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -17,11 +18,12 @@ int* device_status_ptr() {
   if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
   return (int*)p;
 }
-static WaitHooks g_hooks = {0, 50000000};
-WaitHooks wait_hooks() { return g_hooks; }
+// test hooks of the bounded waits (atlas_debug_set_wait_hooks), read at every launch
+static std::atomic<int> g_flag_bias{0}, g_spin_limit{50000000};
+WaitHooks wait_hooks() { return WaitHooks{g_flag_bias.load(), g_spin_limit.load()}; }
 void set_wait_hooks(int bias, int limit) {
-  g_hooks.flag_bias = bias;
-  g_hooks.spin_limit = limit > 0 ? limit : 50000000;
+  g_flag_bias.store(bias);
+  g_spin_limit.store(limit > 0 ? limit : 50000000);
 }
 }  // namespace atlas
 
@@ -64,6 +66,8 @@ int cuda_result(cudaError_t e, const char* what) {
 }  // namespace
 
 int atlas::report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+void atlas::clear_error() { g_err.clear(); }
+int atlas::check_scan_params(const AtlasScanParams* p) { return check_params(p); }
 
 extern "C" {
 

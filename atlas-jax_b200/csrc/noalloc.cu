@@ -47,8 +47,10 @@ extern "C" int atlas_scan_fwd_noalloc(const AtlasScanParams* p, const void* q, c
                                       const float* gamma, const float* W1_in, const float* W2_in,
                                       const float* S1_in, const float* S2_in, void* y, float* W1_out,
                                       float* W2_out, float* S1_out, float* S2_out, void* stream) {
+  atlas::clear_error();
   // argument checks shared with the other entry points (sets the error string)
-  if (atlas_scan_saved_bytes(p) == 0) return ATLAS_ERR_INVALID_ARGUMENT;
+  const int rc0 = atlas::check_scan_params(p);
+  if (rc0) return rc0;
   if (p->precision != ATLAS_PREC_TENSOR)
     return atlas::report_error(ATLAS_ERR_UNSUPPORTED, "atlas_scan_fwd_noalloc supports ATLAS_PREC_TENSOR only");
   if ((long)p->B * p->H > ATLAS_NOALLOC_MAX_CHAINS)

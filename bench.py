@@ -19,6 +19,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -46,22 +47,29 @@ def _peaks():
         return 1400.0, 6650.0, "fallback"
 
 
-def cpu_baseline(sample_T=64, sample_H=4, threads=None):
-    """Times the oracle (numpy restatement of the reference scan) fwd+bwd on one
-    layer of B=1, H=sample_H, T=sample_T, D=64; returns full-model tokens/s
-    (a full token passes 12 heads x 12 layers)."""
+CPU_SAMPLE = dict(B=1, H=12, T=128)  # two chunks per head: the cross-chunk carry path is in the sample
+
+
+def cpu_baseline():
+    """Times the oracle (numpy restatement of the reference scan, float32, BLAS on all
+    host threads) fwd+bwd on one layer of B=1, H=12, T=128, D=64 (two chunks per head);
+    returns full-model tokens/s (a full token passes 12 heads x 12 layers)."""
     import numpy as np
     from oracle import atlas_oracle as O
-    c = CFG
-    ins = O.make_inputs(1, sample_T, sample_H, c["D"], seed=0)
-    st = O.lm_initial_state(1, sample_H, c["D"], c["E"])
+    c, smp = CFG, CPU_SAMPLE
+    ins = O.make_inputs(smp["B"], smp["T"], smp["H"], c["D"], seed=0)
+    st = O.lm_initial_state(smp["B"], smp["H"], c["D"], c["E"])
     t0 = time.perf_counter()
     y, _ = O.scan_forward(*ins, st, c["chunk"], c["omega"], c["ns_steps"])
     dy = np.ones_like(y)
     O.scan_backward(*ins, st, dy, None, c["chunk"], c["omega"], c["ns_steps"], dtype=np.float32)
     dt = time.perf_counter() - t0
-    equiv_tokens = sample_T * sample_H / (c["H"] * c["layers"])
+    equiv_tokens = smp["B"] * smp["T"] * smp["H"] / (c["H"] * c["layers"])
     return equiv_tokens / dt, dt, os.cpu_count()
+
+
+CPU_SAMPLE_TEXT = ("oracle numpy restatement (float32), fwd+bwd of 1 layer, B=1 H=12 T=128 (2 chunks) D=64 E=256, "
+                   "scaled to 12 heads x 12 layers per token")
 
 
 def reference_arm(args, rank):
@@ -73,7 +81,7 @@ def reference_arm(args, rank):
         if i >= args.warmup:
             vals.append(v)
     v = sorted(vals)[len(vals) // 2]
-    sample = "oracle numpy restatement, fwd+bwd of 1 layer, B=1 H=4 T=64 D=64 E=256, scaled to 12 heads x 12 layers"
+    sample = CPU_SAMPLE_TEXT
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
@@ -123,6 +131,65 @@ class Clocks:
             return None
         sm.sort()
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def f32_mode(lib, L, dev, stream, sp, p_bf16, nws, ws, g, world, layers=2, reps=2):
+    """The same scan with float32 activations (the reference's float32 path, held to
+    its float32 accuracy): `layers` layers of fwd+bwd, one untimed pass, then `reps`
+    timed passes; tokens/s of the 12-layer step implied by the per-layer time."""
+    import torch
+    c = CFG
+    B, T, H, D, E = c["B"], c["T"], c["H"], c["D"], c["E"]
+    p = L.AtlasScanParams(*[getattr(p_bf16, n) for n, _ in L.AtlasScanParams._fields_])
+    p.act_dtype = L.ATLAS_F32
+    pp = ctypes.byref(p)
+    if lib.atlas_scan_workspace_bytes(pp) > nws:
+        return None
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    Ls = []
+    for _ in range(layers):
+        Ld = {n: torch.nn.functional.normalize(torch.randn(B, T, H, D, device=dev, generator=g), dim=-1)
+              for n in ("q", "k", "v")}
+        for n, mu in (("alpha", 3.0), ("eta", -3.0), ("theta", 1.0), ("gamma", 0.0)):
+            Ld[n] = torch.sigmoid(mu + 0.5 * torch.randn(B, T, H, device=dev, generator=g))
+        Ld["dy"] = torch.randn(B, T, H, D, device=dev, generator=g) * 0.01
+        for n in ("y", "dq", "dk", "dv"):
+            Ld[n] = torch.empty_like(Ld["q"])
+        for n in ("dalpha", "deta", "dtheta", "dgamma"):
+            Ld[n] = torch.empty(B, T, H, device=dev)
+        Ld["saved"] = torch.empty(lib.atlas_scan_saved_bytes(pp), dtype=torch.uint8, device=dev)
+        Ls.append(Ld)
+    so = [torch.empty(B, H, D, E, device=dev), torch.empty(B, H, E, D, device=dev),
+          torch.empty(B, H, D, E, device=dev), torch.empty(B, H, E, D, device=dev)]
+    di = [torch.empty_like(x) for x in so]
+
+    def one():
+        for Ld in Ls:
+            L.check(lib.atlas_scan_fwd(pp, P(Ld["q"]), P(Ld["k"]), P(Ld["v"]), P(Ld["alpha"]), P(Ld["eta"]),
+                                       P(Ld["theta"]), P(Ld["gamma"]), None, None, None, None, P(Ld["y"]),
+                                       *[P(x) for x in so], P(Ld["saved"]), P(ws), nws, sp))
+        for Ld in reversed(Ls):
+            L.check(lib.atlas_scan_bwd(pp, P(Ld["q"]), P(Ld["k"]), P(Ld["v"]), P(Ld["alpha"]), P(Ld["eta"]),
+                                       P(Ld["theta"]), P(Ld["gamma"]), P(Ld["saved"]), P(Ld["dy"]), None, None,
+                                       None, None, P(Ld["dq"]), P(Ld["dk"]), P(Ld["dv"]), P(Ld["dalpha"]),
+                                       P(Ld["deta"]), P(Ld["dtheta"]), P(Ld["dgamma"]), *[P(x) for x in di],
+                                       P(ws), nws, sp))
+    one()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(reps):
+        one()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    L.check(lib.atlas_scan_status())
+    from atlas_b200 import dp
+    ms_layer = dp.max_over_ranks(t0.elapsed_time(t1)) / (reps * layers)
+    step_ms = ms_layer * c["layers"]
+    return {"value": B * T * world / (step_ms / 1e3), "unit": "tokens/s", "dtype": "f32",
+            "ms_per_layer_fwd_bwd": ms_layer,
+            "how": f"{layers} layers fwd+bwd x {reps} timed passes with float32 q/k/v/dy, per-layer time x "
+                   f"{c['layers']} layers (no all-reduce)"}
 
 
 def gpu_arm(args, rank, world):
@@ -217,8 +284,7 @@ def gpu_arm(args, rank, world):
         step()
     torch.cuda.synchronize()
     L.check(lib.atlas_scan_status())
-    clocks = Clocks(os.path.join(HERE, "gpurun_out" if os.path.isdir(os.path.join(HERE, "gpurun_out"))
-                                 else ".", f"clocks_rank{rank}.csv"))
+    clocks = Clocks(os.path.join(tempfile.gettempdir(), f"atlas_bench_clocks_{os.getpid()}_rank{rank}.csv"))
     barrier()
     torch.cuda.synchronize()
     clocks.start()
@@ -259,13 +325,14 @@ def gpu_arm(args, rank, world):
         e2e_ms = dp.max_over_ranks(t0.elapsed_time(t1)) / e2e_steps
         e2e = tokens / (e2e_ms / 1e3)
 
+    f32 = None if args.no_f32 else f32_mode(lib, L, dev, stream, sp, p, nws, ws, g, world)
     peak_tf, hbm, peak_kind = _peaks()
     f_bwd = B * T * H * F_BWD(D, c["ns_steps"])
     f_fwd = B * T * H * F_FWD(D, c["ns_steps"])
     dom_ms, dom_f, dom = (bwd_ms, f_bwd, "tc_bwd_kernel") if bwd_ms >= fwd_ms else (fwd_ms, f_fwd, "tc_fwd_kernel")
     achieved = dom_f / (dom_ms / 1e3) / 1e12
     out = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": value, "value_per_gpu": value / world, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"170M Atlas scan fwd+bwd, {NL} layers, per GPU B={B} T={T} H={H} D={D} "
@@ -283,12 +350,12 @@ def gpu_arm(args, rank, world):
                      "fwd_ms_per_layer": fwd_ms, "bwd_ms_per_layer": bwd_ms},
         "gpu_launches": 2 * NL * args.steps,
         "clocks": ck,
+        "f32_activations": f32,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         v, dt, cores = cpu_baseline()
         out["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                               "sample": f"oracle numpy fwd+bwd, 1 layer B=1 H=4 T=64 ({dt:.1f} s), "
-                                         "scaled to 12 heads x 12 layers"}
+                               "sample": f"{CPU_SAMPLE_TEXT} ({dt:.1f} s)"}
     if rank == 0:
         print(json.dumps(out), flush=True)
 
@@ -303,10 +370,12 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="profiling only: fewer layers")
     ap.add_argument("--seq", type=int, default=CFG["T"], help="profiling only: shorter sequences")
     ap.add_argument("--no-e2e", action="store_true", help="profiling only: skip the end-to-end leg")
+    ap.add_argument("--no-f32", action="store_true", help="skip the float32-activation leg")
     args = ap.parse_args()
     if args.layers != CFG["layers"] or args.seq != CFG["T"]:
         CFG["layers"], CFG["T"] = args.layers, args.seq
         args.no_cpu = True
+        args.no_f32 = True
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

@@ -7,7 +7,8 @@
  * inner fused-kernel boundary it dispatches to (fused_chunk_scan_kernel,
  * memory_layer.py:535-541 -> atlas_jax/kernels/fused_chunk.py:321-379, a
  * jax.custom_vjp whose backward is JAX recompute + vjp, fused_chunk.py:366-376).
- * A jax.ffi registration binds these entry points one-to-one.
+ * A jax.ffi / XLA custom-call registration binds these entry points one-to-one
+ * (the atlas_xla_* adapters below).
  *
  * Conventions
  *  - All buffers are caller-owned DEVICE pointers; no entry point allocates.
@@ -26,8 +27,19 @@
  *    asynchronous; a returned ATLAS_OK means "launched".  Device-side failures
  *    (bounded waits that expired) are reported in the status word that
  *    atlas_scan_status() reads after the stream is synchronised.
- *  - Thread safety: entry points keep no global mutable state except a
- *    thread-local error string.
+ *  - Thread safety: any thread may call any entry point.  The error message is
+ *    thread-local.  Process-wide state: per-device caches of launch sizes (filled
+ *    once under a mutex), the wait-limit test hooks (atomics), and one device
+ *    status word per GPU, shared by every stream and thread on that GPU: a
+ *    bounded wait that expires in any call sets it, and atlas_scan_status()
+ *    reads and clears it for everyone.
+ *  - The tensor-path kernels are persistent: clusters of one launch wait on each
+ *    other's chunks, so every cluster of the grid must be resident at once.  The
+ *    grid is sized to the device's resident-cluster capacity; kernels of other
+ *    work running concurrently on the same GPU can keep clusters from starting,
+ *    in which case the waits expire (ATLAS_ERR_DEVICE_TIMEOUT in the status
+ *    word) instead of hanging.  Run the scan without concurrent kernels on its
+ *    GPU.
  */
 #ifndef ATLAS_SCAN_H_
 #define ATLAS_SCAN_H_
@@ -59,9 +71,10 @@ enum {
   /* float64 CUDA-core arithmetic: reproduces the reference's math well below its
    * own float32 rounding noise.  For parity runs and small shapes. */
   ATLAS_PREC_EXACT = 0,
-  /* tcgen05 tensor cores with a three-term bf16 split (hi*hi + hi*lo + lo*hi,
-   * float32 accumulation) for every Polar Express product, float32 carries.
-   * The production path. */
+  /* tcgen05 tensor cores, every Polar Express product on split fp16 operands
+   * (hi + lo of a power-of-two multiple of the value, float32 accumulation),
+   * float32 carries: as accurate as the reference's float32 arithmetic.  The
+   * production path. */
   ATLAS_PREC_TENSOR = 1
 };
 
@@ -153,6 +166,39 @@ int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t
 /* Scratch bytes atlas_polar_express_batched needs for this problem. */
 size_t atlas_polar_express_workspace_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ns_steps,
                                            int32_t precision);
+
+/* XLA custom-call adapters (status-returning legacy signature, api_version 2):
+ *   void fn(cudaStream_t stream, void** buffers, const char* opaque, size_t opaque_len,
+ *           XlaCustomCallStatus* status)
+ * `opaque` is one packed AtlasScanParams (atlas_xla_opaque_bytes() bytes).  They are
+ * the jax.ffi registration targets that replace the custom-VJP pair
+ * fused_chunk_scan_kernel (atlas_jax/kernels/fused_chunk.py:321-379, called at
+ * atlas_jax/memory_layer.py:535-541) with the whole scan (memory_layer.py:635-718).
+ * Failures go to XlaCustomCallStatusSetFailure when the process exports it and to
+ * atlas_last_error_string() of the calling thread.
+ *
+ * atlas_xla_fwd buffers (operands, then results):
+ *   0 q  1 k  2 v  3 alpha  4 eta  5 theta  6 gamma  7 W1_in  8 W2_in  9 S1_in  10 S2_in
+ *   11 y  12 W1_out  13 W2_out  14 S1_out  15 S2_out  16 saved  17 workspace
+ * atlas_xla_bwd buffers:
+ *   0 q  1 k  2 v  3 alpha  4 eta  5 theta  6 gamma  7 saved  8 dy
+ *   9 dW1_out  10 dW2_out  11 dS1_out  12 dS2_out
+ *   13 dq  14 dk  15 dv  16 dalpha  17 deta  18 dtheta  19 dgamma
+ *   20 dW1_in  21 dW2_in  22 dS1_in  23 dS2_in  24 workspace
+ * Every buffer is present (gamma all ones when unused, the initial state explicit,
+ * zero final-state cotangents); saved / workspace have atlas_scan_saved_bytes() /
+ * atlas_scan_workspace_bytes() bytes. */
+size_t atlas_xla_opaque_bytes(void);
+void atlas_xla_fwd(void* stream, void** buffers, const char* opaque, size_t opaque_len, void* status);
+void atlas_xla_bwd(void* stream, void** buffers, const char* opaque, size_t opaque_len, void* status);
+
+/* XLA adapter of atlas_polar_express_batched, the target that replaces the Muon
+ * orthogonalisation of atlas_jax/optim.py:68-83.  Buffers: 0 X, 1 Y, 2 workspace
+ * (atlas_polar_express_workspace_bytes()).  `opaque` is the packed struct
+ *   { int64 batch; int32 rows, cols, ns_steps, precision; float eps_in_sqrt; int32 pad; }
+ * of atlas_xla_pe_opaque_bytes() bytes. */
+size_t atlas_xla_pe_opaque_bytes(void);
+void atlas_xla_polar_express(void* stream, void** buffers, const char* opaque, size_t opaque_len, void* status);
 
 /* Reads and clears the device status word of the calling device after the
  * caller synchronised the stream (ATLAS_OK or ATLAS_ERR_DEVICE_TIMEOUT). */

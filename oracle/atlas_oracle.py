@@ -382,7 +382,13 @@ def _prepare(q, k, v, alpha, eta, theta, gamma, chunk, dtype):
     alpha = _pad(cast(alpha), pad, 1.0)                     # memory_layer.py:655
     eta = _pad(cast(eta), pad, 0.0)
     theta = _pad(cast(theta), pad, 0.0)
-    gamma = _pad(cast(gamma), pad, 0.0) if gamma is not None else np.zeros_like(alpha)
+    # gamma=None means all ones, as a NULL gamma does at the C ABI (the reference
+    # passes a gate only when omega > 1, memory_layer.py:435-438, 627-633)
+    if gamma is None:
+        gamma = np.ones(alpha.shape, dtype)
+        gamma[:, T:] = 0.0
+    else:
+        gamma = _pad(cast(gamma), pad, 0.0)
     return T, q, k, v, alpha, eta, theta, gamma
 
 

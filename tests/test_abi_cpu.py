@@ -64,3 +64,40 @@ def test_polar_express_precisions():
     # too small a workspace is refused as well
     rc = lib.atlas_polar_express_batched(dummy, dummy, 1, 8, 8, 5, 0.0, L.ATLAS_PREC_TENSOR, dummy, 16, None)
     assert rc == L.ATLAS_ERR_WORKSPACE
+
+
+def test_xla_adapters_reject_bad_opaque_and_report():
+    """The XLA custom-call adapters validate the packed params before any device work
+    and leave the message in atlas_last_error_string (status pointer NULL: no XLA)."""
+    lib = L.load()
+    assert lib.atlas_xla_opaque_bytes() == ctypes.sizeof(L.AtlasScanParams)
+    bufs = (ctypes.c_void_p * 25)()
+    lib.atlas_xla_fwd(None, bufs, b"short", 5, None)
+    assert b"opaque" in lib.atlas_last_error_string()
+    bad = _p(ns_steps=9)
+    lib.atlas_xla_bwd(None, bufs, ctypes.string_at(ctypes.byref(bad), ctypes.sizeof(bad)), ctypes.sizeof(bad), None)
+    assert b"ns_steps" in lib.atlas_last_error_string()
+
+
+def test_noalloc_clears_error_and_returns_param_code():
+    """atlas_scan_fwd_noalloc reports check failures with their own code (an
+    unsupported tensor-path shape is ATLAS_ERR_UNSUPPORTED) and starts every call
+    with an empty message."""
+    lib = L.load()
+    p = _p(precision=L.ATLAS_PREC_TENSOR)  # D=32: valid, but not a tensor-path shape
+    rc = lib.atlas_scan_fwd_noalloc(ctypes.byref(p), *([None] * 16), None)
+    assert rc == L.ATLAS_ERR_UNSUPPORTED and b"tensor path" in lib.atlas_last_error_string()
+    bad = _p(ns_steps=9)
+    rc = lib.atlas_scan_fwd_noalloc(ctypes.byref(bad), *([None] * 16), None)
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT and b"ns_steps" in lib.atlas_last_error_string()
+
+
+def test_xla_polar_express_opaque_layout():
+    """The Muon adapter's opaque is {int64 batch; int32 rows, cols, ns_steps, precision;
+    float eps; int32 pad}, packed as the JAX binding packs it."""
+    import struct
+    lib = L.load()
+    assert lib.atlas_xla_pe_opaque_bytes() == struct.calcsize("<qiiiifi") == 32
+    bufs = (ctypes.c_void_p * 3)()
+    lib.atlas_xla_polar_express(None, bufs, b"x" * 8, 8, None)
+    assert b"AtlasXlaPEOpaque" in lib.atlas_last_error_string()

@@ -174,3 +174,12 @@ def test_oracle_matches_golden_config0():
     assert rel < 1e-6
     for n, x in zip(("W1", "W2", "S1", "S2"), fin):
         assert np.linalg.norm(x - gold[f"lm_{n}"]) <= 1e-6 * np.linalg.norm(gold[f"lm_{n}"])
+
+
+def test_gamma_none_means_ones():
+    """A missing gamma gate is all ones, as a NULL gamma at the C ABI."""
+    ins = O.make_inputs(1, 70, 2, 16, seed=5)
+    st = O.lm_initial_state(1, 2, 16, 64)
+    y1, s1 = O.scan_forward(*ins[:6], None, st, 32, 4, 2)
+    y2, s2 = O.scan_forward(*ins[:6], np.ones_like(ins[5]), st, 32, 4, 2)
+    assert np.array_equal(y1, y2) and all(np.array_equal(a, b) for a, b in zip(s1, s2))
