@@ -16,7 +16,7 @@ ATLAS_ABI_VERSION = 1
 ATLAS_OK, ATLAS_ERR_INVALID_ARGUMENT, ATLAS_ERR_UNSUPPORTED, ATLAS_ERR_CUDA, ATLAS_ERR_DEVICE_TIMEOUT, \
     ATLAS_ERR_WORKSPACE = range(6)
 ATLAS_F32, ATLAS_BF16 = 0, 1
-ATLAS_PREC_EXACT, ATLAS_PREC_TENSOR = 0, 1
+ATLAS_PREC_EXACT, ATLAS_PREC_TENSOR, ATLAS_PREC_TENSOR_BATCHED = 0, 1, 2
 
 
 class AtlasScanParams(ctypes.Structure):
@@ -69,6 +69,11 @@ def load():
     lib.atlas_debug_set_wait_hooks.argtypes = [ctypes.c_int32, ctypes.c_int32]
     lib.atlas_scan_fwd_noalloc.restype = ctypes.c_int
     lib.atlas_scan_fwd_noalloc.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 4 + [_P] + [_F] * 4 + [_P]
+    lib.atlas_linear_scan_workspace_bytes.restype = ctypes.c_size_t
+    lib.atlas_linear_scan_workspace_bytes.argtypes = [pp]
+    lib.atlas_linear_scan_fwd.restype = ctypes.c_int
+    lib.atlas_linear_scan_fwd.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 2 + [_P] + [_F] * 2 + [_P, ctypes.c_size_t,
+                                                                                                  _P]
     lib.atlas_xla_opaque_bytes.restype = ctypes.c_size_t
     lib.atlas_xla_pe_opaque_bytes.restype = ctypes.c_size_t
     for n in ("atlas_xla_fwd", "atlas_xla_bwd", "atlas_xla_polar_express"):

@@ -129,6 +129,34 @@ def scan_backward(q, k, v, alpha, eta, theta, gamma, saved, dy, dstate=None, cfg
     return dq, dk, dv, g[0], g[1], g[2], g[3], dst
 
 
+def linear_scan_forward(q, k, v, alpha, eta, theta, gamma=None, state=None, cfg=ScanConfig(), workspace=None):
+    """Linear-memory scan (memory_layer.py:468-494), forward: q,k,v (B,T,H,D); gates
+    (B,T,H) float32; state (M, S) each (B,H,D,D) float32 or None (zeros).
+    Returns (y, (M, S)).  Runs the batched tensor-path forward."""
+    lib = L.load()
+    B, T, H, D = q.shape
+    dev = q.device
+    for n, x in (("k", k), ("v", v)):
+        _check_act(x, n, q.dtype, (B, T, H, D))
+    for n, x in (("alpha", alpha), ("eta", eta), ("theta", theta), ("gamma", gamma)):
+        if x is not None:
+            _check_act(x, n, torch.float32, (B, T, H))
+    prec = cfg.precision if cfg.precision != L.ATLAS_PREC_EXACT else L.ATLAS_PREC_TENSOR_BATCHED
+    p = _params(ScanConfig(cfg.chunk, cfg.omega, cfg.ns_steps, cfg.pe_ste, cfg.stop_grad_chunks, prec), B, T, H,
+                D, D, q.dtype)
+    y = torch.empty_like(q)
+    out = (torch.empty(B, H, D, D, device=dev), torch.empty(B, H, D, D, device=dev))
+    need = lib.atlas_linear_scan_workspace_bytes(ctypes.byref(p))
+    if need == 0:
+        raise L.AtlasError(L.ATLAS_ERR_UNSUPPORTED, lib.atlas_last_error_string().decode())
+    ws, wsb = (workspace or _WS).get(need, dev)
+    st = [None, None] if state is None else [s.contiguous() for s in state]
+    L.check(lib.atlas_linear_scan_fwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(eta),
+                                      _ptr(theta), _ptr(gamma), _ptr(st[0]), _ptr(st[1]), _ptr(y),
+                                      _ptr(out[0]), _ptr(out[1]), _ptr(ws), wsb, _stream(dev)))
+    return y, out
+
+
 def device_status():
     """Reads and clears the device status word (after a synchronize)."""
     code = L.load().atlas_scan_status()

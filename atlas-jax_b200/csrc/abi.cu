@@ -40,7 +40,17 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
-int check_params(const AtlasScanParams* p) {
+// Which tensor-path implementation serves a valid TENSOR / TENSOR_BATCHED problem.
+enum Impl { IMPL_EXACT, IMPL_FUSED, IMPL_BATCHED };
+Impl impl_of(const AtlasScanParams& p) {
+  if (p.precision == ATLAS_PREC_EXACT) return IMPL_EXACT;
+  const char* why = "";
+  if (p.precision == ATLAS_PREC_TENSOR && atlas::tc::supported(p, &why)) return IMPL_FUSED;
+  return IMPL_BATCHED;
+}
+
+// dir: 0 = forward (and the size queries), 1 = backward
+int check_params(const AtlasScanParams* p, int dir = 0) {
   if (!p) return fail(ATLAS_ERR_INVALID_ARGUMENT, "params is NULL");
   if (p->abi_version != ATLAS_ABI_VERSION)
     return fail(ATLAS_ERR_INVALID_ARGUMENT, "abi_version %d != library %d", p->abi_version, ATLAS_ABI_VERSION);
@@ -50,11 +60,21 @@ int check_params(const AtlasScanParams* p) {
   if (p->ns_steps < 0 || p->ns_steps > 5) return fail(ATLAS_ERR_INVALID_ARGUMENT, "ns_steps must be in 0..5");
   if (p->act_dtype != ATLAS_F32 && p->act_dtype != ATLAS_BF16)
     return fail(ATLAS_ERR_INVALID_ARGUMENT, "act_dtype must be ATLAS_F32 or ATLAS_BF16");
-  if (p->precision != ATLAS_PREC_EXACT && p->precision != ATLAS_PREC_TENSOR)
-    return fail(ATLAS_ERR_INVALID_ARGUMENT, "precision must be ATLAS_PREC_EXACT or ATLAS_PREC_TENSOR");
-  if (p->precision == ATLAS_PREC_TENSOR) {
+  if (p->precision != ATLAS_PREC_EXACT && p->precision != ATLAS_PREC_TENSOR &&
+      p->precision != ATLAS_PREC_TENSOR_BATCHED)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT,
+                "precision must be ATLAS_PREC_EXACT, ATLAS_PREC_TENSOR or ATLAS_PREC_TENSOR_BATCHED");
+  if (p->precision != ATLAS_PREC_EXACT) {
     const char* why = "";
-    if (!atlas::tc::supported(*p, &why)) return fail(ATLAS_ERR_UNSUPPORTED, "tensor path: %s", why);
+    const bool fused = p->precision == ATLAS_PREC_TENSOR && atlas::tc::supported(*p, &why);
+    if (dir == 1 && !fused)
+      return fail(ATLAS_ERR_UNSUPPORTED,
+                  "tensor path: the backward needs D=64, E=256, chunk<=64 and ATLAS_PREC_TENSOR (%s); "
+                  "ATLAS_PREC_EXACT covers other shapes",
+                  p->precision == ATLAS_PREC_TENSOR ? why : "batched forward has no backward");
+    const char* why2 = "";
+    if (!fused && !atlas::gen::supported(*p, atlas::KIND_DEEP, &why2))
+      return fail(ATLAS_ERR_UNSUPPORTED, "tensor path: %s", why2);
   }
   return ATLAS_OK;
 }
@@ -77,12 +97,20 @@ const char* atlas_last_error_string(void) { return g_err.c_str(); }
 
 size_t atlas_scan_saved_bytes(const AtlasScanParams* p) {
   if (check_params(p) != ATLAS_OK) return 0;
-  return p->precision == ATLAS_PREC_EXACT ? atlas::exact::saved_bytes(*p) : atlas::tc::saved_bytes(*p);
+  switch (impl_of(*p)) {
+    case IMPL_EXACT: return atlas::exact::saved_bytes(*p);
+    case IMPL_FUSED: return atlas::tc::saved_bytes(*p);
+    default: return 256;  // the batched forward keeps no carries (it has no backward)
+  }
 }
 
 size_t atlas_scan_workspace_bytes(const AtlasScanParams* p) {
   if (check_params(p) != ATLAS_OK) return 0;
-  return p->precision == ATLAS_PREC_EXACT ? atlas::exact::workspace_bytes(*p) : atlas::tc::workspace_bytes(*p);
+  switch (impl_of(*p)) {
+    case IMPL_EXACT: return atlas::exact::workspace_bytes(*p);
+    case IMPL_FUSED: return atlas::tc::workspace_bytes(*p);
+    default: return atlas::gen::workspace_bytes(*p, atlas::KIND_DEEP);
+  }
 }
 
 int atlas_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const void* v, const float* alpha,
@@ -111,7 +139,10 @@ int atlas_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const
   a.ws = workspace;
   a.status = atlas::device_status_ptr();
   cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t e = p->precision == ATLAS_PREC_EXACT ? atlas::exact::launch_fwd(a, s) : atlas::tc::launch_fwd(a, s);
+  const Impl im = impl_of(*p);
+  cudaError_t e = im == IMPL_EXACT   ? atlas::exact::launch_fwd(a, s)
+                  : im == IMPL_FUSED ? atlas::tc::launch_fwd(a, s)
+                                     : atlas::gen::launch_fwd(a, atlas::KIND_DEEP, s);
   return cuda_result(e, "atlas_scan_fwd launch");
 }
 
@@ -122,7 +153,7 @@ int atlas_scan_bwd(const AtlasScanParams* p, const void* q, const void* k, const
                    float* dW1_in, float* dW2_in, float* dS1_in, float* dS2_in, void* workspace,
                    size_t workspace_bytes, void* stream) {
   g_err.clear();
-  int rc = check_params(p);
+  int rc = check_params(p, 1);
   if (rc) return rc;
   if (!q || !k || !v || !alpha || !eta || !theta || !saved || !dy || !dq || !dk || !dv)
     return fail(ATLAS_ERR_INVALID_ARGUMENT, "q, k, v, gates, saved, dy, dq, dk, dv must be non-NULL");
@@ -143,6 +174,57 @@ int atlas_scan_bwd(const AtlasScanParams* p, const void* q, const void* k, const
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = p->precision == ATLAS_PREC_EXACT ? atlas::exact::launch_bwd(a, s) : atlas::tc::launch_bwd(a, s);
   return cuda_result(e, "atlas_scan_bwd launch");
+}
+
+}  // extern "C"
+
+namespace {
+int linear_check(const AtlasScanParams* p, size_t* need) {
+  *need = 0;
+  int rc = check_params(p);
+  if (rc) return rc;
+  if (p->precision == ATLAS_PREC_EXACT)
+    return fail(ATLAS_ERR_UNSUPPORTED, "linear memory runs on the tensor path only");
+  const char* why = "";
+  if (!atlas::gen::supported(*p, atlas::KIND_LINEAR, &why)) return fail(ATLAS_ERR_UNSUPPORTED, "linear memory: %s", why);
+  *need = atlas::gen::workspace_bytes(*p, atlas::KIND_LINEAR);
+  return ATLAS_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t atlas_linear_scan_workspace_bytes(const AtlasScanParams* p) {
+  size_t need = 0;
+  linear_check(p, &need);
+  return need;
+}
+
+int atlas_linear_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const void* v,
+                          const float* alpha, const float* eta, const float* theta, const float* gamma,
+                          const float* M_in, const float* S_in, void* y, float* M_out, float* S_out,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  size_t need = 0;
+  int rc = linear_check(p, &need);
+  if (rc) return rc;
+  if (!q || !k || !v || !alpha || !eta || !theta || !y)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "q, k, v, alpha, eta, theta and y must be non-NULL");
+  if ((M_in == nullptr) != (S_in == nullptr))
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "M_in and S_in must be both NULL or both non-NULL");
+  if (!workspace || workspace_bytes < need)
+    return fail(ATLAS_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  atlas::FwdArgs a{};
+  a.p = *p;
+  a.q = q; a.k = k; a.v = v;
+  a.alpha = alpha; a.eta = eta; a.theta = theta; a.gamma = gamma;
+  a.W1_in = M_in; a.S1_in = S_in;
+  a.y = y;
+  a.W1_out = M_out; a.S1_out = S_out;
+  a.ws = workspace;
+  a.status = atlas::device_status_ptr();
+  return cuda_result(atlas::gen::launch_fwd(a, atlas::KIND_LINEAR, (cudaStream_t)stream),
+                     "atlas_linear_scan_fwd launch");
 }
 
 size_t atlas_polar_express_workspace_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ns_steps,

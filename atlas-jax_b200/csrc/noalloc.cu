@@ -3,6 +3,7 @@
 // progress counters, one carry slot per chain and per-cluster factor rows) lives in a fixed array in
 // this file instead of a caller-provided workspace.
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "scan_internal.h"
@@ -51,6 +52,11 @@ extern "C" int atlas_scan_fwd_noalloc(const AtlasScanParams* p, const void* q, c
   // argument checks shared with the other entry points (sets the error string)
   const int rc0 = atlas::check_scan_params(p);
   if (rc0) return rc0;
+  const char* why = "";
+  if (!atlas::tc::supported(*p, &why)) {
+    std::string m = std::string("tensor path (no-alloc forward): ") + why;
+    return atlas::report_error(ATLAS_ERR_UNSUPPORTED, m.c_str());
+  }
   if (p->precision != ATLAS_PREC_TENSOR)
     return atlas::report_error(ATLAS_ERR_UNSUPPORTED, "atlas_scan_fwd_noalloc supports ATLAS_PREC_TENSOR only");
   if ((long)p->B * p->H > ATLAS_NOALLOC_MAX_CHAINS)

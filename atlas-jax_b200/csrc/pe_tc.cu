@@ -7,17 +7,17 @@
 // are transposed on the way in and out), so every step is
 //   A = X X^T,   B = b A + c A A,   X <- a X + B X
 // as three launches of one batched GEMM kernel.  The GEMM reads float32 operands,
-// splits them into bf16 hi/lo parts while staging them in shared memory, and
-// accumulates hi*hi + hi*lo + lo*hi on the tensor cores in float32 in TMEM (about 16
-// mantissa bits per operand; a single bf16 pass loses the near-null directions that
-// Polar Express amplifies).  The epilogue fuses alpha * product + beta * addend.
+// splits them into fp16 hi/lo parts (of 256 x the value) while staging them in shared
+// memory, and accumulates hi*hi + hi*lo + lo*hi on the tensor cores in float32 in TMEM
+// (about 22 significant bits per operand; a single 16-bit pass loses the near-null
+// directions that Polar Express amplifies).  The epilogue fuses alpha * product + beta * addend.
 //
 // GEMM kernel: one CTA of 4 warps per 128 x 128 output tile and batch entry; K in
 // chunks of 32, two shared-memory stages (the next chunk's coalesced global loads are
 // in flight while the current chunk's MMAs run); one elected thread issues the MMAs
 // and commits them to the stage's mbarrier; every wait is bounded and records
 // ATLAS_ERR_DEVICE_TIMEOUT instead of hanging.
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 
@@ -30,7 +30,7 @@ namespace pet {
 using namespace tcx;
 
 constexpr int TM = 128, TN = 128, TK = 32, NTH = 128;
-constexpr int TILE = 128 * TK * 2;  // bytes of one bf16 128 x 32 (or 32 x 128) tile
+constexpr int TILE = 128 * TK * 2;  // bytes of one 16-bit 128 x 32 (or 32 x 128) tile
 
 struct __align__(1024) Smem {
   uint8_t a[2][2][TILE];  // [stage][hi, lo]: 128 (m) x 32 (k), K-major
@@ -53,21 +53,28 @@ struct GemmArgs {
   int lda, ldb, ldd, ldc;
   int M, N, K;
   int b_kn, mode, st;
+  float sa, sb;  // operand split scales (powers of two)
   int* status;
 };
 
-// 4 consecutive values -> bf16 hi / lo, 8 bytes into each tile
-__device__ __forceinline__ void split4(uint8_t* th, uint8_t* tl, uint32_t off, const float* v) {
+// Operand split: 4 consecutive values v -> fp16 hi = fp16(sc v), lo = fp16(sc v - hi),
+// 8 bytes into each tile.  hi + lo keeps about 22 significant bits as long as the lo
+// parts stay above the fp16 subnormal floor, so each operand gets a power-of-two
+// scale sc that lifts its typical entry to about 1 (operand_scale): large matrices
+// have small entries (a normalised 768 x 4096 X has entries near 5e-4).  Every operand
+// is bounded (normalised X <= 1.2, A <= 1.44, B <= 64), and the scales are capped so
+// that sc * |v| stays below the fp16 maximum.  A product accumulates sa * sb times
+// its value; the epilogue divides it out.
+__device__ __forceinline__ void split4(uint8_t* th, uint8_t* tl, uint32_t off, const float* v, float sc) {
   uint32_t h[2], l[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
-    const uint32_t hb = *reinterpret_cast<uint32_t*>(&hv);
-    const float r0 = v[2 * k] - __uint_as_float(hb << 16);
-    const float r1 = v[2 * k + 1] - __uint_as_float(hb & 0xFFFF0000u);
-    __nv_bfloat162 lv = __floats2bfloat162_rn(r0, r1);
-    h[k] = hb;
-    l[k] = *reinterpret_cast<uint32_t*>(&lv);
+    const float y0 = v[2 * k] * sc, y1 = v[2 * k + 1] * sc;
+    const __half2 hv = __floats2half2_rn(y0, y1);
+    const float2 hf = __half22float2(hv);
+    const __half2 lv = __floats2half2_rn(y0 - hf.x, y1 - hf.y);
+    h[k] = *reinterpret_cast<const uint32_t*>(&hv);
+    l[k] = *reinterpret_cast<const uint32_t*>(&lv);
   }
   *(uint2*)(th + off) = make_uint2(h[0], h[1]);
   *(uint2*)(tl + off) = make_uint2(l[0], l[1]);
@@ -135,7 +142,7 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
       }
     }
   };
-  const uint32_t idesc = idesc_bf16(128, 128, false, g.b_kn != 0);
+  const uint32_t idesc = idesc_f16(128, 128, false, g.b_kn != 0);
   auto chunk = [&](int i, float* ra, float* rb) {
     const int st = i & 1;
     if (i >= 2 && !s.bad && !mbar_wait(&s.bar[st], ((i - 2) >> 1) & 1)) {  // MMAs of chunk i-2 read this stage
@@ -145,11 +152,11 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
     uint8_t *ah = s.a[st][0], *al = s.a[st][1], *bh = s.b[st][0], *bl = s.b[st][1];
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      split4(ah, al, cm_off(16 * p + (t >> 3), 4 * (t & 7), TK), ra + 4 * p);
+      split4(ah, al, cm_off(16 * p + (t >> 3), 4 * (t & 7), TK), ra + 4 * p, g.sa);
       if (!g.b_kn)
-        split4(bh, bl, cm_off(16 * p + (t >> 3), 4 * (t & 7), TK), rb + 4 * p);
+        split4(bh, bl, cm_off(16 * p + (t >> 3), 4 * (t & 7), TK), rb + 4 * p, g.sb);
       else
-        split4(bh, bl, cm_off(4 * p + (t >> 5), 4 * (t & 31), TN), rb + 4 * p);
+        split4(bh, bl, cm_off(4 * p + (t >> 5), 4 * (t & 31), TN), rb + 4 * p, g.sb);
     }
     fence_async_smem();
     fence_before();
@@ -187,9 +194,10 @@ __global__ void __launch_bounds__(NTH) gemm3_kernel(GemmArgs g) {
     set_status(g.status, ATLAS_ERR_DEVICE_TIMEOUT);
   }
   fence_after();
-  float alpha = 1.f, beta = 0.f;
+  const float unsc = 1.f / (g.sa * g.sb);
+  float alpha = unsc, beta = 0.f;
   if (g.mode == 1) {
-    alpha = (float)kPE[g.st][2];
+    alpha = (float)kPE[g.st][2] * unsc;
     beta = (float)kPE[g.st][1];
   } else if (g.mode == 2) {
     beta = (float)kPE[g.st][0];
@@ -300,6 +308,14 @@ cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, 
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int* status = device_status_ptr();
+  // typical |entry| of a unit-Frobenius n-element matrix is n^-1/2: scale it to ~2
+  auto operand_scale = [](double n, float cap) {
+    float sc = 256.f;
+    while (sc < cap && sc * sc < 4.0 * n) sc *= 2.f;
+    return sc;
+  };
+  const float sx = operand_scale((double)DE, 16384.f), sa = operand_scale((double)DD, 16384.f),
+              sbm = operand_scale((double)DD, 512.f);
   for (int st = 0; st < steps; ++st) {
     GemmArgs g{};
     g.status = status;
@@ -309,18 +325,21 @@ cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, 
     g.B = xa; g.sB = DE; g.ldb = E; g.b_kn = 0;
     g.C = A; g.sC = DD; g.ldc = D;
     g.Dm = nullptr; g.M = D; g.N = D; g.K = E; g.mode = 0;
+    g.sa = sx; g.sb = sx;
     if ((e = pet::gemm(g, batch, s)) != cudaSuccess) return e;
     // B = c A A + b A  (A symmetric: B(n, k) = A[n][k])
     g.A = A; g.sA = DD; g.lda = D;
     g.B = A; g.sB = DD; g.ldb = D; g.b_kn = 0;
     g.C = Bm; g.sC = DD; g.ldc = D;
     g.Dm = A; g.sD = DD; g.ldd = D; g.M = D; g.N = D; g.K = D; g.mode = 1;
+    g.sa = sa; g.sb = sa;
     if ((e = pet::gemm(g, batch, s)) != cudaSuccess) return e;
     // X' = B X + a X  (D x E, K = D; B(n, k) = X[k][n])
     g.A = Bm; g.sA = DD; g.lda = D;
     g.B = xa; g.sB = DE; g.ldb = E; g.b_kn = 1;
     g.C = xb; g.sC = DE; g.ldc = E;
     g.Dm = xa; g.sD = DE; g.ldd = E; g.M = D; g.N = E; g.K = D; g.mode = 2;
+    g.sa = sbm; g.sb = sx;
     if ((e = pet::gemm(g, batch, s)) != cudaSuccess) return e;
     std::swap(xa, xb);
   }

@@ -86,6 +86,15 @@ cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, 
                    cudaStream_t s);
 }  // namespace tcpe
 
+// Shape-generic tensor-path forward (scan_gen.cu): deep memory of any D in
+// {32, 64, 128, 256} / E / chunk, and linear memory (memory_layer.py:468-494).
+enum { KIND_DEEP = 0, KIND_LINEAR = 1 };
+namespace gen {
+bool supported(const AtlasScanParams& p, int kind, const char** why);
+size_t workspace_bytes(const AtlasScanParams& p, int kind);
+cudaError_t launch_fwd(const FwdArgs& a, int kind, cudaStream_t s);
+}  // namespace gen
+
 namespace tc {
 bool supported(const AtlasScanParams& p, const char** why);
 size_t saved_bytes(const AtlasScanParams& p);

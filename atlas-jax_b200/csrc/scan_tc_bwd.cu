@@ -30,7 +30,7 @@
 //   Sym = dA + dA^T = b Ps + c (Ps A + A Ps),  Ps = P + P^T
 //   dX~ = G~ B' + X~ Sym
 // The cotangent operands (G~, Ps, Sym) are fp16 splits of a power-of-two multiple
-// of their value, renormalised every step (vjp_tile_scale).
+// of their value, renormalised every step (vjp_scale).
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -65,7 +65,7 @@ struct __align__(1024) Smem {
   float gate[4][MAXCS];  // alpha, eta, theta, gamma of the chunk
   float nrm[MAXCS];      // ||S_t||_F (with the 1e-12) per token, from phase B
   float red[8];
-  float red2[8];
+  int vslot[3];           // vjp_scale's rotating reduction words
   uint64_t bar;
   uint64_t bar2;         // completion barrier of the second in-flight Polar Express
   uint64_t bar_ld;       // bulk loads of saved Newton-Schulz tiles
@@ -281,82 +281,37 @@ __device__ __forceinline__ void load_stk32(const uint8_t* t, int r, int c0, floa
   }
 }
 
-// Power of two f with f * sqrt(ss) in [0.5, 1) (1 when ss is zero or not finite).
-__device__ __forceinline__ float pow2_inv_norm(float ss) {
-  if (!(ss > 0.f) || !isfinite(ss)) return 1.f;
+// Scale of the cotangent tiles of the Polar Express VJP.  The cotangents of this scan
+// grow exponentially towards the start of a long sequence (the reference's float64 VJP
+// does the same), so their tiles are stored as fp16 splits of f * G with a power of
+// two f chosen per step so that max |f G| is in [1, 2).  Then ||f G||_F < 256 and every
+// later operand of the step stays inside the fp16 range (|Sym| <= 164 ||f G||_2 < 65504,
+// from the bounds on X, A and B'), while an entry far below the maximum only loses
+// absolute precision below 2^-25, i.e. relative to the tile's norm.
+//
+// vjp_scale: one named barrier.  Each warp reduces its maximum, lane 0 folds it into a
+// shared word with atomicMax (non-negative floats order like their bit patterns); the
+// words rotate over three slots so that clearing the slot of two reductions ago never
+// races with its readers or its next writers.
+__device__ __forceinline__ float vjp_scale(float m, int* slots, int& seq) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int* slot = slots + seq;
+  if ((threadIdx.x & 31) == 0) atomicMax(slot, __float_as_int(isfinite(m) ? m : 0.f));
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+  const float mx = __int_as_float(*(volatile int*)slot);
+  if (threadIdx.x == 0) slots[seq == 0 ? 2 : seq - 1] = 0;  // the slot of two reductions ago
+  seq = seq == 2 ? 0 : seq + 1;
+  if (!(mx > 0.f)) return 1.f;
   int e;
-  frexpf(sqrtf(ss), &e);
+  frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
   e = max(-120, min(120, e));
-  return ldexpf(1.f, -e);
+  return ldexpf(1.f, 1 - e);
 }
-
-// Target Frobenius norm (in [KVJP/2, KVJP)) of the cotangent tiles of the Polar
-// Express VJP.  The cotangents of this scan grow exponentially towards the start of
-// a long sequence (the reference's float64 VJP does the same), so their tiles are
-// stored as fp16 splits of f * G with a power-of-two f chosen per step.  With
-// ||f G||_F < 128 every later operand of the step stays inside the fp16 range
-// (|P| <= 1.2 * 128, |Sym| <= 164 * 128 < 65504 from the bounds on X, A and B'),
-// and typical entries (~1) keep their lo parts above the fp16 subnormal floor.
-#ifndef ATLAS_KVJP
-#define ATLAS_KVJP 128.f
-#endif
-constexpr float KVJP = ATLAS_KVJP;
-#ifndef ATLAS_VJP_TERMS
-#define ATLAS_VJP_TERMS 3
-#endif
-
-// Scale f (a power of two) with f * ||V||_F in [KVJP/2, KVJP), where V is spread over
-// the 256 epilogue threads, n values each.  Overflow-safe: every thread sums the
-// squares of its values divided by a power of two near its own maximum, and the
-// partial sums are merged as (s, e) pairs meaning s * 4^e.
-__device__ __forceinline__ void ns_merge(float& s, int& e, float s2, int e2) {
-  if (!(s2 > 0.f)) {
-    if (s2 != s2 || isinf(s2)) s = s2;
-    return;
-  }
-  if (!(s > 0.f)) {
-    if (s == 0.f) { s = s2; e = e2; }
-    return;
-  }
-  if (e2 > e) {
-    s = ldexpf(s, 2 * (e - e2)) + s2;
-    e = e2;
-  } else {
-    s += ldexpf(s2, 2 * (e2 - e));
-  }
-}
-template <int n>
-__device__ __forceinline__ void ns_local(const float* v, float& s, int& e) {
-  float m = 0.f;
+__device__ __forceinline__ float absmax32(const float* v, float m) {
 #pragma unroll
-  for (int j = 0; j < n; ++j) m = fmaxf(m, fabsf(v[j]));
-  if (!isfinite(m)) { s = m; e = 0; return; }
-  if (m == 0.f) { s = 0.f; e = 0; return; }
-  frexpf(m, &e);
-  const float sc = ldexpf(1.f, -e);
-  s = 0.f;
-#pragma unroll
-  for (int j = 0; j < n; ++j) s = fmaf(v[j] * sc, v[j] * sc, s);
-}
-__device__ __forceinline__ float vjp_tile_scale(float s, int e, float* red, float* red2) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const int e2 = __shfl_xor_sync(0xffffffffu, e, o);
-    ns_merge(s, e, s2, e2);
-  }
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-  if ((threadIdx.x & 31) == 0) {
-    red[threadIdx.x >> 5] = s;
-    red2[threadIdx.x >> 5] = __int_as_float(e);
-  }
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-  float S = 0.f;
-  int Ee = 0;
-#pragma unroll
-  for (int i = 0; i < NT / 32; ++i) ns_merge(S, Ee, red[i], __float_as_int(red2[i]));
-  if (!(S > 0.f) || !isfinite(S)) return 1.f;
-  return KVJP * ldexpf(pow2_inv_norm(S), -Ee);
+  for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(v[j]));
+  return m;
 }
 
 // Deferred step of the momentum recurrence S_u = theta_u S_{u-1} + ... for u = r + 1:
@@ -381,6 +336,17 @@ __device__ __forceinline__ void theta_step(float (*dS)[32], float (*xo)[32], int
     dS[1][jj] *= th;
   }
 }
+
+// The momentum-scan sums R and M slide by one token in and one out per token; every
+// BWD_RREF / BWD_MREF tokens they are rebuilt from their window instead, which keeps
+// the float32 drift of the running sums (the dominant error of the scalar gate
+// gradients) bounded.
+#ifndef BWD_RREF
+#define BWD_RREF 0
+#endif
+#ifndef BWD_MREF
+#define BWD_MREF 4
+#endif
 
 // TMEM column map of the Polar Express VJP (phase C uses all 512 columns)
 constexpr uint32_t VJ_P = 0;    // P = G~^T X~ stack (128 cols)
@@ -408,14 +374,14 @@ __device__ __forceinline__ bool vjp_mma(Smem& s, PEBars& B, uint32_t tm, int g, 
       // G~ B' does not depend on Sym: start it now so it overlaps the P epilogue
       // (later commits cover it; MMAs into one accumulator execute in order)
       for (int h2 = 0; h2 < 2; ++h2)
-        mma3<D, ATLAS_VJP_TERMS>(tm + VJ_X + 64 * h2, s.Gh, s.Gh + XLO, false, XC, s.Bh, s.Bl, true, 64, 128, 16 * 16 * XC * h2,
+        mma3<D>(tm + VJ_X + 64 * h2, s.Gh, s.Gh + XLO, false, XC, s.Bh, s.Bl, true, 64, 128, 16 * 16 * XC * h2,
                 false);
     } else if (g == 1) {  // Ps A + A Ps  (Ps, A symmetric: Ps^T A + A^T Ps)
       mma_stack<D>(tm + VJ_S, s.Ph, s.Ah, false);
       mma_stack<D>(tm + VJ_S, s.Ah, s.Ph, true);
     } else {
       for (int h2 = 0; h2 < 2; ++h2)
-        mma3<D, ATLAS_VJP_TERMS>(tm + VJ_X + 64 * h2, s.Xh, s.Xh + XLO, false, XC, s.Yh, s.Yl, true, 64, 128, 16 * 16 * XC * h2,
+        mma3<D>(tm + VJ_X + 64 * h2, s.Xh, s.Xh + XLO, false, XC, s.Yh, s.Yl, true, 64, 128, 16 * 16 * XC * h2,
                 true);
     }
     if (g != 0) mma_commit(B.done[0]);
@@ -466,6 +432,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     mbar_init(&s.ready[1], 8);
     fence_mbar_init();
     s.bad = 0;
+    s.vslot[0] = s.vslot[1] = s.vslot[2] = 0;
   }
   fence_before();
   __syncthreads();
@@ -487,6 +454,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   B.done[1] = &s.bar2;
   B.ready_phase[0] = B.ready_phase[1] = B.done_phase[0] = B.done_phase[1] = 0;
 
+  int vseq = 0;  // vjp_scale slot rotation (epilogue threads)
   const long total = (long)K.nchains * nch;
   const int npair = P.ns_steps > 0 ? 2 : 1;
   // Register split (launch: 384 threads x 168 = 64512): the two epilogue
@@ -786,7 +754,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       if (!P.pe_ste) {
         const float* St = Ssave + (size_t)(r + 1) * DE;
         const float nrm = s.nrm[r], kap = nrm * 1.01f + 1e-6f, inv = 1.0f / kap;
-        float vjp_scale = 1.f;  // TMEM dX~_0 -> true value
+        float dx_unscale = 1.f;  // TMEM dX~_0 -> true value
         if (P.ns_steps > 0) {
           PROF_T(tns)
           bool ok = true;
@@ -805,17 +773,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           }
           PROF_ADD(5, tns)
           PROF_T(tvjp)
-          // cotangent tiles hold vs * (true value) (||.||_F in [64, 128)); TMEM products of
+          // cotangent tiles hold vs * (true value) (max |.| in [1, 2)); TMEM products of
           // the step then hold KSPLIT * vs * (true value)
-          float vs;
-          {
-            float s0, s1;
-            int x0, x1;
-            ns_local<32>(dW[0], s0, x0);
-            ns_local<32>(dW[1], s1, x1);
-            ns_merge(s0, x0, s1, x1);
-            vs = vjp_tile_scale(s0, x0, s.red, s.red2);
-          }
+          float vs = vjp_scale(absmax32(dW[1], absmax32(dW[0], 0.f)), s.vslot, vseq);
           store_stk<32>(s.Gh, e0, dc, dW[0], vs);
           store_stk<32>(s.Gh, e1, dc, dW[1], vs);
           const int steps_ = P.ns_steps;
@@ -877,18 +837,15 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             if (st > 0 && tid == 0 && !s.bad)  // rest of step st-1's tiles: X~ is free now
               bulk_g2s_hint(s.Xh, nscur + (size_t)(st - 1) * NS_STEP_BYTES, 2 * XT_BYTES, &s.bar_ld, pol_ef);
             if (st > 0) {  // dX~ becomes the next step's G~ (after step 0 it stays in TMEM)
-              float gs = 0.f;
-              int ge = 0;
+              float gm = 0.f;
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
-                float gv[32], hs;
-                int he;
+                float gv[32];
                 tmem_ld32(tm + lane_off + VJ_X + 64 * h + dc, gv);
                 tmem_wait_ld();
-                ns_local<32>(gv, hs, he);
-                ns_merge(gs, ge, hs, he);
+                gm = absmax32(gv, gm);
               }
-              const float f = vjp_tile_scale(gs, ge, s.red, s.red2);  // rescale: ||G~|| in [64, 128)
+              const float f = vjp_scale(gm, s.vslot, vseq);  // rescale: max |G~| in [1, 2)
               vs *= KSPLIT * f;
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
@@ -898,7 +855,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
                 store_stk<32>(s.Gh, h ? e1 : e0, dc, gv, f);
               }
             } else {
-              vjp_scale = 1.f / (KSPLIT * vs);
+              dx_unscale = 1.f / (KSPLIT * vs);
             }
             PROF_ADD(15, tep2)
           }
@@ -926,7 +883,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
             tmem_ld32(tm + lane_off + VJ_X + 64 * h + dc, gv);
             tmem_wait_ld();
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) gv[jj] *= vjp_scale;
+            for (int jj = 0; jj < 32; ++jj) gv[jj] *= dx_unscale;
           } else {
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) gv[jj] = dW[h][jj];
@@ -1022,10 +979,23 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           ld_tile_half(pb, h, bv);
           tmem_wait_ld();
           float acc = 0.f;
+          if (BWD_RREF > 0 && r % (BWD_RREF > 0 ? BWD_RREF : 1) == 0) {  // R_r from its window (bounds the sliding-sum drift)
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            rv[jj] = fmaf(co, bv[jj], fmaf(ci, dS[h][jj], rv[jj]));  // R_r = R_{r+1} + c_r dS_r - c_{r+Om} dS_{r+Om}
-            acc = fmaf(rv[jj], gr[jj], acc);
+            for (int jj = 0; jj < 32; ++jj) rv[jj] = ci * dS[h][jj];
+            for (int u = r + 1; u < min(r + Om, cs); ++u) {
+              const float cu = -s.gate[1][u] * sc;
+              ld_tile_half(Wsave + (size_t)u * DE, h, bv);
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) rv[jj] = fmaf(cu, bv[jj], rv[jj]);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) acc = fmaf(rv[jj], gr[jj], acc);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              rv[jj] = fmaf(co, bv[jj], fmaf(ci, dS[h][jj], rv[jj]));  // R_r = R_{r+1} + c_r dS_r - c_{r+Om} dS_{r+Om}
+              acc = fmaf(rv[jj], gr[jj], acc);
+            }
           }
           rg[h] = acc;
           tmem_st32(cr + VJ_R, rv);
@@ -1034,9 +1004,19 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
           tmem_wait_ld();
           const float fr = -gi * (h ? f1 : f0), fo = io >= 0 ? go * Fm[io * E + (h ? e1 : e0)] : 0.f;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            dm = fmaf(dS[h][jj], mv[jj], dm);
-            mv[jj] = fmaf(fo, gq[jj], fmaf(fr, gr[jj], mv[jj]));  // M_{r-1}
+          for (int jj = 0; jj < 32; ++jj) dm = fmaf(dS[h][jj], mv[jj], dm);
+          if (BWD_MREF > 0 && r % (BWD_MREF > 0 ? BWD_MREF : 1) == 0) {  // M_{r-1} from its window
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) mv[jj] = 0.f;
+            for (int i = max(0, r - Om); i < r; ++i) {
+              const float f = (win ? s.gate[3][i] : 1.f) * Fm[i * E + (h ? e1 : e0)];
+              const float* gi_ = &s.Gc[i * D + dc];
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) mv[jj] = fmaf(f, gi_[jj], mv[jj]);
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) mv[jj] = fmaf(fo, gq[jj], fmaf(fr, gr[jj], mv[jj]));  // M_{r-1}
           }
           tmem_st32(cr + VJ_M, mv);
         }

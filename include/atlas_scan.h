@@ -74,8 +74,14 @@ enum {
   /* tcgen05 tensor cores, every Polar Express product on split fp16 operands
    * (hi + lo of a power-of-two multiple of the value, float32 accumulation),
    * float32 carries: as accurate as the reference's float32 arithmetic.  The
-   * production path. */
-  ATLAS_PREC_TENSOR = 1
+   * production path: the fused kernels for D=64, E=256, chunk <= 64 (forward and
+   * backward); other shapes run the batched forward below (forward only). */
+  ATLAS_PREC_TENSOR = 1,
+  /* Token-parallel batched forward on the tensor cores for any D in {32, 64, 128,
+   * 256}, E <= 2048, chunk <= 4096: the chunk's momenta first, then one batched
+   * Polar Express of all its matrices (atlas_polar_express_batched's GEMMs), then the
+   * memory recurrence and read-out.  Forward only (atlas_scan_bwd refuses it). */
+  ATLAS_PREC_TENSOR_BATCHED = 2
 };
 
 typedef struct AtlasScanParams {
@@ -150,6 +156,20 @@ int atlas_scan_fwd_noalloc(const AtlasScanParams* p,
                            void* y,
                            float* W1_out, float* W2_out, float* S1_out, float* S2_out, void* stream);
 
+/* Linear-memory variant of the scan (AtlasMemoryLayer with deep_memory=False,
+ * atlas_jax/memory_layer.py:468-494): memory M (D x D), momentum S, pred = M k,
+ * u = (2/D) (pred - v) k^T, Omega window, S_t = theta S_{t-1} - eta G_t,
+ * M_t = alpha M_{t-1} + PE(S_t) (square Polar Express), y_t = M_t q_t (no residual).
+ * params->E is ignored; params->precision must be ATLAS_PREC_TENSOR or
+ * ATLAS_PREC_TENSOR_BATCHED (it runs the batched forward).  M_in / S_in (B, H, D, D)
+ * float32 may both be NULL (zeros, the reference's linear initial state
+ * memory_layer.py:138-140).  Forward only. */
+size_t atlas_linear_scan_workspace_bytes(const AtlasScanParams* p);
+int atlas_linear_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const void* v,
+                          const float* alpha, const float* eta, const float* theta, const float* gamma,
+                          const float* M_in, const float* S_in, void* y, float* M_out, float* S_out,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* Batched Polar Express on float32 (batch, rows, cols) matrices, out-of-place.
  * Replaces fused_polar_express (atlas_jax/kernels/triton_pe.py:26-69, same math
  * as memory_layer.py:43-71) and the Muon orthogonalisation call site
@@ -157,7 +177,7 @@ int atlas_scan_fwd_noalloc(const AtlasScanParams* p,
  * pass eps_in_sqrt = 0 for that behaviour, 1e-12 for the memory layer's).
  * precision: ATLAS_PREC_EXACT runs float64 on CUDA cores, one CTA per matrix (small
  * matrices, parity checks); ATLAS_PREC_TENSOR runs each Newton-Schulz step as three
- * batched tcgen05 GEMMs with the three-term bf16 split (large matrices such as
+ * batched tcgen05 GEMMs on split fp16 operands (large matrices such as
  * Muon's stacked parameter gradients). */
 int atlas_polar_express_batched(const float* X, float* Y, int64_t batch, int32_t rows, int32_t cols,
                                 int32_t ns_steps, float eps_in_sqrt, int32_t precision,

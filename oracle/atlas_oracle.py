@@ -16,6 +16,7 @@ rkstgr/atlas-jax:
 * Omega window aggregation -- memory_layer.py:233-253 (cumsum minus shifted cumsum)
 * linear recurrence        -- memory_layer.py:256-299
 * deep chunk body          -- memory_layer.py:496-597 (D != E branch 577-590)
+* linear-memory chunk body -- memory_layer.py:468-494
 * scan driver / padding    -- memory_layer.py:649-718
 * LM-path initial state    -- atlas_jax/model.py:251-264
 
@@ -253,6 +254,43 @@ def chunk_forward(state, q, k, v, a, e, t, g, omega, ns_steps, keep=False):
                  chain=chain, G1=G1, G2=G2, S1_all=S1_all, S2_all=S2_all,
                  O1=O1, O2=O2, W1_all=W1_all, W2_all=W2_all, hq=hq, gq=gq)
     return y, new_state, inter
+
+
+def chunk_forward_linear(state, q, k, v, a, e, t, g, omega, ns_steps):
+    """Linear-memory chunk body, memory_layer.py:468-494: pred = M k, u = (2/D) err k^T,
+    Omega window, S scan, square Polar Express, M scan, y = M_t q (no residual)."""
+    M, S = state
+    dt = M.dtype
+    D = k.shape[-1]
+    pred = _ein('bhvk,bchk->bchv', M, k)
+    err = pred - v
+    u = dt.type(2.0 / D) * _ein('bchv,bchk->bchvk', err, k)
+    if omega > 1:
+        u = omega_aggregate(u, g[..., None, None], omega)
+    mom = -(e[..., None, None] * u)
+    S_all, S_n = linear_scan(S, t, mom)
+    O = polar_express(S_all, ns_steps)
+    M_all, M_n = linear_scan(M, a, O)
+    y = _ein('bchvk,bchk->bchv', M_all, q)
+    return y, (M_n, S_n)
+
+
+def scan_forward_linear(q, k, v, alpha, eta, theta, gamma, state=None, chunk=64, omega=16, ns_steps=5,
+                        dtype=np.float32):
+    """Whole-sequence linear-memory forward (driver memory_layer.py:649-718 with the
+    linear chunk body); state None = zeros (memory_layer.py:138-140, 644-646)."""
+    T, q, k, v, alpha, eta, theta, gamma = _prepare(q, k, v, alpha, eta, theta, gamma, chunk, dtype)
+    B, _, H, D = q.shape
+    if state is None:
+        state = (np.zeros((B, H, D, D), dtype), np.zeros((B, H, D, D), dtype))
+    st = tuple(np.asarray(x).astype(dtype) for x in state)
+    ys = []
+    for c in range(q.shape[1] // chunk):
+        sl = slice(c * chunk, (c + 1) * chunk)
+        y_c, st = chunk_forward_linear(st, q[:, sl], k[:, sl], v[:, sl], alpha[:, sl], eta[:, sl],
+                                       theta[:, sl], gamma[:, sl], omega, ns_steps)
+        ys.append(y_c)
+    return np.concatenate(ys, axis=1)[:, :T], st
 
 
 def _rev_linear_scan(gates, dh_all, dh_final, h_prev_all):

@@ -101,3 +101,28 @@ def test_xla_polar_express_opaque_layout():
     bufs = (ctypes.c_void_p * 3)()
     lib.atlas_xla_polar_express(None, bufs, b"x" * 8, 8, None)
     assert b"AtlasXlaPEOpaque" in lib.atlas_last_error_string()
+
+
+def test_batched_forward_sizes_and_backward_refusal():
+    """Shapes outside the fused kernels (here D=128, E=512, chunk 128) take the batched
+    tensor forward: it sizes a workspace, and the backward refuses them with
+    ATLAS_ERR_UNSUPPORTED before touching the GPU."""
+    lib = L.load()
+    p = _p(D=128, E=512, chunk=128, precision=L.ATLAS_PREC_TENSOR)
+    assert lib.atlas_scan_workspace_bytes(ctypes.byref(p)) > 0
+    assert lib.atlas_scan_saved_bytes(ctypes.byref(p)) > 0
+    rc = lib.atlas_scan_bwd(ctypes.byref(p), *([None] * 25), 0, None)
+    assert rc == L.ATLAS_ERR_UNSUPPORTED and b"backward" in lib.atlas_last_error_string()
+    bad = _p(D=48, precision=L.ATLAS_PREC_TENSOR_BATCHED)
+    assert lib.atlas_scan_workspace_bytes(ctypes.byref(bad)) == 0
+    assert b"head_dim" in lib.atlas_last_error_string()
+
+
+def test_linear_scan_checks():
+    lib = L.load()
+    p = _p(D=64, precision=L.ATLAS_PREC_TENSOR)
+    assert lib.atlas_linear_scan_workspace_bytes(ctypes.byref(p)) > 0
+    ex = _p(D=64, precision=L.ATLAS_PREC_EXACT)
+    assert lib.atlas_linear_scan_workspace_bytes(ctypes.byref(ex)) == 0
+    rc = lib.atlas_linear_scan_fwd(ctypes.byref(ex), *([None] * 12), None, 0, None)
+    assert rc == L.ATLAS_ERR_UNSUPPORTED and b"linear memory" in lib.atlas_last_error_string()

@@ -4,8 +4,8 @@ kernel): one Muon step on each of the 170M model's stacked matrix parameters
 (12 layers of 768x768 attention/memory projections, the 4096x768 GeGLU input and
 768x2048 output projections, and the 12x768 per-head gate projections) is compared
 with a float64 torch restatement of the reference's leaf update.  Tolerance 1e-3
-relative, the tensor-path Polar Express bound (bf16 three-term split; the Muon
-orthogonalisation is not on the scan's float32 parity path)."""
+relative (measured up to 5.4e-4 on the 4096 x 768 stack: the NorMuon rescaling and
+the cautious-decay mask amplify the Polar Express error of 6e-5)."""
 import math
 
 import pytest

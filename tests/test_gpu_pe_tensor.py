@@ -1,6 +1,6 @@
 """GPU parity of the tensor-path batched Polar Express (atlas_polar_express_batched
-with ATLAS_PREC_TENSOR: three batched tcgen05 GEMMs per Newton-Schulz step with the
-three-term bf16 split), the dispatch target of Muon's orthogonalisation
+with ATLAS_PREC_TENSOR: three batched tcgen05 GEMMs per Newton-Schulz step on split
+fp16 operands), the dispatch target of Muon's orthogonalisation
 (atlas_jax/optim.py:68-83) and of the memory layer's Polar Express
 (memory_layer.py:43-71).
 
@@ -8,9 +8,9 @@ Reference: a float64 torch restatement of the same iteration on the GPU (test
 infrastructure), and the float64 exact path on a small case.  Shapes follow the
 170M model's Muon stacks (768 x 768, 4096 x 768, 768 x 2048, the 12 x 768 gate
 projections) plus ragged sizes that exercise the masked tile edges.  Tolerance
-1e-3 relative (Frobenius; measured 3e-8 to 1.5e-4): the three-term split keeps
-about 16 mantissa bits per operand, and Polar Express amplifies rounding in the
-small singular directions.
+2e-4 relative (Frobenius; measured on B200 3e-8 to 6.4e-5, against 3e-6 to 5e-6
+for a float32 torch restatement): the split keeps about 22 significant bits per
+operand, and Polar Express amplifies rounding in the small singular directions.
 """
 import pytest
 import torch
@@ -18,11 +18,11 @@ import torch
 from oracle import atlas_oracle as O
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-3
+TOL = 2e-4
 
 
-def _ref(X, steps, eps):
-    X = X.double()
+def _ref(X, steps, eps, dtype=torch.float64):
+    X = X.to(dtype)
     tall = X.shape[-2] > X.shape[-1]
     if tall:
         X = X.transpose(-1, -2)
@@ -55,8 +55,11 @@ def test_tensor_pe_matches_float64(shape, steps, eps):
     Y = polar_express(X, steps, eps, precision=ATLAS_PREC_TENSOR)
     torch.cuda.synchronize()
     device_status()
-    err = _rel(Y, _ref(X, steps, eps))
-    print(shape, steps, f"{err:.2e}")
+    ref = _ref(X, steps, eps)
+    err = _rel(Y, ref)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    err32 = _rel(_ref(X, steps, eps, torch.float32), ref)
+    print(shape, steps, f"kernel {err:.2e}  float32 restatement {err32:.2e}")
     assert Y.shape == X.shape and bool(torch.isfinite(Y).all())
     assert err < TOL, err
 
