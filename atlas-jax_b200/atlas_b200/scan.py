@@ -45,17 +45,23 @@ def _check_act(x, name, dtype, shape):
 
 
 class Workspace:
-    """Grow-only scratch buffer reused across calls (the ABI itself never allocates)."""
+    """Grow-only scratch buffers reused across calls (the ABI itself never allocates).
+
+    One buffer per (device, current stream): calls issued on different streams or
+    devices never share scratch, and a buffer is only regrown by calls ordered on
+    the stream that used it."""
 
     def __init__(self):
-        self.buf = None
+        self.bufs = {}
 
     def get(self, nbytes, device):
         if nbytes == 0:
             return None, 0
-        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
-        return self.buf, self.buf.numel()
+        key = (device, torch.cuda.current_stream(device).cuda_stream)
+        buf = self.bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = self.bufs[key] = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        return buf, buf.numel()
 
 
 _WS = Workspace()
