@@ -2,12 +2,13 @@
 with its scan running on the B200 kernels.
 
 Same constructor fields (AtlasConfig, atlas_jax/config.py:6-33) and the same call
-signature, ``layer(x, memory_state=None) -> (y, DeepMemoryState)``.  The
-projections, short convolutions, normalisation, gates, retrieve gate and output
-projection (memory_layer.py:606-633, 720-725) stay ordinary torch ops around the
-scan, exactly where the reference keeps them in XLA; the scan itself
-(memory_layer.py:635-718) is one call to the C ABI through ``AtlasScan`` (forward
-and backward kernels), with no PyTorch fallback.
+signature, ``layer(x, memory_state=None) -> (y, DeepMemoryState)``.  Per call:
+one GEMM of x against every projection (q, k, v, the gates and the retrieve gate,
+concatenated), the fused prologue kernel (short convolutions, rms_norm, polynomial
+features, sigmoid gates; memory_layer.py:606-633), the scan (635-718) through
+``AtlasScan``, the fused retrieve gate (720-722) and the c_proj GEMM (724-725).
+Every non-GEMM step runs in libatlas_scan.so, forward and backward; there is no
+PyTorch fallback.
 """
 
 import math
@@ -16,9 +17,9 @@ from typing import NamedTuple, Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from .scan import ScanConfig, atlas_scan
+from .layer_io import LayerGeometry, prologue, retrieve_gate
 from . import _lib as L
 
 
@@ -49,25 +50,15 @@ class DeepMemoryState(NamedTuple):
     S_W2: torch.Tensor
 
 
-def rms_norm(x):
-    """memory_layer.py:211-216 (computed in float32)."""
-    xf = x.float()
-    return (xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + 1e-6)).to(x.dtype)
-
-
 class ShortConv(nn.Module):
-    """Causal depthwise 1-D convolution, memory_layer.py:303-329."""
+    """Parameters of a causal depthwise 1-D convolution (memory_layer.py:303-329); the
+    convolution itself runs inside the fused prologue kernel."""
 
     def __init__(self, dim, kernel_size=4):
         super().__init__()
         self.kernel_size = kernel_size
         self.weight = nn.Parameter(torch.randn(dim, 1, kernel_size) * 0.02)
         self.bias = nn.Parameter(torch.zeros(dim))
-
-    def forward(self, x):  # (B, T, C)
-        xt = F.pad(x.transpose(1, 2), (self.kernel_size - 1, 0))
-        y = F.conv1d(xt, self.weight.to(x.dtype), self.bias.to(x.dtype), groups=x.shape[-1])
-        return y.transpose(1, 2)
 
 
 class AtlasMemoryLayer(nn.Module):
@@ -106,40 +97,44 @@ class AtlasMemoryLayer(nn.Module):
                                    pe_ste=config.pe_ste, stop_grad_chunks=config.stop_grad_chunks,
                                    precision=precision)
 
-    def _poly(self, x):
-        out = self.poly_coeffs[0] * x
-        xp = x
-        for i in range(1, self.config.poly_degree):
-            xp = xp * x
-            out = out + self.poly_coeffs[i] * xp
-        return out
+    def geometry(self, B, T):
+        cfg = self.config
+        return LayerGeometry(B, T, self.n_head, self.head_dim, cfg.conv_kernel, cfg.poly_degree if
+                             self.poly_coeffs is not None else 0, self.gate_gamma is not None,
+                             self.retrieve_gate is not None, cfg.max_lr)
+
+    def _fused_weights(self):
+        """The projections as one GEMM operand and the prologue's parameter stacks."""
+        lin = [self.c_q, self.c_k, self.c_v, self.gate_alpha, self.gate_eta, self.gate_theta]
+        gates = [self.gate_alpha, self.gate_eta, self.gate_theta]
+        if self.gate_gamma is not None:
+            lin.append(self.gate_gamma)
+            gates.append(self.gate_gamma)
+        if self.retrieve_gate is not None:
+            lin.append(self.retrieve_gate)
+        W = torch.cat([m.weight for m in lin], 0)
+        conv_w = torch.stack([c.weight[:, 0, :] for c in (self.conv_q, self.conv_k, self.conv_v)]).float()
+        conv_b = torch.stack([c.bias for c in (self.conv_q, self.conv_k, self.conv_v)]).float()
+        gate_b = torch.stack([m.bias for m in gates]).float()
+        poly = self.poly_coeffs.float() if self.poly_coeffs is not None else None
+        return W, conv_w.contiguous(), conv_b.contiguous(), gate_b.contiguous(), poly
 
     def forward(self, x, memory_state=None):
         B, T, C = x.shape
         H, D, E = self.n_head, self.head_dim, self.expand_dim
-        q = self.conv_q(self.c_q(x)).reshape(B, T, H, D)      # memory_layer.py:606-609
-        k = self.conv_k(self.c_k(x)).reshape(B, T, H, D)
-        v = self.conv_v(self.c_v(x)).reshape(B, T, H, D)
-        if self.poly_coeffs is not None:                       # 611-618
-            q = self._poly(rms_norm(q))
-            k = rms_norm(self._poly(k))
-        else:
-            q, k = rms_norm(q), rms_norm(k)
-        alpha = torch.sigmoid(self.gate_alpha(x)).float()     # 620-633, gates already activated
-        eta = (torch.sigmoid(self.gate_eta(x)) * self.config.max_lr).float()
-        theta = torch.sigmoid(self.gate_theta(x)).float()
-        gamma = torch.sigmoid(self.gate_gamma(x)).float() if self.gate_gamma is not None else None
+        geo = self.geometry(B, T)
+        act = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        W, conv_w, conv_b, gate_b, poly = self._fused_weights()
+        # memory_layer.py:606-633: one GEMM for every projection, then the fused prologue
+        proj = (x.reshape(B * T, C).to(act) @ W.to(act).T).contiguous()
+        q, k, v, alpha, eta, theta, gamma, ret = prologue(geo, proj, conv_w, conv_b, poly, gate_b)
         if memory_state is None:                               # 635-643
             W1 = self.W1_init.float().unsqueeze(0).expand(B, H, D, E).contiguous()
             W2 = self.W2_init.float().unsqueeze(0).expand(B, H, E, D).contiguous()
             memory_state = DeepMemoryState(W1, W2, torch.zeros_like(W1), torch.zeros_like(W2))
-        act = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
-        y, st = atlas_scan(q.to(act).contiguous(), k.to(act).contiguous(), v.to(act).contiguous(),
-                           alpha.contiguous(), eta.contiguous(), theta.contiguous(),
-                           None if gamma is None else gamma.contiguous(),
+        y, st = atlas_scan(q, k, v, alpha, eta, theta, gamma,
                            tuple(s.float().contiguous() for s in memory_state), self.scan_cfg)
-        y = y.to(x.dtype)
-        if self.retrieve_gate is not None:                     # 720-722
-            y = y * torch.sigmoid(self.retrieve_gate(x)).unsqueeze(-1)
-        y = self.c_proj(y.reshape(B, T, H * D))                # 724-725
+        if ret is not None:                                    # 720-722
+            y = retrieve_gate(geo, y, ret)
+        y = self.c_proj(y.reshape(B, T, H * D).to(x.dtype))    # 724-725
         return y, DeepMemoryState(*st)

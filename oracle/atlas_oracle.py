@@ -518,3 +518,54 @@ def make_xavier_state(B, H, D, E, seed=1, dtype=np.float32):
     W1 = np.broadcast_to(W1, (B, H, D, E)).copy()
     W2 = np.broadcast_to(W2, (B, H, E, D)).copy()
     return (W1, W2, np.zeros((B, H, D, E), dtype), np.zeros((B, H, E, D), dtype))
+
+
+# ----------------------------------------------------------------------------
+# Layer prologue / epilogue around the scan (memory_layer.py:606-633, 720-722)
+# ----------------------------------------------------------------------------
+def rms_norm(x):
+    """memory_layer.py:211-216 (mean of squares over the last axis, eps 1e-6)."""
+    return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + 1e-6)
+
+
+def short_conv(x, w, b):
+    """Causal depthwise conv, memory_layer.py:303-329.  x (B,T,C), w (C,K), b (C)."""
+    K = w.shape[-1]
+    xp = np.concatenate([np.zeros((x.shape[0], K - 1, x.shape[2]), x.dtype), x], axis=1)
+    out = np.broadcast_to(b, x.shape).astype(x.dtype).copy()
+    for j in range(K):
+        out += w[:, j] * xp[:, j:j + x.shape[1]]
+    return out
+
+
+def poly_features(x, a):
+    """memory_layer.py:455-462: sum_i a_i x^(i+1)."""
+    out, xp = a[0] * x, x
+    for i in range(1, len(a)):
+        xp = xp * x
+        out = out + a[i] * xp
+    return out
+
+
+def layer_prologue(proj, B, T, H, D, conv_w, conv_b, poly, gate_bias, has_gamma, has_retrieve, max_lr):
+    """memory_layer.py:606-633 (and the retrieve gate's sigmoid, 720-721) applied to the
+    concatenated projection proj (B*T, 3*H*D + G*H), columns [q|k|v|alpha|eta|theta|gamma?|retrieve?].
+    Returns q, k, v (B,T,H,D) and the activated gates [alpha, eta, theta, gamma|None, retrieve|None]."""
+    di = H * D
+    P = proj.reshape(B, T, -1)
+    qkv = [short_conv(P[..., i * di:(i + 1) * di], conv_w[i], conv_b[i]).reshape(B, T, H, D) for i in range(3)]
+    q, k, v = qkv
+    if poly is not None and len(poly) > 0:
+        q = poly_features(rms_norm(q), poly)
+        k = rms_norm(poly_features(k, poly))
+    else:
+        q, k = rms_norm(q), rms_norm(k)
+    names = ["alpha", "eta", "theta"] + (["gamma"] if has_gamma else []) + (["retrieve"] if has_retrieve else [])
+    gates = {}
+    for i, n in enumerate(names):
+        z = P[..., 3 * di + i * H:3 * di + (i + 1) * H]
+        if n != "retrieve":
+            z = z + gate_bias[i]
+        s = _sigmoid(z)
+        gates[n] = s * max_lr if n == "eta" else s
+    return q, k, v, [gates.get(n) for n in ("alpha", "eta", "theta", "gamma", "retrieve")]

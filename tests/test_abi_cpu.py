@@ -126,3 +126,36 @@ def test_linear_scan_checks():
     assert lib.atlas_linear_scan_workspace_bytes(ctypes.byref(ex)) == 0
     rc = lib.atlas_linear_scan_fwd(ctypes.byref(ex), *([None] * 12), None, 0, None)
     assert rc == L.ATLAS_ERR_UNSUPPORTED and b"linear memory" in lib.atlas_last_error_string()
+
+
+def test_layer_io_exports_sizes_and_validation():
+    import os
+    from atlas_b200.layer_io import LayerGeometry, _lib
+    lib = _lib()
+    for n in L.header_functions(os.path.join(os.path.dirname(L.HEADER), "atlas_layer.h")):
+        assert hasattr(lib, n), n
+    geo = LayerGeometry(2, 50, 3, 64)
+    assert geo.n_proj == 3 * 3 * 64 + 5 * 3
+    p = geo.params(None)
+    assert lib.atlas_layer_prologue_workspace_bytes(ctypes.byref(p)) == 2 * 50 * 3 * 3 * 64 * 4
+    rc = lib.atlas_layer_prologue_fwd(ctypes.byref(p), *([None] * 14))
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT and b"NULL" in lib.atlas_last_error_string()
+    bad = LayerGeometry(2, 50, 3, 512).params(None)
+    assert lib.atlas_layer_prologue_workspace_bytes(ctypes.byref(bad)) == 0
+    assert b"head_dim" in lib.atlas_last_error_string()
+    bad = LayerGeometry(2, 50, 3, 64, conv_kernel=9).params(None)
+    assert lib.atlas_layer_retrieve_fwd(ctypes.byref(bad), None, None, None, None) == L.ATLAS_ERR_INVALID_ARGUMENT
+    # a valid check clears the message left by the failure above
+    assert lib.atlas_layer_prologue_workspace_bytes(ctypes.byref(p)) > 0
+    assert lib.atlas_last_error_string() == b""
+
+
+def test_layer_io_argument_counts_match_header():
+    """The ctypes prototypes have as many arguments as the C declarations."""
+    import os
+    import re
+    from atlas_b200.layer_io import _lib
+    lib = _lib()
+    txt = open(os.path.join(os.path.dirname(L.HEADER), "atlas_layer.h")).read()
+    for name, args in re.findall(r"(atlas_layer_\w+)\(([^;]*)\);", txt):
+        assert len(getattr(lib, name).argtypes) == args.count(",") + 1, name

@@ -183,3 +183,25 @@ def test_gamma_none_means_ones():
     y1, s1 = O.scan_forward(*ins[:6], None, st, 32, 4, 2)
     y2, s2 = O.scan_forward(*ins[:6], np.ones_like(ins[5]), st, 32, 4, 2)
     assert np.array_equal(y1, y2) and all(np.array_equal(a, b) for a, b in zip(s1, s2))
+
+
+def test_layer_prologue_oracle_matches_torch_restatement():
+    """oracle.layer_prologue (numpy) against tests/layer_ref.py (torch conv1d), float64."""
+    import torch
+    import layer_ref as LR
+    B, T, H, D, K = 2, 9, 2, 16, 4
+    rng = np.random.default_rng(0)
+    for P, hg, hr in ((2, True, True), (0, False, False), (3, True, False)):
+        G = 3 + hg + hr
+        proj = rng.standard_normal((B * T, 3 * H * D + G * H))
+        cw, cb, poly, gb = LR.make_params(H, D, K, P, G - hr)
+        a = O.layer_prologue(proj, B, T, H, D, cw.astype(np.float64), cb.astype(np.float64),
+                             None if poly is None else poly.astype(np.float64), gb.astype(np.float64), hg, hr, 0.1)
+        t = lambda x: None if x is None else torch.as_tensor(x, dtype=torch.float64)  # noqa: E731
+        b = LR.prologue(t(proj), B, T, H, D, t(cw), t(cb), t(poly), t(gb), hg, hr, 0.1)
+        for x, y in zip(a[:3], b[:3]):
+            np.testing.assert_allclose(x, y.numpy(), rtol=1e-12, atol=1e-12)
+        for x, y in zip(a[3], b[3]):
+            assert (x is None) == (y is None)
+            if x is not None:
+                np.testing.assert_allclose(x, y.numpy(), rtol=1e-12, atol=1e-14)
