@@ -74,6 +74,9 @@ def load():
     lib.atlas_linear_scan_fwd.restype = ctypes.c_int
     lib.atlas_linear_scan_fwd.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 2 + [_P] + [_F] * 2 + [_P, ctypes.c_size_t,
                                                                                                   _P]
+    lib.atlas_linear_scan_bwd.restype = ctypes.c_int
+    lib.atlas_linear_scan_bwd.argtypes = [pp] + [_P] * 3 + [_F] * 4 + [_F] * 2 + [_P] + [_F] * 2 + [_P] * 3 + \
+        [_F] * 4 + [_F] * 2 + [_P, ctypes.c_size_t, _P]
     lib.atlas_xla_opaque_bytes.restype = ctypes.c_size_t
     lib.atlas_xla_pe_opaque_bytes.restype = ctypes.c_size_t
     for n in ("atlas_xla_fwd", "atlas_xla_bwd", "atlas_xla_polar_express"):

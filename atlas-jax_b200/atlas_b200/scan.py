@@ -138,7 +138,8 @@ def scan_backward(q, k, v, alpha, eta, theta, gamma, saved, dy, dstate=None, cfg
 def linear_scan_forward(q, k, v, alpha, eta, theta, gamma=None, state=None, cfg=ScanConfig(), workspace=None):
     """Linear-memory scan (memory_layer.py:468-494), forward: q,k,v (B,T,H,D); gates
     (B,T,H) float32; state (M, S) each (B,H,D,D) float32 or None (zeros).
-    Returns (y, (M, S)).  Runs the batched tensor-path forward."""
+    Returns (y, (M, S)).  ATLAS_PREC_EXACT runs the float64 path (the one the backward
+    uses); other precisions run the batched tensor-path forward."""
     lib = L.load()
     B, T, H, D = q.shape
     dev = q.device
@@ -147,9 +148,7 @@ def linear_scan_forward(q, k, v, alpha, eta, theta, gamma=None, state=None, cfg=
     for n, x in (("alpha", alpha), ("eta", eta), ("theta", theta), ("gamma", gamma)):
         if x is not None:
             _check_act(x, n, torch.float32, (B, T, H))
-    prec = cfg.precision if cfg.precision != L.ATLAS_PREC_EXACT else L.ATLAS_PREC_TENSOR_BATCHED
-    p = _params(ScanConfig(cfg.chunk, cfg.omega, cfg.ns_steps, cfg.pe_ste, cfg.stop_grad_chunks, prec), B, T, H,
-                D, D, q.dtype)
+    p = _params(cfg, B, T, H, D, D, q.dtype)
     y = torch.empty_like(q)
     out = (torch.empty(B, H, D, D, device=dev), torch.empty(B, H, D, D, device=dev))
     need = lib.atlas_linear_scan_workspace_bytes(ctypes.byref(p))
@@ -161,6 +160,33 @@ def linear_scan_forward(q, k, v, alpha, eta, theta, gamma=None, state=None, cfg=
                                       _ptr(theta), _ptr(gamma), _ptr(st[0]), _ptr(st[1]), _ptr(y),
                                       _ptr(out[0]), _ptr(out[1]), _ptr(ws), wsb, _stream(dev)))
     return y, out
+
+
+def linear_scan_backward(q, k, v, alpha, eta, theta, gamma, state, dy, dstate=None, cfg=ScanConfig(),
+                         workspace=None):
+    """VJP of ``linear_scan_forward`` on the float64 path (cfg.precision must be
+    ATLAS_PREC_EXACT).  Returns (dq, dk, dv, dalpha, deta, dtheta, dgamma, (dM, dS))."""
+    lib = L.load()
+    B, T, H, D = q.shape
+    dev = q.device
+    p = _params(cfg, B, T, H, D, D, q.dtype)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    g = [torch.empty(B, T, H, device=dev) for _ in range(4)]
+    dst = (torch.empty(B, H, D, D, device=dev), torch.empty(B, H, D, D, device=dev))
+    st = [None, None] if state is None else [s.contiguous() for s in state]
+    dso = [None, None] if dstate is None else [None if s is None else s.contiguous() for s in dstate]
+    need = lib.atlas_linear_scan_workspace_bytes(ctypes.byref(p))
+    if need == 0:
+        raise L.AtlasError(L.ATLAS_ERR_UNSUPPORTED, lib.atlas_last_error_string().decode())
+    ws, wsb = (workspace or _WS).get(need, dev)
+    L.check(lib.atlas_linear_scan_bwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(eta),
+                                      _ptr(theta), _ptr(gamma), _ptr(st[0]), _ptr(st[1]), _ptr(dy.contiguous()),
+                                      _ptr(dso[0]), _ptr(dso[1]), _ptr(dq), _ptr(dk), _ptr(dv),
+                                      *[_ptr(x) for x in g], _ptr(dst[0]), _ptr(dst[1]), _ptr(ws), wsb,
+                                      _stream(dev)))
+    if gamma is None:
+        g[3] = None
+    return dq, dk, dv, g[0], g[1], g[2], g[3], dst
 
 
 def device_status():

@@ -183,8 +183,10 @@ int linear_check(const AtlasScanParams* p, size_t* need) {
   *need = 0;
   int rc = check_params(p);
   if (rc) return rc;
-  if (p->precision == ATLAS_PREC_EXACT)
-    return fail(ATLAS_ERR_UNSUPPORTED, "linear memory runs on the tensor path only");
+  if (p->precision == ATLAS_PREC_EXACT) {
+    *need = atlas::exact::lin_workspace_bytes(*p);
+    return ATLAS_OK;
+  }
   const char* why = "";
   if (!atlas::gen::supported(*p, atlas::KIND_LINEAR, &why)) return fail(ATLAS_ERR_UNSUPPORTED, "linear memory: %s", why);
   *need = atlas::gen::workspace_bytes(*p, atlas::KIND_LINEAR);
@@ -223,8 +225,50 @@ int atlas_linear_scan_fwd(const AtlasScanParams* p, const void* q, const void* k
   a.W1_out = M_out; a.S1_out = S_out;
   a.ws = workspace;
   a.status = atlas::device_status_ptr();
+  if (p->precision == ATLAS_PREC_EXACT) {
+    atlas::LinArgs la{};
+    la.p = *p;
+    la.q = q; la.k = k; la.v = v;
+    la.alpha = alpha; la.eta = eta; la.theta = theta; la.gamma = gamma;
+    la.M_in = M_in; la.S_in = S_in;
+    la.y = y; la.M_out = M_out; la.S_out = S_out;
+    la.ws = workspace;
+    la.bwd = 0;
+    return cuda_result(atlas::exact::lin_launch(la, (cudaStream_t)stream), "atlas_linear_scan_fwd launch (exact)");
+  }
   return cuda_result(atlas::gen::launch_fwd(a, atlas::KIND_LINEAR, (cudaStream_t)stream),
                      "atlas_linear_scan_fwd launch");
+}
+
+int atlas_linear_scan_bwd(const AtlasScanParams* p, const void* q, const void* k, const void* v,
+                          const float* alpha, const float* eta, const float* theta, const float* gamma,
+                          const float* M_in, const float* S_in, const void* dy, const float* dM_out,
+                          const float* dS_out, void* dq, void* dk, void* dv, float* dalpha, float* deta,
+                          float* dtheta, float* dgamma, float* dM_in, float* dS_in, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  g_err.clear();
+  if (p && p->precision != ATLAS_PREC_EXACT)
+    return fail(ATLAS_ERR_UNSUPPORTED, "the linear-memory backward runs on ATLAS_PREC_EXACT");
+  size_t need = 0;
+  int rc = linear_check(p, &need);
+  if (rc) return rc;
+  if (!q || !k || !v || !alpha || !eta || !theta || !dq || !dk || !dv || !dalpha || !deta || !dtheta)
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "inputs, dq, dk, dv and the gate gradients must be non-NULL");
+  if ((M_in == nullptr) != (S_in == nullptr))
+    return fail(ATLAS_ERR_INVALID_ARGUMENT, "M_in and S_in must be both NULL or both non-NULL");
+  if (!workspace || workspace_bytes < need)
+    return fail(ATLAS_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  atlas::LinArgs la{};
+  la.p = *p;
+  la.q = q; la.k = k; la.v = v; la.dy = dy;
+  la.alpha = alpha; la.eta = eta; la.theta = theta; la.gamma = gamma;
+  la.M_in = M_in; la.S_in = S_in; la.dM_out = dM_out; la.dS_out = dS_out;
+  la.dq = dq; la.dk = dk; la.dv = dv;
+  la.dalpha = dalpha; la.deta = deta; la.dtheta = dtheta; la.dgamma = dgamma;
+  la.dM_in = dM_in; la.dS_in = dS_in;
+  la.ws = workspace;
+  la.bwd = 1;
+  return cuda_result(atlas::exact::lin_launch(la, (cudaStream_t)stream), "atlas_linear_scan_bwd launch");
 }
 
 size_t atlas_polar_express_workspace_bytes(int64_t batch, int32_t rows, int32_t cols, int32_t ns_steps,

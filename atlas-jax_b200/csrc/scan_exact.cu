@@ -655,6 +655,275 @@ __global__ void __launch_bounds__(kThreads) pe_kernel(const float* X, float* Y, 
   }
 }
 
+// ---- linear memory (memory_layer.py:468-494), forward and backward ----------------
+// One CTA per chain, float64, the square memory M and momentum S (reference layout
+// M[v][k]) in the workspace.  Square Polar Express goes through the wide routine
+// (memory_layer.py:65-69: A = X X^T, X' = a X + B X).
+__host__ __device__ inline size_t lin_ws_doubles(int D, int cs, int nch, int steps) {
+  const size_t DD = (size_t)D * D;
+  return DD * (2 + 5 + 1 + 3 * (size_t)steps + 5 + 3 + 2 * (size_t)nch + 3 * (size_t)cs + 1) +
+         4 * (size_t)cs * D + 4 * (size_t)D + 4 * (size_t)cs + 32;
+}
+
+// err_r = M0 k_r - v_r (memory_layer.py:471-472) for the chunk's tokens (0 on padding)
+template <typename TA>
+__device__ void lin_frozen(const LinArgs& a, int b, int hh, int c, const double* M0, double* kd, double* err) {
+  const AtlasScanParams& P = a.p;
+  const int D = P.D, cs = P.chunk;
+  for (int i = threadIdx.x; i < cs * D; i += blockDim.x) {
+    const int t = c * cs + i / D, d = i % D;
+    kd[i] = t < P.T ? (double)ld_act((const TA*)a.k, (((size_t)b * P.T + t) * P.H + hh) * D + d) : 0.0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < cs * D; i += blockDim.x) {
+    const int r = i / D, vv = i % D, t = c * cs + r;
+    double sum = 0;
+    for (int k = 0; k < D; ++k) sum += M0[(size_t)vv * D + k] * kd[r * D + k];
+    err[i] = sum - (t < P.T ? (double)ld_act((const TA*)a.v, (((size_t)b * P.T + t) * P.H + hh) * D + vv) : 0.0);
+  }
+  __syncthreads();
+}
+
+// window weight of token i in G_r (1 without the Omega window), memory_layer.py:233-253
+__device__ __forceinline__ double lin_w(const LinArgs& a, int b, int hh, int tok) {
+  return a.p.omega > 1 ? (double)load_gates(a.alpha, a.eta, a.theta, a.gamma, a.p.T, a.p.H, b, hh, tok).g : 1.0;
+}
+
+// S <- theta S - eta G_r, G_r = sum_{i in window(r)} w_i (2/D) err_i k_i^T  (523-533)
+__device__ void lin_momentum(const LinArgs& a, int b, int hh, int c, int r, double* S, const double* err,
+                             const double* kd, double th, double et) {
+  const int D = a.p.D;
+  const double s = 2.0 / D;
+  const int i0 = a.p.omega > 1 ? max(0, r - a.p.omega + 1) : r;
+  for (int idx = threadIdx.x; idx < D * D; idx += blockDim.x) {
+    const int vv = idx / D, k = idx % D;
+    double g = 0;
+    for (int i = i0; i <= r; ++i) g += lin_w(a, b, hh, c * a.p.chunk + i) * err[i * D + vv] * kd[i * D + k];
+    S[idx] = th * S[idx] - et * s * g;
+  }
+  __syncthreads();
+}
+
+template <typename TA>
+__global__ void __launch_bounds__(kThreads) lin_kernel(LinArgs a) {
+  const AtlasScanParams& P = a.p;
+  const int D = P.D, cs = P.chunk, T = P.T, H = P.H, steps = P.ns_steps, nc = n_chunks(P);
+  const size_t DD = (size_t)D * D;
+  const int bh = blockIdx.x, b = bh / H, hh = bh % H;
+  const double s = 2.0 / D;
+  const bool win = P.omega > 1;
+  double* p = (double*)a.ws + (size_t)bh * lin_ws_doubles(D, cs, nc, steps);
+  double* M = p; p += DD;
+  double* S = p; p += DD;
+  PEWork pw;
+  pw.X = p; p += DD;
+  pw.Xn = p; p += DD;
+  pw.A = p; p += DD;
+  pw.AA = p; p += DD;
+  pw.Bm = p; p += DD;
+  double* O = p; p += DD;
+  double* hist = p; p += 3 * (size_t)steps * DD;
+  VJPWork vw;
+  vw.G = p; p += DD;
+  vw.dX = p; p += DD;
+  vw.dB = p; p += DD;
+  vw.dA = p; p += DD;
+  vw.T = p; p += DD;
+  double* dM = p; p += DD;
+  double* dS = p; p += DD;
+  double* dSt = p; p += DD;
+  double* carry = p; p += 2 * DD * nc;
+  double* Sall = p; p += (size_t)cs * DD;
+  double* Mall = p; p += (size_t)(cs + 1) * DD;
+  double* R = p; p += (size_t)cs * DD;
+  double* kd = p; p += (size_t)cs * D;
+  double* err = p; p += (size_t)cs * D;
+  double* tR = p; p += (size_t)cs * D;
+  double* dkd = p; p += (size_t)cs * D;
+  double* qd = p; p += D;
+  double* dyv = p; p += D;
+  p += 2 * D;
+  double* gsc = p; p += 4 * cs;  // dalpha, deta, dtheta, dgamma of the chunk
+  double* red = p;
+  const size_t off = (size_t)bh * DD;
+  for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+    M[i] = a.M_in ? (double)a.M_in[off + i] : 0.0;  // memory_layer.py:138-140: zeros
+    S[i] = a.S_in ? (double)a.S_in[off + i] : 0.0;
+  }
+  __syncthreads();
+  // ---- forward (the whole output in forward mode; the chunk carries in backward mode) ----
+  for (int c = 0; c < nc; ++c) {
+    if (a.bwd)
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+        carry[2 * DD * c + i] = M[i];
+        carry[2 * DD * c + DD + i] = S[i];
+      }
+    lin_frozen<TA>(a, b, hh, c, M, kd, err);
+    for (int r = 0; r < cs; ++r) {
+      const int t = c * cs + r;
+      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, t);
+      lin_momentum(a, b, hh, c, r, S, err, kd, g.t, g.e);
+      pe_forward(S, O, D, D, steps, 1e-12, pw, nullptr, red);
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) M[i] = g.a * M[i] + O[i];
+      __syncthreads();
+      if (!a.bwd && t < T) {  // y_t = M_t q_t (490-492)
+        for (int vv = threadIdx.x; vv < D; vv += blockDim.x) {
+          double sum = 0;
+          for (int k = 0; k < D; ++k)
+            sum += M[(size_t)vv * D + k] * (double)ld_act((const TA*)a.q, (((size_t)b * T + t) * H + hh) * D + k);
+          st_act((TA*)a.y, (((size_t)b * T + t) * H + hh) * D + vv, (float)sum);
+        }
+      }
+    }
+  }
+  if (!a.bwd) {
+    for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+      if (a.M_out) a.M_out[off + i] = (float)M[i];
+      if (a.S_out) a.S_out[off + i] = (float)S[i];
+    }
+    return;
+  }
+  // ---- backward, chunks in reverse ----
+  for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+    dM[i] = a.dM_out ? (double)a.dM_out[off + i] : 0.0;
+    dS[i] = a.dS_out ? (double)a.dS_out[off + i] : 0.0;
+  }
+  __syncthreads();
+  for (int c = nc - 1; c >= 0; --c) {
+    const double* M0 = carry + 2 * DD * c;
+    const double* S0 = M0 + DD;
+    for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+      Mall[i] = M0[i];
+      S[i] = S0[i];
+    }
+    for (size_t i = threadIdx.x; i < (size_t)cs * DD; i += blockDim.x) R[i] = 0.0;
+    __syncthreads();
+    lin_frozen<TA>(a, b, hh, c, M0, kd, err);
+    for (int r = 0; r < cs; ++r) {  // recompute S_t and M_t of the chunk
+      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + r);
+      lin_momentum(a, b, hh, c, r, S, err, kd, g.t, g.e);
+      double* Sr = Sall + r * DD;
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) Sr[i] = S[i];
+      pe_forward(S, O, D, D, steps, 1e-12, pw, nullptr, red);
+      const double* Mp = Mall + r * DD;
+      double* Mr = Mall + (r + 1) * DD;
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) Mr[i] = g.a * Mp[i] + O[i];
+      __syncthreads();
+    }
+    for (int r = cs - 1; r >= 0; --r) {
+      const int t = c * cs + r;
+      const Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, t);
+      for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const size_t o = (((size_t)b * T + t) * H + hh) * D + d;
+        qd[d] = t < T ? (double)ld_act((const TA*)a.q, o) : 0.0;
+        dyv[d] = t < T && a.dy ? (double)ld_act((const TA*)a.dy, o) : 0.0;
+      }
+      __syncthreads();
+      const double* Mr = Mall + (r + 1) * DD;
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) dM[i] += dyv[i / D] * qd[i % D];
+      if (t < T)  // dq = M_t^T dy
+        for (int k = threadIdx.x; k < D; k += blockDim.x) {
+          double sum = 0;
+          for (int vv = 0; vv < D; ++vv) sum += Mr[(size_t)vv * D + k] * dyv[vv];
+          st_act((TA*)a.dq, (((size_t)b * T + t) * H + hh) * D + k, (float)sum);
+        }
+      __syncthreads();
+      double acc = 0;
+      const double* Mp = Mall + r * DD;
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) acc += dM[i] * Mp[i];
+      const double dal = block_sum(acc, red);
+      // dS_t = theta_{t+1} dS_{t+1} + PE_vjp(S_t, dO_t = dM_t)
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) dSt[i] = dS[i];
+      __syncthreads();
+      const double* Sr = Sall + r * DD;
+      const double n = pe_forward(Sr, O, D, D, steps, 1e-12, pw, hist, red);
+      pe_vjp(Sr, dM, dSt, D, D, steps, n, hist, vw, red);
+      const double* Sp = r > 0 ? Sall + (r - 1) * DD : S0;
+      const int i0 = win ? max(0, r - P.omega + 1) : r;
+      double ath = 0, aet = 0;
+      for (size_t idx = threadIdx.x; idx < DD; idx += blockDim.x) {
+        const int vv = (int)(idx / D), k = (int)(idx % D);
+        ath += dSt[idx] * Sp[idx];
+        double gsum = 0;
+        for (int i = i0; i <= r; ++i) {
+          gsum += lin_w(a, b, hh, c * cs + i) * s * err[i * D + vv] * kd[i * D + k];
+          R[(size_t)i * DD + idx] -= g.e * dSt[idx];  // dG_r = -eta dS_t, to every token of the window
+        }
+        aet += dSt[idx] * gsum;
+      }
+      const double dth = block_sum(ath, red);
+      const double det = -block_sum(aet, red);
+      if (threadIdx.x == 0) {
+        gsc[r] = dal;
+        gsc[cs + r] = det;
+        gsc[2 * cs + r] = dth;
+      }
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+        dM[i] *= g.a;
+        dS[i] = g.t * dSt[i];
+      }
+      __syncthreads();
+    }
+    // u_i = (2/D) err_i k_i^T with du_i = w_i R_i: tR_i = (2/D) R_i k_i, derr_i = w_i tR_i
+    for (int i2 = threadIdx.x; i2 < cs * D; i2 += blockDim.x) {
+      const int i = i2 / D, vv = i2 % D;
+      double sum = 0;
+      for (int k = 0; k < D; ++k) sum += R[(size_t)i * DD + (size_t)vv * D + k] * kd[i * D + k];
+      tR[i2] = s * sum;
+    }
+    for (int i2 = threadIdx.x; i2 < cs * D; i2 += blockDim.x) {
+      const int i = i2 / D, k = i2 % D;
+      const double wi = lin_w(a, b, hh, c * cs + i);
+      double sum = 0;
+      for (int vv = 0; vv < D; ++vv) sum += R[(size_t)i * DD + (size_t)vv * D + k] * err[i * D + vv];
+      dkd[i2] = wi * s * sum;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < cs; i += blockDim.x) {  // dgamma_i = <u_i, R_i>
+      double sum = 0;
+      for (int vv = 0; vv < D; ++vv) sum += err[i * D + vv] * tR[i * D + vv];
+      gsc[3 * cs + i] = sum;
+    }
+    __syncthreads();
+    for (int i2 = threadIdx.x; i2 < cs * D; i2 += blockDim.x) tR[i2] *= lin_w(a, b, hh, c * cs + i2 / D);  // derr
+    __syncthreads();
+    for (int i2 = threadIdx.x; i2 < cs * D; i2 += blockDim.x) {  // err = M0 k - v
+      const int i = i2 / D, k = i2 % D, t = c * cs + i;
+      double sum = dkd[i2];
+      for (int vv = 0; vv < D; ++vv) sum += M0[(size_t)vv * D + k] * tR[i * D + vv];
+      if (t < T) {
+        const size_t o = (((size_t)b * T + t) * H + hh) * D + k;
+        st_act((TA*)a.dk, o, (float)sum);
+        st_act((TA*)a.dv, (((size_t)b * T + t) * H + hh) * D + k, (float)-tR[i2]);
+      }
+    }
+    for (size_t idx = threadIdx.x; idx < DD; idx += blockDim.x) {
+      const int vv = (int)(idx / D), k = (int)(idx % D);
+      double sum = 0;
+      for (int i = 0; i < cs; ++i) sum += tR[i * D + vv] * kd[i * D + k];
+      dM[idx] += sum;
+    }
+    for (int r = threadIdx.x; r < cs; r += blockDim.x) {
+      const int t = c * cs + r;
+      if (t >= T) continue;
+      const size_t gi = ((size_t)b * T + t) * H + hh;
+      a.dalpha[gi] = (float)gsc[r];
+      a.deta[gi] = (float)gsc[cs + r];
+      a.dtheta[gi] = (float)gsc[2 * cs + r];
+      if (a.dgamma) a.dgamma[gi] = win ? (float)gsc[3 * cs + r] : 0.f;
+    }
+    __syncthreads();
+    if (P.stop_grad_chunks) {  // memory_layer.py:665: the incoming carry is detached
+      for (size_t i = threadIdx.x; i < DD; i += blockDim.x) dM[i] = dS[i] = 0.0;
+      __syncthreads();
+    }
+  }
+  for (size_t i = threadIdx.x; i < DD; i += blockDim.x) {
+    if (a.dM_in) a.dM_in[off + i] = (float)dM[i];
+    if (a.dS_in) a.dS_in[off + i] = (float)dS[i];
+  }
+}
+
 // ---- host side ----------------------------------------------------------------
 size_t saved_bytes(const AtlasScanParams& p) {
   return (size_t)p.B * p.H * n_chunks(p) * 4 * (size_t)p.D * p.E * sizeof(double);
@@ -677,6 +946,17 @@ cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t s) {
     bwd_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(a);
   else
     bwd_kernel<float><<<grid, kThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+size_t lin_workspace_bytes(const AtlasScanParams& p) {
+  return (size_t)p.B * p.H * lin_ws_doubles(p.D, p.chunk, n_chunks(p), p.ns_steps) * sizeof(double);
+}
+cudaError_t lin_launch(const LinArgs& a, cudaStream_t s) {
+  dim3 grid(a.p.B * a.p.H);
+  if (a.p.act_dtype == ATLAS_BF16)
+    lin_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(a);
+  else
+    lin_kernel<float><<<grid, kThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 size_t pe_workspace_bytes(int64_t batch, int rows, int cols, int) {

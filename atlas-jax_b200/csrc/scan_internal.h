@@ -56,7 +56,24 @@ struct DeviceCache {
 
 __host__ __device__ inline int n_chunks(const AtlasScanParams& p) { return (p.T + p.chunk - 1) / p.chunk; }
 
+// Linear memory (memory_layer.py:468-494) on the float64 path: forward (bwd = 0) or
+// forward recompute + VJP (bwd = 1), one CTA per chain.
+struct LinArgs {
+  AtlasScanParams p;
+  const void *q, *k, *v, *dy;
+  const float *alpha, *eta, *theta, *gamma;
+  const float *M_in, *S_in, *dM_out, *dS_out;
+  void* y;
+  float *M_out, *S_out;
+  void *dq, *dk, *dv;
+  float *dalpha, *deta, *dtheta, *dgamma, *dM_in, *dS_in;
+  void* ws;
+  int bwd;
+};
+
 namespace exact {
+size_t lin_workspace_bytes(const AtlasScanParams& p);
+cudaError_t lin_launch(const LinArgs& a, cudaStream_t s);
 size_t saved_bytes(const AtlasScanParams& p);
 size_t workspace_bytes(const AtlasScanParams& p);
 cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t s);

@@ -160,15 +160,29 @@ int atlas_scan_fwd_noalloc(const AtlasScanParams* p,
  * atlas_jax/memory_layer.py:468-494): memory M (D x D), momentum S, pred = M k,
  * u = (2/D) (pred - v) k^T, Omega window, S_t = theta S_{t-1} - eta G_t,
  * M_t = alpha M_{t-1} + PE(S_t) (square Polar Express), y_t = M_t q_t (no residual).
- * params->E is ignored; params->precision must be ATLAS_PREC_TENSOR or
- * ATLAS_PREC_TENSOR_BATCHED (it runs the batched forward).  M_in / S_in (B, H, D, D)
+ * params->E is ignored.  ATLAS_PREC_TENSOR / ATLAS_PREC_TENSOR_BATCHED run the
+ * batched tensor-core forward; ATLAS_PREC_EXACT runs float64 on CUDA cores, one CTA
+ * per chain (and is the precision of the backward below).  M_in / S_in (B, H, D, D)
  * float32 may both be NULL (zeros, the reference's linear initial state
- * memory_layer.py:138-140).  Forward only. */
+ * memory_layer.py:138-140).  The workspace size depends on params->precision. */
 size_t atlas_linear_scan_workspace_bytes(const AtlasScanParams* p);
 int atlas_linear_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const void* v,
                           const float* alpha, const float* eta, const float* theta, const float* gamma,
                           const float* M_in, const float* S_in, void* y, float* M_out, float* S_out,
                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* VJP of atlas_linear_scan_fwd (JAX autodiff of memory_layer.py:468-494 under the
+ * scan driver 649-718): recomputes the forward from (M_in, S_in) and returns dq, dk,
+ * dv (act_dtype), the gate gradients (B, T, H) float32 (dgamma may be NULL) and the
+ * initial-state cotangents dM_in, dS_in (may be NULL).  dy, dM_out, dS_out NULL mean
+ * zero cotangents.  params->precision must be ATLAS_PREC_EXACT; the workspace is
+ * atlas_linear_scan_workspace_bytes() of the same params. */
+int atlas_linear_scan_bwd(const AtlasScanParams* p, const void* q, const void* k, const void* v,
+                          const float* alpha, const float* eta, const float* theta, const float* gamma,
+                          const float* M_in, const float* S_in, const void* dy, const float* dM_out,
+                          const float* dS_out, void* dq, void* dk, void* dv, float* dalpha, float* deta,
+                          float* dtheta, float* dgamma, float* dM_in, float* dS_in, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* Batched Polar Express on float32 (batch, rows, cols) matrices, out-of-place.
  * Replaces fused_polar_express (atlas_jax/kernels/triton_pe.py:26-69, same math

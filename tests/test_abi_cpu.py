@@ -123,9 +123,13 @@ def test_linear_scan_checks():
     p = _p(D=64, precision=L.ATLAS_PREC_TENSOR)
     assert lib.atlas_linear_scan_workspace_bytes(ctypes.byref(p)) > 0
     ex = _p(D=64, precision=L.ATLAS_PREC_EXACT)
-    assert lib.atlas_linear_scan_workspace_bytes(ctypes.byref(ex)) == 0
+    assert lib.atlas_linear_scan_workspace_bytes(ctypes.byref(ex)) > 0
     rc = lib.atlas_linear_scan_fwd(ctypes.byref(ex), *([None] * 12), None, 0, None)
-    assert rc == L.ATLAS_ERR_UNSUPPORTED and b"linear memory" in lib.atlas_last_error_string()
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT
+    rc = lib.atlas_linear_scan_bwd(ctypes.byref(p), *([None] * 21), None, 0, None)
+    assert rc == L.ATLAS_ERR_UNSUPPORTED and b"EXACT" in lib.atlas_last_error_string()
+    rc = lib.atlas_linear_scan_bwd(ctypes.byref(ex), *([None] * 21), None, 0, None)
+    assert rc == L.ATLAS_ERR_INVALID_ARGUMENT
 
 
 def test_layer_io_exports_sizes_and_validation():

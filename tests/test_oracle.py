@@ -205,3 +205,19 @@ def test_layer_prologue_oracle_matches_torch_restatement():
             assert (x is None) == (y is None)
             if x is not None:
                 np.testing.assert_allclose(x, y.numpy(), rtol=1e-12, atol=1e-14)
+
+
+def test_linear_torch_restatement_matches_oracle_forward():
+    """tests/torch_ref.scan_linear (the autograd checker of the linear backward) equals
+    the oracle's linear forward in float64."""
+    import torch
+    import torch_ref as TR
+    B, T, H, D = 1, 40, 2, 8
+    ins = O.make_inputs(B, T, H, D, seed=4, gamma_mode="random")
+    rng = np.random.default_rng(1)
+    st = (0.1 * rng.standard_normal((B, H, D, D)), 0.01 * rng.standard_normal((B, H, D, D)))
+    y_o, fin = O.scan_forward_linear(*ins, st, 16, 4, 5, dtype=np.float64)
+    t = [torch.as_tensor(np.asarray(x, np.float64)) for x in ins]
+    y_t, fin_t = TR.scan_linear(*t, tuple(torch.as_tensor(x) for x in st), 16, 4, 5)
+    np.testing.assert_allclose(y_t.numpy(), y_o, rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(fin_t[0].numpy(), fin[0], rtol=1e-10, atol=1e-12)

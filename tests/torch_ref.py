@@ -106,3 +106,39 @@ def scan(q, k, v, a, e, t, g, state, cs, w, ns, ste=False, stop_grad=False):
         y, st = chunk(st, q[:, sl], k[:, sl], v[:, sl], a[:, sl], e[:, sl], t[:, sl], g[:, sl], w, ns, ste)
         ys.append(y)
     return torch.cat(ys, 1)[:, :T], st
+
+
+def chunk_linear(state, q, k, v, a, e, t, g, w, ns, ste):
+    """Linear-memory chunk body, memory_layer.py:468-494."""
+    M, S = state
+    D = k.shape[-1]
+    err = torch.einsum('bhvk,bchk->bchv', M, k) - v
+    u = (2.0 / D) * torch.einsum('bchv,bchk->bchvk', err, k)
+    if w > 1:
+        u = omega(u, g[..., None, None], w)
+    Sa, S = lscan(S, t, -(e[..., None, None] * u))
+    Ma, M = lscan(M, a, pe(Sa, ns, ste))
+    return torch.einsum('bchvk,bchk->bchv', Ma, q), (M, S)
+
+
+def scan_linear(q, k, v, a, e, t, g, state, cs, w, ns, ste=False, stop_grad=False):
+    """Driver 649-718 over the linear chunk body (state (M, S))."""
+    T = q.shape[1]
+    pad = (-T) % cs
+
+    def p(x, val):
+        if pad == 0:
+            return x
+        shape = list(x.shape)
+        shape[1] = pad
+        return torch.cat([x, torch.full(shape, val, dtype=x.dtype, device=x.device)], 1)
+    q, k, v = p(q, 0.0), p(k, 0.0), p(v, 0.0)
+    a, e, t, g = p(a, 1.0), p(e, 0.0), p(t, 0.0), p(g, 0.0)
+    ys, st = [], state
+    for c in range(q.shape[1] // cs):
+        sl = slice(c * cs, (c + 1) * cs)
+        if stop_grad:
+            st = tuple(x.detach() for x in st)
+        y, st = chunk_linear(st, q[:, sl], k[:, sl], v[:, sl], a[:, sl], e[:, sl], t[:, sl], g[:, sl], w, ns, ste)
+        ys.append(y)
+    return torch.cat(ys, 1)[:, :T], st
