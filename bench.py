@@ -192,6 +192,61 @@ def f32_mode(lib, L, dev, stream, sp, p_bf16, nws, ws, g, world, layers=2, reps=
                    f"{c['layers']} layers (no all-reduce)"}
 
 
+def next_rows(dev, stream, peak_tf, hbm):
+    """Device-timed figures for the rows beyond the headline scan (rank 0, one GPU):
+    the MAG sliding-window attention at config 3's shape (B=2, T=32768, 12 heads x 64,
+    window 1024) forward+backward, and the fused layer prologue forward+backward at
+    the 170M layer shape (B=8, T=8192, C=768).  3 untimed + 5 timed passes each;
+    every input is larger than L2."""
+    import torch
+    from atlas_b200.swa import swa_backward, swa_forward
+    from atlas_b200.layer_io import LayerGeometry, prologue_backward, prologue_forward
+    out = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+
+    def timed(f, n=5):
+        for _ in range(3):
+            f()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for _ in range(n):
+            f()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / n
+    B, T, H, D, W = 2, 32768, 12, 64, 1024
+    q, k, v, do = (torch.randn(B, T, H, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(4))
+    o, lse = swa_forward(q, k, v, W)
+    f_ms = timed(lambda: swa_forward(q, k, v, W))
+    b_ms = timed(lambda: swa_backward(q, k, v, o, lse, do, W))
+    pairs = B * H * sum(min(t, W) + 1 for t in range(T))  # (query, key) pairs inside the band
+    ff, fb = 4 * D * pairs, 10 * D * pairs  # QK^T + PV; QK^T, dO V^T, P^T dO, dS^T Q, dS K
+    out["mag_swa"] = {"workload": f"banded RoPE attention B={B} T={T} H={H} D={D} window={W}",
+                      "fwd_ms": f_ms, "bwd_ms": b_ms, "fwd_tflops": ff / f_ms / 1e9, "bwd_tflops": fb / b_ms / 1e9,
+                      "frac_fwd_bwd": (ff + fb) / ((f_ms + b_ms) / 1e3) / 1e12 / peak_tf,
+                      "unit": "TFLOP/s of the band (algorithmic)", "kernels": "swa fwd_kernel, dkv_kernel, dq_kernel"}
+    del q, k, v, do, o, lse
+    B, T, H, D = 8, 8192, 12, 64
+    geo = LayerGeometry(B, T, H, D)
+    proj = torch.randn(B * T, geo.n_proj, device=dev, generator=g).to(torch.bfloat16)
+    cw = torch.randn(3, H * D, 4, device=dev, generator=g) * 0.3
+    cb = torch.zeros(3, H * D, device=dev)
+    poly = torch.ones(2, device=dev)
+    gb = torch.zeros(4, H, device=dev)
+    qo, ko, vo, gates = prologue_forward(geo, proj, cw, cb, poly, gb)
+    pf = timed(lambda: prologue_forward(geo, proj, cw, cb, poly, gb))
+    pb = timed(lambda: prologue_backward(geo, proj, cw, cb, poly, gb, qo, ko, vo, gates))
+    nb = proj.numel() * 2
+    fbytes = nb + 3 * qo.numel() * 2 + 5 * B * T * H * 4        # proj in; q, k, v, 5 gates out
+    bbytes = 2 * nb + 3 * qo.numel() * 2 + 5 * B * T * H * 4 + 2 * 3 * qo.numel() * 4  # + dproj out, dc round trip
+    out["layer_prologue"] = {"workload": f"prologue B={B} T={T} H={H} D={D} (bf16)", "fwd_ms": pf, "bwd_ms": pb,
+                             "fwd_gbs": fbytes / pf / 1e6, "bwd_gbs": bbytes / pb / 1e6,
+                             "frac_hbm_fwd": fbytes / pf / 1e6 / hbm, "unit": "GB/s (algorithmic bytes)"}
+    return out
+
+
 def gpu_arm(args, rank, world):
     import torch
     from atlas_b200 import _lib as L
@@ -352,6 +407,8 @@ def gpu_arm(args, rank, world):
         "clocks": ck,
         "f32_activations": f32,
     }
+    if rank == 0 and world == 1 and not args.no_next:
+        out["next_rows"] = next_rows(dev, stream, peak_tf, hbm)
     if rank == 0 and world == 1 and not args.no_cpu:
         v, dt, cores = cpu_baseline()
         out["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
@@ -371,11 +428,13 @@ def main():
     ap.add_argument("--seq", type=int, default=CFG["T"], help="profiling only: shorter sequences")
     ap.add_argument("--no-e2e", action="store_true", help="profiling only: skip the end-to-end leg")
     ap.add_argument("--no-f32", action="store_true", help="skip the float32-activation leg")
+    ap.add_argument("--no-next", action="store_true", help="skip the attention / prologue leg")
     args = ap.parse_args()
     if args.layers != CFG["layers"] or args.seq != CFG["T"]:
         CFG["layers"], CFG["T"] = args.layers, args.seq
         args.no_cpu = True
         args.no_f32 = True
+        args.no_next = True
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
