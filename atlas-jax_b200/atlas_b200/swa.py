@@ -27,7 +27,7 @@ def _lib():
     if not _bound:
         pp = ctypes.POINTER(AtlasSwaParams)
         lib.atlas_swa_fwd.restype = ctypes.c_int
-        lib.atlas_swa_fwd.argtypes = [pp, _P, _P, _P, _P, _P, _P]
+        lib.atlas_swa_fwd.argtypes = [pp, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]
         lib.atlas_swa_workspace_bytes.restype = ctypes.c_size_t
         lib.atlas_swa_workspace_bytes.argtypes = [pp]
         lib.atlas_swa_bwd.restype = ctypes.c_int
@@ -51,7 +51,9 @@ def swa_forward(q, k, v, window, rope=True):
     p = _params(q, window, rope)
     o = torch.empty_like(q)
     lse = torch.empty(B, H, T, device=q.device)
-    L.check(lib.atlas_swa_fwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), _stream(q.device)))
+    ws = torch.empty(lib.atlas_swa_workspace_bytes(ctypes.byref(p)), dtype=torch.uint8, device=q.device)
+    L.check(lib.atlas_swa_fwd(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), _ptr(ws), ws.numel(),
+                              _stream(q.device)))
     return o, lse
 
 

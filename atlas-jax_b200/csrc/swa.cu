@@ -2,21 +2,23 @@
 // cores: the attention core of atlas_jax/model.py:77-135 for the MAG hybrid.
 //
 // Tiles are 128 queries x 128 keys x D = 64, bf16 operands in shared memory in the
-// core-matrix layout of tc_ops.cuh, float32 accumulators in TMEM.  One CTA of four
-// warps owns one 128-row block; thread i owns TMEM lane i, i.e. one query row (the
-// forward and dQ kernels) or one key row (the dK/dV kernel), so every row
-// statistic of the softmax stays in that thread's registers: no shuffles, no
-// shared-memory reductions.  Only the band's key blocks are visited:
-// ceil((window + 128) / 128) + 1 of them per row block instead of T / 128.
+// core-matrix layout of tc_ops.cuh, float32 accumulators in TMEM.  One CTA of eight
+// warps owns one 128-row block.  Warp w reads TMEM lane quadrant w % 4 (rows
+// 32 (w % 4) ..) and column half w / 4, so each row is shared by two threads, and the
+// softmax statistics of a row need one exchange through shared memory per key block.
+// Only the band's key blocks are visited: ceil((window + 128) / 128) + 1 of them per
+// row block instead of T / 128.
 //
+//   rope     a pre-pass rotates q and k once (model.py:49-75, 117-121) into the
+//            workspace; the tiles are then plain 16-byte copies (cp.async), the next
+//            block's tiles in flight while the current block computes.
 //   forward  per key block: S = Q K^T (TMEM), online softmax in registers,
 //            P (bf16) -> smem, O_blk = P V (TMEM), O = O * corr + O_blk.
 //   backward delta = rowsum(dO * O); dK/dV kernel per key block over its query
 //            blocks: S^T = K Q^T and dP^T = V dO^T, P^T = exp(S^T - lse),
 //            dS^T = P^T (dP^T - delta), dV += P^T dO, dK += dS^T Q (TMEM);
-//            dQ kernel per query block over its key blocks: dQ += dS K.
-//   RoPE (model.py:49-75) is applied to q and k as the tiles are loaded, and its
-//   transpose to dq and dk as they are stored.
+//            dQ kernel per query block over its key blocks: dQ += dS K.  dq and dk
+//            leave through the transpose of the rotation.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -33,14 +35,16 @@ namespace swa {
 using namespace tcx;
 constexpr int HD = 64;   // head dim
 constexpr int BR = 128;  // rows per block (queries or keys)
-constexpr int TILE = BR * HD * 2;       // one 128 x 64 bf16 tile
-constexpr int PTILE = BR * BR * 2;      // one 128 x 128 bf16 tile
+constexpr int NTH = 256;
+constexpr int TILE = BR * HD * 2;   // one 128 x 64 bf16 tile
+constexpr int PTILE = BR * BR * 2;  // one 128 x 128 bf16 tile
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Args {
   AtlasSwaParams p;
   const __nv_bfloat16 *q, *k, *v, *o, *dout;
   __nv_bfloat16 *out, *dq, *dk, *dv;
+  __nv_bfloat16 *qr, *kr;  // rotated q, k (workspace)
   float* lse;
   float* delta;
   int* status;
@@ -50,71 +54,89 @@ __device__ __forceinline__ uint8_t* align128(uint8_t* p) {
   return (uint8_t*)(((uintptr_t)p + 127) & ~(uintptr_t)127);
 }
 
-__device__ __forceinline__ void tmem_ld32x(uint32_t taddr, float* v) {
-  tmem_ld16(taddr, v);
-  tmem_ld16(taddr + 16, v + 16);
-}
+// RoPE inverse frequency i, model.py:54-55: 1 / 10000^(2i / D)
+__device__ __forceinline__ float inv_freq(int i) { return 1.0f / powf(10000.0f, (float)(2 * i) / (float)HD); }
 
-// RoPE inverse frequencies, model.py:54-55: 1 / 10000^(2i / D)
-__device__ __forceinline__ void init_invf(float* invf) {
-  if (threadIdx.x < HD / 2) invf[threadIdx.x] = 1.0f / powf(10000.0f, (float)(2 * threadIdx.x) / (float)HD);
-}
-
-// Loads rows [r0, r0 + 128) of head (b, h) of a (B, T, H, 64) bf16 tensor into a
-// 128 x 64 core-matrix tile (K-major for rows-as-M/N operands, MN-major when the rows
-// are the K index), zero rows outside [0, T).  With rope, rows are rotated by their
-// position (model.py:66-75: halves x1 = x[:32], x2 = x[32:]).  Each thread moves
-// 16-byte groups c8 and c8 + 4 of a row, the two halves a rotation pairs.
-__device__ void load_tile(uint8_t* tile, const __nv_bfloat16* x, int b, int h, int r0, int T, int H, bool rope,
-                          const float* invf) {
-  for (int u = threadIdx.x; u < BR * 4; u += blockDim.x) {
-    const int r = u >> 2, c8 = u & 3, t = r0 + r;
-    uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-    if (t >= 0 && t < T) {
-      const __nv_bfloat16* row = x + (((size_t)b * T + t) * H + h) * HD;
-      lo = *(const uint4*)(row + 8 * c8);
-      hi = *(const uint4*)(row + 32 + 8 * c8);
-      if (rope) {
-        __nv_bfloat16* x1 = (__nv_bfloat16*)&lo;
-        __nv_bfloat16* x2 = (__nv_bfloat16*)&hi;
+// q, k -> rotated qr, kr (model.py:66-75: x1 = x[:32], x2 = x[32:]; out = [x1 c - x2 s,
+// x2 c + x1 s]); without rope a plain copy.  One thread per (row, group of 8 pairs, q|k).
+__global__ void rope_kernel(Args a) {
+  const AtlasSwaParams& P = a.p;
+  const long units = (long)P.B * P.T * P.H * 4 * 2;
+  for (long u = (long)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (long)gridDim.x * blockDim.x) {
+    const int which = (int)(u & 1), c8 = (int)((u >> 1) & 3);
+    const long rowi = u >> 3;
+    const int t = (int)((rowi / P.H) % P.T);
+    const __nv_bfloat16* src = (which ? a.k : a.q) + (size_t)rowi * HD;
+    __nv_bfloat16* dst = (which ? a.kr : a.qr) + (size_t)rowi * HD;
+    uint4 lo = *(const uint4*)(src + 8 * c8), hi = *(const uint4*)(src + 32 + 8 * c8);
+    if (P.rope) {
+      __nv_bfloat16* x1 = (__nv_bfloat16*)&lo;
+      __nv_bfloat16* x2 = (__nv_bfloat16*)&hi;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float sn, cs;
-          sincosf((float)t * invf[8 * c8 + j], &sn, &cs);
-          const float a = __bfloat162float(x1[j]), bb = __bfloat162float(x2[j]);
-          x1[j] = __float2bfloat16_rn(a * cs - bb * sn);
-          x2[j] = __float2bfloat16_rn(bb * cs + a * sn);
-        }
+      for (int j = 0; j < 8; ++j) {
+        float sn, cs;
+        sincosf((float)t * inv_freq(8 * c8 + j), &sn, &cs);
+        const float x = __bfloat162float(x1[j]), y = __bfloat162float(x2[j]);
+        x1[j] = __float2bfloat16_rn(x * cs - y * sn);
+        x2[j] = __float2bfloat16_rn(y * cs + x * sn);
       }
     }
-    *(uint4*)(tile + cm_off(r, 8 * c8, HD)) = lo;
-    *(uint4*)(tile + cm_off(r, 32 + 8 * c8, HD)) = hi;
+    *(uint4*)(dst + 8 * c8) = lo;
+    *(uint4*)(dst + 32 + 8 * c8) = hi;
   }
 }
 
-// Writes one float row (64 values, this thread's) to (B, T, H, 64) bf16 at position
-// t, optionally through the transpose of RoPE (the cotangent of a rotated input).
-__device__ void store_row(__nv_bfloat16* x, int b, int h, int t, int T, int H, float* v, bool rope_t,
-                          const float* invf) {
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Issues the copies of rows [r0, r0 + 128) of head (b, h) of a (B, T, H, 64) bf16
+// tensor into a 128 x 64 core-matrix tile (K-major when the rows are the M/N index,
+// MN-major when they are the K index); rows outside [0, T) are zero-filled.
+__device__ void load_tile_async(uint8_t* tile, const __nv_bfloat16* x, int b, int h, int r0, int T, int H) {
+  for (int u = threadIdx.x; u < BR * 8; u += blockDim.x) {
+    const int r = u >> 3, c8 = u & 7, t = r0 + r;
+    uint8_t* d = tile + cm_off(r, 8 * c8, HD);
+    if (t >= 0 && t < T)
+      cp_async16(d, x + (((size_t)b * T + t) * H + h) * HD + 8 * c8);
+    else
+      *(uint4*)d = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Column split of a 64-wide row between the two warps of a lane quadrant: half ch
+// owns columns [16 ch, 16 ch + 16) and [32 + 16 ch, 32 + 16 ch + 16), so both halves of
+// every RoPE pair (i, i + 32) stay with one thread.
+__device__ __forceinline__ int col_of(int ch, int j) { return (j < 16 ? 0 : 16) + 16 * ch + j; }
+
+// Writes this thread's 32 values of row t (columns col_of(ch, 0..31)) of a
+// (B, T, H, 64) bf16 tensor, optionally through the transpose of RoPE (the cotangent
+// of a rotated input: [g1; g2] -> [g1 c + g2 s; g2 c - g1 s]).
+__device__ void store_half_row(__nv_bfloat16* x, int b, int h, int t, int T, int H, int ch, float* v, bool rope_t) {
   if (t >= T) return;
   if (rope_t) {
 #pragma unroll
-    for (int i = 0; i < HD / 2; ++i) {  // [x1; x2] -> [x1 c + x2 s; x2 c - x1 s]
+    for (int j = 0; j < 16; ++j) {
       float sn, cs;
-      sincosf((float)t * invf[i], &sn, &cs);
-      const float a = v[i], bb = v[i + 32];
-      v[i] = a * cs + bb * sn;
-      v[i + 32] = bb * cs - a * sn;
+      sincosf((float)t * inv_freq(16 * ch + j), &sn, &cs);
+      const float g1 = v[j], g2 = v[16 + j];
+      v[j] = g1 * cs + g2 * sn;
+      v[16 + j] = g2 * cs - g1 * sn;
     }
   }
   __nv_bfloat16* row = x + (((size_t)b * T + t) * H + h) * HD;
 #pragma unroll
-  for (int c = 0; c < HD; c += 8) {
+  for (int g = 0; g < 4; ++g) {
     uint4 pk;
     __nv_bfloat162* p2 = (__nv_bfloat162*)&pk;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) p2[j] = __floats2bfloat162_rn(v[c + 2 * j], v[c + 2 * j + 1]);
-    *(uint4*)(row + c) = pk;
+    for (int j = 0; j < 4; ++j) p2[j] = __floats2bfloat162_rn(v[8 * g + 2 * j], v[8 * g + 2 * j + 1]);
+    *(uint4*)(row + col_of(ch, 8 * g)) = pk;
   }
 }
 
@@ -130,8 +152,14 @@ __device__ __forceinline__ void store16(uint8_t* tile, int r, int c0, const floa
   }
 }
 
-// D (+)= A B^T-style products over K: A (128 x K) K-major tile with tileC = ka;
-// B either K-major (rows = N, tileC = kb) or MN-major (rows = K, tileC = N).
+// this thread's 32 columns col_of(ch, .) of a 64-column TMEM accumulator row
+__device__ __forceinline__ void tmem_ld_half(uint32_t taddr, int ch, float* v) {
+  tmem_ld16(taddr + 16 * ch, v);
+  tmem_ld16(taddr + 32 + 16 * ch, v + 16);
+}
+
+// D (+)= A * B over K: A (128 x K) K-major tile with a_cols columns; B either K-major
+// (rows = N, b_cols = K) or MN-major (rows = K, b_cols = N).
 __device__ __forceinline__ void mma_tiles(uint32_t tmd, const uint8_t* A, int a_cols, const uint8_t* Bt, int b_cols,
                                           bool b_mn, int N, int K, bool accumulate) {
   const uint32_t id = idesc_bf16(128, N, false, b_mn);
@@ -163,27 +191,24 @@ __device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase, volatil
   return !*bad;
 }
 
-// ---------------------------------------------------------------------------
-// forward
-// ---------------------------------------------------------------------------
-struct FwdSmem {
-  uint8_t Q[TILE], K[TILE], V[TILE], P[PTILE];
-  float invf[HD / 2];
-  uint64_t bar;
-  uint32_t tmem;
-  volatile int bad;
+// cp.async copies of this thread landed -> visible to every thread and to the tensor core
+__device__ __forceinline__ void tiles_ready() {
+  cp_async_wait<0>();
+  fence_async_smem();
+  cta_sync();
+}
+
+struct Roles {
+  uint32_t tm, lane;
+  int w, qd, ch, rloc;
 };
 
-__global__ void __launch_bounds__(128) fwd_kernel(Args a) {
-  extern __shared__ uint8_t raw[];
-  FwdSmem& s = *(FwdSmem*)align128(raw);
-  const AtlasSwaParams& P = a.p;
-  const int T = P.T, H = P.H, W = P.window, tid = threadIdx.x, w = tid >> 5;
-  const int b = blockIdx.y / H, h = blockIdx.y % H, q0 = blockIdx.x * BR, row = q0 + tid;
-  const bool rope = P.rope != 0;
-  init_invf(s.invf);
+// TMEM allocation (warp 0), barrier init, and this thread's roles
+template <class S>
+__device__ __forceinline__ Roles setup(S& s, uint32_t cols) {
+  const int tid = threadIdx.x, w = tid >> 5;
   if (w == 0) {
-    tmem_alloc(&s.tmem, 256);
+    tmem_alloc(&s.tmem, cols);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -192,82 +217,133 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     s.bad = 0;
   }
   cta_sync();
-  const uint32_t tm = s.tmem, lane = (uint32_t)(32 * w) << 16;
-  load_tile(s.Q, a.q, b, h, q0, T, H, rope, s.invf);
+  Roles u;
+  u.w = w;
+  u.qd = w & 3;
+  u.ch = w >> 2;
+  u.rloc = 32 * u.qd + (tid & 31);
+  u.tm = s.tmem;
+  u.lane = (uint32_t)(32 * u.qd) << 16;
+  return u;
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+struct FwdSmem {
+  uint8_t Q[TILE], K[2][TILE], V[TILE], P[PTILE];
+  float mx[2][BR], ls[2][BR];
+  uint64_t bar;
+  uint32_t tmem;
+  volatile int bad;
+};
+
+__global__ void __launch_bounds__(NTH) fwd_kernel(Args a) {
+  extern __shared__ uint8_t raw[];
+  FwdSmem& s = *(FwdSmem*)align128(raw);
+  const AtlasSwaParams& P = a.p;
+  const int T = P.T, H = P.H, W = P.window;
+  const int b = blockIdx.y / H, h = blockIdx.y % H, q0 = blockIdx.x * BR;
+  const Roles u = setup(s, 256);
+  const int row = q0 + u.rloc, ch = u.ch;
   const int kb0 = max(0, q0 - W) / BR, kb1 = min(T - 1, q0 + BR - 1) / BR;
+  load_tile_async(s.Q, a.qr, b, h, q0, T, H);
+  load_tile_async(s.K[0], a.kr, b, h, kb0 * BR, T, H);
+  cp_async_commit();
+  load_tile_async(s.V, a.v, b, h, kb0 * BR, T, H);
+  cp_async_commit();
   const float sl2 = rsqrtf((float)HD) * LOG2E;  // scores in log2 units
-  float m = -INFINITY, lsum = 0.f, o[HD];
+  float m = -INFINITY, lsum = 0.f, o[32];
 #pragma unroll
-  for (int i = 0; i < HD; ++i) o[i] = 0.f;
+  for (int i = 0; i < 32; ++i) o[i] = 0.f;
   uint32_t phase = 0;
-  for (int kb = kb0; kb <= kb1 && !s.bad; ++kb) {
-    const int k0 = kb * BR;
-    load_tile(s.K, a.k, b, h, k0, T, H, rope, s.invf);
-    load_tile(s.V, a.v, b, h, k0, T, H, false, s.invf);
+  bool done = true;
+  for (int kb = kb0; kb <= kb1; ++kb) {
+    const int k0 = kb * BR, cur = (kb - kb0) & 1;
+    cp_async_wait<1>();  // Q and K[cur]; V may still be in flight
     fence_async_smem();
     cta_sync();
-    if (w == 0) {
-      mma_tiles(tm, s.Q, HD, s.K, HD, false, BR, HD, false);  // S = Q K^T
+    if (u.w == 0) {
+      mma_tiles(u.tm, s.Q, HD, s.K[cur], HD, false, BR, HD, false);  // S = Q K^T
       mma_commit(&s.bar);
     }
+    if (kb < kb1) load_tile_async(s.K[cur ^ 1], a.kr, b, h, k0 + BR, T, H);
+    cp_async_commit();  // (possibly empty group: keeps the group count uniform)
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) break;
-    // online softmax of this thread's row over the block's keys (model.py:126-131)
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
+    // online softmax over this block's keys (model.py:126-131); this thread holds
+    // keys [64 ch, 64 ch + 64) of its row
     float mx = -INFINITY;
-    for (int c = 0; c < BR; c += 16) {
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
       float v[16];
-      tmem_ld16(tm + lane + c, v);
+      tmem_ld16(u.tm + u.lane + 64 * ch + c, v);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int key = k0 + c + j;
+        const int key = k0 + 64 * ch + c + j;
         if (key <= row && row - key <= W && key < T) mx = fmaxf(mx, v[j] * sl2);
       }
     }
-    const float mn = fmaxf(m, mx);
+    s.mx[ch][u.rloc] = mx;
+    cta_sync();
+    const float mn = fmaxf(m, fmaxf(s.mx[0][u.rloc], s.mx[1][u.rloc]));
     const float corr = mn == -INFINITY ? 1.f : exp2f(m - mn);
     float psum = 0.f;
-    for (int c = 0; c < BR; c += 16) {
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
       float v[16];
-      tmem_ld16(tm + lane + c, v);
+      tmem_ld16(u.tm + u.lane + 64 * ch + c, v);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int key = k0 + c + j;
+        const int key = k0 + 64 * ch + c + j;
         const bool ok = key <= row && row - key <= W && key < T;
         v[j] = ok ? exp2f(v[j] * sl2 - mn) : 0.f;
         psum += v[j];
       }
-      store16(s.P, tid, c, v);
+      store16(s.P, u.rloc, 64 * ch + c, v);
     }
     lsum = lsum * corr + psum;
     m = mn;
+    cp_async_wait<1>();  // V of this block (the newest group is the next K)
     fence_async_smem();
     cta_sync();
-    if (w == 0) {
-      mma_tiles(tm + 128, s.P, BR, s.V, HD, true, HD, BR, false);  // O_blk = P V
+    if (u.w == 0) {
+      mma_tiles(u.tm + 128, s.P, BR, s.V, HD, true, HD, BR, false);  // O_blk = P V
       mma_commit(&s.bar);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) break;
-    for (int c = 0; c < HD; c += 32) {
-      float v[32];
-      tmem_ld32x(tm + lane + 128 + c, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[c + j] = fmaf(o[c + j], corr, v[j]);
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+      done = false;
+      break;
     }
-    cta_sync();  // the next block's loads overwrite K, V and P
-  }
-  if (!s.bad && row < T) {
-    const float inv = 1.f / lsum;
+    if (kb < kb1) load_tile_async(s.V, a.v, b, h, k0 + BR, T, H);
+    cp_async_commit();
+    float v[32];
+    tmem_ld_half(u.tm + u.lane + 128, ch, v);
+    tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] *= inv;
-    store_row(a.out, b, h, row, T, H, o, false, s.invf);
-    a.lse[((size_t)b * H + h) * T + row] = (m + log2f(lsum)) * (1.f / LOG2E);
+    for (int j = 0; j < 32; ++j) o[j] = fmaf(o[j], corr, v[j]);
+  }
+  cp_async_wait<0>();
+  if (done) {
+    s.ls[ch][u.rloc] = lsum;
+    cta_sync();
+    const float tot = s.ls[0][u.rloc] + s.ls[1][u.rloc];
+    if (row < T) {
+      const float inv = 1.f / tot;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[j] *= inv;
+      store_half_row(a.out, b, h, row, T, H, ch, o, false);
+      if (ch == 0) a.lse[((size_t)b * H + h) * T + row] = (m + log2f(tot)) * (1.f / LOG2E);
+    }
   }
   cta_sync();
-  if (w == 0) tmem_dealloc(tm, 256);
+  if (u.w == 0) tmem_dealloc(u.tm, 256);
 }
 
 // ---------------------------------------------------------------------------
@@ -298,185 +374,190 @@ __global__ void delta_kernel(Args a) {
 }
 
 struct KVSmem {
-  uint8_t K[TILE], V[TILE], Q[TILE], dO[TILE], Pt[PTILE], dSt[PTILE];
-  float lse2[BR], delta[BR], invf[HD / 2];
+  uint8_t K[TILE], V[TILE], Q[2][TILE], dO[2][TILE], Pt[PTILE], dSt[PTILE];
+  float lse2[2][BR], delta[2][BR];
   uint64_t bar;
   uint32_t tmem;
   volatile int bad;
 };
 
-// dK, dV for one block of 128 keys over the query blocks that see it
-__global__ void __launch_bounds__(128) dkv_kernel(Args a) {
+// dK, dV of one block of 128 keys over the query blocks that see it
+__global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
   extern __shared__ uint8_t raw[];
   KVSmem& s = *(KVSmem*)align128(raw);
   const AtlasSwaParams& P = a.p;
-  const int T = P.T, H = P.H, W = P.window, tid = threadIdx.x, w = tid >> 5;
-  const int b = blockIdx.y / H, h = blockIdx.y % H, k0 = blockIdx.x * BR, kr = k0 + tid;
-  const bool rope = P.rope != 0;
-  init_invf(s.invf);
-  if (w == 0) {
-    tmem_alloc(&s.tmem, 512);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&s.bar, 1);
-    fence_mbar_init();
-    s.bad = 0;
-  }
-  cta_sync();
-  const uint32_t tm = s.tmem, lane = (uint32_t)(32 * w) << 16;
-  load_tile(s.K, a.k, b, h, k0, T, H, rope, s.invf);
-  load_tile(s.V, a.v, b, h, k0, T, H, false, s.invf);
+  const int T = P.T, H = P.H, W = P.window, tid = threadIdx.x;
+  const int b = blockIdx.y / H, h = blockIdx.y % H, k0 = blockIdx.x * BR;
+  const Roles u = setup(s, 512);
+  const int kr = k0 + u.rloc, ch = u.ch;
   const int qb0 = k0 / BR, qb1 = min(T - 1, k0 + BR - 1 + W) / BR;
-  const float sl2 = rsqrtf((float)HD) * LOG2E;
   const size_t bh = (size_t)b * H + h;
-  uint32_t phase = 0;
-  for (int qb = qb0; qb <= qb1; ++qb) {
-    const int q0 = qb * BR;
-    load_tile(s.Q, a.q, b, h, q0, T, H, rope, s.invf);
-    load_tile(s.dO, a.dout, b, h, q0, T, H, false, s.invf);
-    {
-      const int t = q0 + tid;
-      s.lse2[tid] = t < T ? a.lse[bh * T + t] * LOG2E : 0.f;
-      s.delta[tid] = t < T ? a.delta[bh * T + t] : 0.f;
+  auto stage = [&](int qb, int buf) {  // Q, dO tiles and the queries' lse, delta
+    load_tile_async(s.Q[buf], a.qr, b, h, qb * BR, T, H);
+    load_tile_async(s.dO[buf], a.dout, b, h, qb * BR, T, H);
+    if (tid < BR) {
+      const int t = qb * BR + tid;
+      s.lse2[buf][tid] = t < T ? a.lse[bh * T + t] * LOG2E : 0.f;
+      s.delta[buf][tid] = t < T ? a.delta[bh * T + t] : 0.f;
     }
-    fence_async_smem();
-    cta_sync();
-    if (w == 0) {
-      mma_tiles(tm, s.K, HD, s.Q, HD, false, BR, HD, false);         // S^T = K Q^T
-      mma_tiles(tm + 128, s.V, HD, s.dO, HD, false, BR, HD, false);  // dP^T = V dO^T
+  };
+  load_tile_async(s.K, a.kr, b, h, k0, T, H);
+  load_tile_async(s.V, a.v, b, h, k0, T, H);
+  stage(qb0, 0);
+  cp_async_commit();
+  const float sl2 = rsqrtf((float)HD) * LOG2E;
+  uint32_t phase = 0;
+  bool done = true;
+  for (int qb = qb0; qb <= qb1; ++qb) {
+    const int q0 = qb * BR, cur = (qb - qb0) & 1;
+    tiles_ready();
+    if (u.w == 0) {
+      mma_tiles(u.tm, s.K, HD, s.Q[cur], HD, false, BR, HD, false);         // S^T = K Q^T
+      mma_tiles(u.tm + 128, s.V, HD, s.dO[cur], HD, false, BR, HD, false);  // dP^T = V dO^T
       mma_commit(&s.bar);
     }
+    if (qb < qb1) stage(qb + 1, cur ^ 1);
+    cp_async_commit();
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) break;
-    for (int c = 0; c < BR; c += 16) {
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
+      const int cc = 64 * ch + c;
       float sv[16], dp[16];
-      tmem_ld16(tm + lane + c, sv);
-      tmem_ld16(tm + lane + 128 + c, dp);
+      tmem_ld16(u.tm + u.lane + cc, sv);
+      tmem_ld16(u.tm + u.lane + 128 + cc, dp);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int qq = q0 + c + j;
+        const int qq = q0 + cc + j;
         const bool ok = kr <= qq && qq - kr <= W && qq < T && kr < T;
-        const float pr = ok ? exp2f(sv[j] * sl2 - s.lse2[c + j]) : 0.f;
+        const float pr = ok ? exp2f(sv[j] * sl2 - s.lse2[cur][cc + j]) : 0.f;
         sv[j] = pr;
-        dp[j] = pr * (dp[j] - s.delta[c + j]);
+        dp[j] = pr * (dp[j] - s.delta[cur][cc + j]);
       }
-      store16(s.Pt, tid, c, sv);
-      store16(s.dSt, tid, c, dp);
+      store16(s.Pt, u.rloc, cc, sv);
+      store16(s.dSt, u.rloc, cc, dp);
     }
     fence_async_smem();
     cta_sync();
-    if (w == 0) {
-      mma_tiles(tm + 256, s.Pt, BR, s.dO, HD, true, HD, BR, qb > qb0);  // dV += P^T dO
-      mma_tiles(tm + 320, s.dSt, BR, s.Q, HD, true, HD, BR, qb > qb0);  // dK += dS^T Q
+    if (u.w == 0) {
+      mma_tiles(u.tm + 256, s.Pt, BR, s.dO[cur], HD, true, HD, BR, qb > qb0);  // dV += P^T dO
+      mma_tiles(u.tm + 320, s.dSt, BR, s.Q[cur], HD, true, HD, BR, qb > qb0);  // dK += dS^T Q
       mma_commit(&s.bar);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) break;
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
   }
-  if (!s.bad) {
-    float v[HD];
-    tmem_ld32x(tm + lane + 256, v);
-    tmem_ld32x(tm + lane + 288, v + 32);
+  cp_async_wait<0>();
+  if (done) {
+    float v[32];
+    tmem_ld_half(u.tm + u.lane + 256, ch, v);
     tmem_wait_ld();
-    store_row(a.dv, b, h, kr, T, H, v, false, s.invf);
-    tmem_ld32x(tm + lane + 320, v);
-    tmem_ld32x(tm + lane + 352, v + 32);
+    store_half_row(a.dv, b, h, kr, T, H, ch, v, false);
+    tmem_ld_half(u.tm + u.lane + 320, ch, v);
     tmem_wait_ld();
     const float sc = rsqrtf((float)HD);
 #pragma unroll
-    for (int i = 0; i < HD; ++i) v[i] *= sc;
-    store_row(a.dk, b, h, kr, T, H, v, rope, s.invf);
+    for (int i = 0; i < 32; ++i) v[i] *= sc;
+    store_half_row(a.dk, b, h, kr, T, H, ch, v, P.rope != 0);
   }
   cta_sync();
-  if (w == 0) tmem_dealloc(tm, 512);
+  if (u.w == 0) tmem_dealloc(u.tm, 512);
 }
 
 struct QSmem {
-  uint8_t Q[TILE], dO[TILE], K[TILE], V[TILE], dS[PTILE];
-  float invf[HD / 2];
+  uint8_t Q[TILE], dO[TILE], K[2][TILE], V[2][TILE], dS[PTILE];
   uint64_t bar;
   uint32_t tmem;
   volatile int bad;
 };
 
-// dQ for one block of 128 queries over its band of key blocks
-__global__ void __launch_bounds__(128) dq_kernel(Args a) {
+// dQ of one block of 128 queries over its band of key blocks
+__global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
   extern __shared__ uint8_t raw[];
   QSmem& s = *(QSmem*)align128(raw);
   const AtlasSwaParams& P = a.p;
-  const int T = P.T, H = P.H, W = P.window, tid = threadIdx.x, w = tid >> 5;
-  const int b = blockIdx.y / H, h = blockIdx.y % H, q0 = blockIdx.x * BR, row = q0 + tid;
-  const bool rope = P.rope != 0;
-  init_invf(s.invf);
-  if (w == 0) {
-    tmem_alloc(&s.tmem, 512);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(&s.bar, 1);
-    fence_mbar_init();
-    s.bad = 0;
-  }
-  cta_sync();
-  const uint32_t tm = s.tmem, lane = (uint32_t)(32 * w) << 16;
-  load_tile(s.Q, a.q, b, h, q0, T, H, rope, s.invf);
-  load_tile(s.dO, a.dout, b, h, q0, T, H, false, s.invf);
+  const int T = P.T, H = P.H, W = P.window;
+  const int b = blockIdx.y / H, h = blockIdx.y % H, q0 = blockIdx.x * BR;
+  const Roles u = setup(s, 512);
+  const int row = q0 + u.rloc, ch = u.ch;
   const size_t bh = (size_t)b * H + h;
   const float lse2 = row < T ? a.lse[bh * T + row] * LOG2E : 0.f;
   const float dl = row < T ? a.delta[bh * T + row] : 0.f;
   const int kb0 = max(0, q0 - W) / BR, kb1 = min(T - 1, q0 + BR - 1) / BR;
+  load_tile_async(s.Q, a.qr, b, h, q0, T, H);
+  load_tile_async(s.dO, a.dout, b, h, q0, T, H);
+  load_tile_async(s.K[0], a.kr, b, h, kb0 * BR, T, H);
+  load_tile_async(s.V[0], a.v, b, h, kb0 * BR, T, H);
+  cp_async_commit();
   const float sl2 = rsqrtf((float)HD) * LOG2E;
   uint32_t phase = 0;
+  bool done = true;
   for (int kb = kb0; kb <= kb1; ++kb) {
-    const int k0 = kb * BR;
-    load_tile(s.K, a.k, b, h, k0, T, H, rope, s.invf);
-    load_tile(s.V, a.v, b, h, k0, T, H, false, s.invf);
-    fence_async_smem();
-    cta_sync();
-    if (w == 0) {
-      mma_tiles(tm, s.Q, HD, s.K, HD, false, BR, HD, false);         // S = Q K^T
-      mma_tiles(tm + 128, s.dO, HD, s.V, HD, false, BR, HD, false);  // dP = dO V^T
+    const int k0 = kb * BR, cur = (kb - kb0) & 1;
+    tiles_ready();
+    if (u.w == 0) {
+      mma_tiles(u.tm, s.Q, HD, s.K[cur], HD, false, BR, HD, false);         // S = Q K^T
+      mma_tiles(u.tm + 128, s.dO, HD, s.V[cur], HD, false, BR, HD, false);  // dP = dO V^T
       mma_commit(&s.bar);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) break;
-    for (int c = 0; c < BR; c += 16) {
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
+    // K[cur ^ 1] and V[cur ^ 1] were last read by the previous block's MMAs (complete)
+    if (kb < kb1) {
+      load_tile_async(s.K[cur ^ 1], a.kr, b, h, k0 + BR, T, H);
+      load_tile_async(s.V[cur ^ 1], a.v, b, h, k0 + BR, T, H);
+    }
+    cp_async_commit();
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
+      const int cc = 64 * ch + c;
       float sv[16], dp[16];
-      tmem_ld16(tm + lane + c, sv);
-      tmem_ld16(tm + lane + 128 + c, dp);
+      tmem_ld16(u.tm + u.lane + cc, sv);
+      tmem_ld16(u.tm + u.lane + 128 + cc, dp);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int key = k0 + c + j;
+        const int key = k0 + cc + j;
         const bool ok = key <= row && row - key <= W && key < T && row < T;
         const float pr = ok ? exp2f(sv[j] * sl2 - lse2) : 0.f;
         dp[j] = pr * (dp[j] - dl);
       }
-      store16(s.dS, tid, c, dp);
+      store16(s.dS, u.rloc, cc, dp);
     }
     fence_async_smem();
     cta_sync();
-    if (w == 0) {
-      mma_tiles(tm + 256, s.dS, BR, s.K, HD, true, HD, BR, kb > kb0);  // dQ += dS K
+    if (u.w == 0) {
+      mma_tiles(u.tm + 256, s.dS, BR, s.K[cur], HD, true, HD, BR, kb > kb0);  // dQ += dS K
       mma_commit(&s.bar);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) break;
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
   }
-  if (!s.bad) {
-    float v[HD];
-    tmem_ld32x(tm + lane + 256, v);
-    tmem_ld32x(tm + lane + 288, v + 32);
+  cp_async_wait<0>();
+  if (done) {
+    float v[32];
+    tmem_ld_half(u.tm + u.lane + 256, ch, v);
     tmem_wait_ld();
     const float sc = rsqrtf((float)HD);
 #pragma unroll
-    for (int i = 0; i < HD; ++i) v[i] *= sc;
-    store_row(a.dq, b, h, row, T, H, v, rope, s.invf);
+    for (int i = 0; i < 32; ++i) v[i] *= sc;
+    store_half_row(a.dq, b, h, row, T, H, ch, v, P.rope != 0);
   }
   cta_sync();
-  if (w == 0) tmem_dealloc(tm, 512);
+  if (u.w == 0) tmem_dealloc(u.tm, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -492,13 +573,28 @@ static int check(const AtlasSwaParams* p) {
   return ATLAS_OK;
 }
 
-template <class S>
-static size_t smem_of() {
-  return sizeof(S) + 128;
+static size_t act_bytes(const AtlasSwaParams& p) {
+  return ((size_t)p.B * p.T * p.H * HD * 2 + 255) & ~(size_t)255;
 }
+static size_t ws_bytes(const AtlasSwaParams& p) { return 2 * act_bytes(p) + (size_t)p.B * p.H * p.T * sizeof(float); }
 
 static int launch_status(cudaError_t e) {
   return e == cudaSuccess ? ATLAS_OK : report_error(ATLAS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+static int elem_grid(long n) { return (int)std::max(1L, std::min((n + 255) / 256, 148L * 16)); }
+
+// rotated q, k into the workspace
+static void carve(Args& a, void* ws) {
+  uint8_t* w = (uint8_t*)ws;
+  a.qr = (__nv_bfloat16*)w;
+  a.kr = (__nv_bfloat16*)(w + act_bytes(a.p));
+  a.delta = (float*)(w + 2 * act_bytes(a.p));
+}
+
+template <class S>
+static cudaError_t set_smem(const void* fn, size_t bytes) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
 }  // namespace swa
@@ -507,11 +603,18 @@ static int launch_status(cudaError_t e) {
 using namespace atlas;
 using namespace atlas::swa;
 
+extern "C" size_t atlas_swa_workspace_bytes(const AtlasSwaParams* p) {
+  if (check(p) != ATLAS_OK) return 0;
+  return ws_bytes(*p);
+}
+
 extern "C" int atlas_swa_fwd(const AtlasSwaParams* p, const void* q, const void* k, const void* v, void* o,
-                             float* lse, void* stream) {
+                             float* lse, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check(p);
   if (rc) return rc;
   if (!q || !k || !v || !o || !lse) return report_error(ATLAS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (!workspace || workspace_bytes < ws_bytes(*p))
+    return report_error(ATLAS_ERR_WORKSPACE, "workspace smaller than atlas_swa_workspace_bytes()");
   Args a{};
   a.p = *p;
   a.q = (const __nv_bfloat16*)q;
@@ -520,16 +623,14 @@ extern "C" int atlas_swa_fwd(const AtlasSwaParams* p, const void* q, const void*
   a.out = (__nv_bfloat16*)o;
   a.lse = lse;
   a.status = device_status_ptr();
-  const size_t sm = smem_of<FwdSmem>();
-  cudaError_t e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  carve(a, workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+  rope_kernel<<<elem_grid((long)p->B * p->T * p->H * 8), 256, 0, s>>>(a);
+  const size_t sm = sizeof(FwdSmem) + 128;
+  cudaError_t e = set_smem<FwdSmem>((const void*)fwd_kernel, sm);
   if (e != cudaSuccess) return launch_status(e);
-  fwd_kernel<<<dim3((p->T + BR - 1) / BR, p->B * p->H), 128, sm, (cudaStream_t)stream>>>(a);
+  fwd_kernel<<<dim3((p->T + BR - 1) / BR, p->B * p->H), NTH, sm, s>>>(a);
   return launch_status(cudaGetLastError());
-}
-
-extern "C" size_t atlas_swa_workspace_bytes(const AtlasSwaParams* p) {
-  if (check(p) != ATLAS_OK) return 0;
-  return (size_t)p->B * p->H * p->T * sizeof(float);
 }
 
 extern "C" int atlas_swa_bwd(const AtlasSwaParams* p, const void* q, const void* k, const void* v, const void* o,
@@ -539,7 +640,7 @@ extern "C" int atlas_swa_bwd(const AtlasSwaParams* p, const void* q, const void*
   if (rc) return rc;
   if (!q || !k || !v || !o || !lse || !dout || !dq || !dk || !dv)
     return report_error(ATLAS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
-  if (!workspace || workspace_bytes < (size_t)p->B * p->H * p->T * sizeof(float))
+  if (!workspace || workspace_bytes < ws_bytes(*p))
     return report_error(ATLAS_ERR_WORKSPACE, "workspace smaller than atlas_swa_workspace_bytes()");
   Args a{};
   a.p = *p;
@@ -552,20 +653,21 @@ extern "C" int atlas_swa_bwd(const AtlasSwaParams* p, const void* q, const void*
   a.dk = (__nv_bfloat16*)dk;
   a.dv = (__nv_bfloat16*)dv;
   a.lse = const_cast<float*>(lse);
-  a.delta = (float*)workspace;
   a.status = device_status_ptr();
+  carve(a, workspace);
   cudaStream_t s = (cudaStream_t)stream;
-  const long rows = (long)p->B * p->T * p->H;
-  delta_kernel<<<(int)std::min<long>((rows + 255) / 256, 148L * 16), 256, 0, s>>>(a);
+  rope_kernel<<<elem_grid((long)p->B * p->T * p->H * 8), 256, 0, s>>>(a);
+  delta_kernel<<<elem_grid((long)p->B * p->T * p->H), 256, 0, s>>>(a);
   const dim3 grid((p->T + BR - 1) / BR, p->B * p->H);
-  size_t sm = smem_of<KVSmem>();
-  cudaError_t e = cudaFuncSetAttribute(dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  // each CTA of these two kernels allocates all 512 TMEM columns of its SM; their
+  // shared-memory requests (>= 114 KB) keep them at one CTA per SM
+  size_t sm = std::max(sizeof(KVSmem) + 128, (size_t)120 * 1024);
+  cudaError_t e = set_smem<KVSmem>((const void*)dkv_kernel, sm);
   if (e != cudaSuccess) return launch_status(e);
-  dkv_kernel<<<grid, 128, sm, s>>>(a);
-  // one CTA per SM (as for dkv_kernel): each allocates 512 TMEM columns, all of the SM's
-  sm = std::max(smem_of<QSmem>(), (size_t)120 * 1024);
-  e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  dkv_kernel<<<grid, NTH, sm, s>>>(a);
+  sm = std::max(sizeof(QSmem) + 128, (size_t)120 * 1024);
+  e = set_smem<QSmem>((const void*)dq_kernel, sm);
   if (e != cudaSuccess) return launch_status(e);
-  dq_kernel<<<grid, 128, sm, s>>>(a);
+  dq_kernel<<<grid, NTH, sm, s>>>(a);
   return launch_status(cudaGetLastError());
 }

@@ -40,12 +40,13 @@ typedef struct {
   int32_t rope;        /* 1: apply RoPE to q and k inside the kernels (the reference); 0: q, k as given */
 } AtlasSwaParams;
 
+/* Workspace of both calls: the rotated q and k (bf16) and B*H*T float32 (the
+ * per-query dO.o sums of the backward). */
+size_t atlas_swa_workspace_bytes(const AtlasSwaParams* p);
+
 /* Forward: o (B,T,H,D) bf16 and lse (B,H,T) float32. */
 int atlas_swa_fwd(const AtlasSwaParams* p, const void* q, const void* k, const void* v, void* o, float* lse,
-                  void* stream);
-
-/* Workspace of atlas_swa_bwd: B*H*T float32 (the per-query dO.o sums). */
-size_t atlas_swa_workspace_bytes(const AtlasSwaParams* p);
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* VJP: dq, dk (with respect to the pre-RoPE q, k), dv, all (B,T,H,D) bf16. */
 int atlas_swa_bwd(const AtlasSwaParams* p, const void* q, const void* k, const void* v, const void* o,
