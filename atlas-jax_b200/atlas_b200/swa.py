@@ -109,3 +109,16 @@ class SlidingWindowAttention(nn.Module):
         q, k, v = (t.reshape(B, T, H, D).contiguous() for t in qkv.split(H * D, dim=-1))
         o = sliding_window_attention(q, k, v, self.window_size)
         return self.to_out(o.reshape(B, T, H * D).to(x.dtype))
+
+
+if __name__ == "__main__":
+    # Profiling case: seeded bf16 q, k, v, dO of shape (1, 32768, 12, 64), window 1024,
+    # forward + backward twice (python -m atlas_b200.swa from atlas-jax_b200/).
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    q, k, v, do = (torch.randn(1, 32768, 12, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    for _ in range(2):
+        o, lse = swa_forward(q, k, v, 1024)
+        swa_backward(q, k, v, o, lse, do, 1024)
+    torch.cuda.synchronize()
+    print("ok")
