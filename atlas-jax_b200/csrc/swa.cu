@@ -86,6 +86,13 @@ __global__ void rope_kernel(Args a) {
   }
 }
 
+// 2^x on the SFU (ex2.approx: relative error ~2^-22; 2^-inf = 0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
 }
@@ -275,38 +282,37 @@ __global__ void __launch_bounds__(NTH) fwd_kernel(Args a) {
       break;
     }
     // online softmax over this block's keys (model.py:126-131); this thread holds
-    // keys [64 ch, 64 ch + 64) of its row
+    // keys [64 ch, 64 ch + 64) of its row.  Blocks wholly inside the band skip the mask.
+    float sv[64];
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) tmem_ld16(u.tm + u.lane + 64 * ch + c, sv + c);
+    tmem_wait_ld();
+    const bool full = k0 + BR - 1 <= q0 && q0 + BR - 1 - k0 <= W && k0 + BR <= T;
     float mx = -INFINITY;
+    if (full) {
 #pragma unroll
-    for (int c = 0; c < 64; c += 16) {
-      float v[16];
-      tmem_ld16(u.tm + u.lane + 64 * ch + c, v);
-      tmem_wait_ld();
+      for (int j = 0; j < 64; ++j) mx = fmaxf(mx, sv[j]);
+    } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int key = k0 + 64 * ch + c + j;
-        if (key <= row && row - key <= W && key < T) mx = fmaxf(mx, v[j] * sl2);
+      for (int j = 0; j < 64; ++j) {
+        const int key = k0 + 64 * ch + j;
+        if (!(key <= row && row - key <= W && key < T)) sv[j] = -INFINITY;
+        mx = fmaxf(mx, sv[j]);
       }
     }
-    s.mx[ch][u.rloc] = mx;
+    s.mx[ch][u.rloc] = mx * sl2;
     cta_sync();
     const float mn = fmaxf(m, fmaxf(s.mx[0][u.rloc], s.mx[1][u.rloc]));
-    const float corr = mn == -INFINITY ? 1.f : exp2f(m - mn);
+    const float corr = mn == -INFINITY ? 1.f : ex2(m - mn);
+    const float msub = mn == -INFINITY ? 0.f : mn;
     float psum = 0.f;
 #pragma unroll
-    for (int c = 0; c < 64; c += 16) {
-      float v[16];
-      tmem_ld16(u.tm + u.lane + 64 * ch + c, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int key = k0 + 64 * ch + c + j;
-        const bool ok = key <= row && row - key <= W && key < T;
-        v[j] = ok ? exp2f(v[j] * sl2 - mn) : 0.f;
-        psum += v[j];
-      }
-      store16(s.P, u.rloc, 64 * ch + c, v);
+    for (int j = 0; j < 64; ++j) {
+      sv[j] = ex2(fmaf(sv[j], sl2, -msub));  // masked keys: ex2(-inf) = 0
+      psum += sv[j];
     }
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) store16(s.P, u.rloc, 64 * ch + c, sv + c);
     lsum = lsum * corr + psum;
     m = mn;
     cp_async_wait<1>();  // V of this block (the newest group is the next K)
@@ -410,6 +416,7 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
   bool done = true;
   for (int qb = qb0; qb <= qb1; ++qb) {
     const int q0 = qb * BR, cur = (qb - qb0) & 1;
+    const bool full = k0 + BR - 1 <= q0 && q0 + BR - 1 - k0 <= W && q0 + BR <= T;  // no mask needed
     tiles_ready();
     if (u.w == 0) {
       mma_tiles(u.tm, s.K, HD, s.Q[cur], HD, false, BR, HD, false);         // S^T = K Q^T
@@ -433,8 +440,8 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int qq = q0 + cc + j;
-        const bool ok = kr <= qq && qq - kr <= W && qq < T && kr < T;
-        const float pr = ok ? exp2f(sv[j] * sl2 - s.lse2[cur][cc + j]) : 0.f;
+        const bool ok = full || (kr <= qq && qq - kr <= W && qq < T && kr < T);
+        const float pr = ok ? ex2(fmaf(sv[j], sl2, -s.lse2[cur][cc + j])) : 0.f;
         sv[j] = pr;
         dp[j] = pr * (dp[j] - s.delta[cur][cc + j]);
       }
@@ -501,6 +508,7 @@ __global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
   bool done = true;
   for (int kb = kb0; kb <= kb1; ++kb) {
     const int k0 = kb * BR, cur = (kb - kb0) & 1;
+    const bool full = k0 + BR - 1 <= q0 && q0 + BR - 1 - k0 <= W && q0 + BR <= T;  // no mask needed
     tiles_ready();
     if (u.w == 0) {
       mma_tiles(u.tm, s.Q, HD, s.K[cur], HD, false, BR, HD, false);         // S = Q K^T
@@ -528,8 +536,8 @@ __global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = k0 + cc + j;
-        const bool ok = key <= row && row - key <= W && key < T && row < T;
-        const float pr = ok ? exp2f(sv[j] * sl2 - lse2) : 0.f;
+        const bool ok = full || (key <= row && row - key <= W && key < T && row < T);
+        const float pr = ok ? ex2(fmaf(sv[j], sl2, -lse2)) : 0.f;
         dp[j] = pr * (dp[j] - dl);
       }
       store16(s.dS, u.rloc, cc, dp);
