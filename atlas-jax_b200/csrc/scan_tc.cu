@@ -247,6 +247,8 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   for (long k = cluster; k < total; k += nclusters) {
     const int q = (int)(k % K.nchains), c = (int)(k / K.nchains);
     const int b = q / H, hh = q % H;
+    PROF_T(titem)
+    PROF_T(twait)
     // ---- wait for the previous chunk of this chain ----
     if (c > 0 && tid == 0 && !s.bad) {
       int spins = 0;
@@ -260,6 +262,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
       }
     }
     epi_sync();
+    PROF_ADD(13, twait)
     float* slot = carry_slot(a, K.carries, q, c, nch);
     float* mine = slot + 2 * rank * DE;  // [W, S] of this CTA's matrix
     if (c == 0) {  // initial carry: caller's state or the LM init (model.py:251-264)
@@ -426,6 +429,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
     __threadfence();
     cluster_sync();
     if (rank == 0 && tid == 0) st_release(&K.flags[q], c + 1);
+    PROF_ADD(14, titem)
   }
   }  // epilogue warps
   fence_before();

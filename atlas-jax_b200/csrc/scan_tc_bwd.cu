@@ -485,6 +485,8 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   for (long kk = cluster; kk < total; kk += nclusters) {
     const int q = (int)(kk % K.nchains), j = (int)(kk / K.nchains), c = nch - 1 - j;
     const int b = q / H, hh = q % H;
+    PROF_T(titem)
+    PROF_T(twait)
     if (j > 0 && tid == 0 && !s.bad) {
       int spins = 0;
       while (ld_acquire(&K.flags[q]) < j + K.hooks.flag_bias) {
@@ -497,6 +499,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
       }
     }
     epi_sync();
+    PROF_ADD(26, twait)
     const float* slot = (const float*)a.saved + ((size_t)q * nch + c) * 4 * DE;
     const float* mine = slot + 2 * rank * DE;
     // zero the accumulators of this cluster (rank 0: dF, rank 1: dG and scalars)
@@ -1240,6 +1243,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     __threadfence();
     cluster_sync();
     if (rank == 0 && tid == 0) st_release(&K.flags[q], j + 1);
+    PROF_ADD(27, titem)
   }
   }  // epilogue warps
   fence_before();
