@@ -18,7 +18,7 @@ from .scan import _ptr, _stream
 class AtlasLayerParams(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "abi_version", "B", "T", "H", "D", "conv_kernel", "poly_degree", "has_gamma", "has_retrieve",
-        "act_dtype")] + [("max_lr", ctypes.c_float)]
+        "act_dtype", "proj_stride")] + [("max_lr", ctypes.c_float)]
 
 
 _P = ctypes.c_void_p
@@ -56,6 +56,7 @@ class LayerGeometry:
     has_gamma: bool = True
     has_retrieve: bool = True
     max_lr: float = 0.1
+    pad_rows: bool = True  # proj rows padded to a multiple of 8 elements (16-byte lanes)
 
     @property
     def n_gates(self):
@@ -66,10 +67,16 @@ class LayerGeometry:
         """Columns of the concatenated projection: q, k, v (H*D each) then the gates (H each)."""
         return 3 * self.H * self.D + self.n_gates * self.H
 
+    @property
+    def proj_stride(self):
+        """Row stride of proj / dproj: n_proj rounded up to 8 (padding columns are zero)."""
+        return (self.n_proj + 7) // 8 * 8 if self.pad_rows else self.n_proj
+
     def params(self, dtype):
         return AtlasLayerParams(L.ATLAS_ABI_VERSION, self.B, self.T, self.H, self.D, self.conv_kernel,
                                 self.poly_degree, int(self.has_gamma), int(self.has_retrieve),
-                                L.ATLAS_BF16 if dtype == torch.bfloat16 else L.ATLAS_F32, self.max_lr)
+                                L.ATLAS_BF16 if dtype == torch.bfloat16 else L.ATLAS_F32, self.proj_stride,
+                                self.max_lr)
 
 
 def _need(x, dtype, shape, name):
@@ -78,13 +85,13 @@ def _need(x, dtype, shape, name):
 
 
 def prologue_forward(geo, proj, conv_w, conv_b, poly, gate_bias):
-    """proj (B*T, NP) act dtype -> q, k, v (B,T,H,D) act dtype and the gates (B,T,H) float32
+    """proj (B*T, proj_stride) act dtype -> q, k, v (B,T,H,D) act dtype and the gates (B,T,H) float32
     [alpha, eta, theta, gamma or None, retrieve or None]."""
     lib = _lib()
     B, T, H, D = geo.B, geo.T, geo.H, geo.D
     dt, dev = proj.dtype, proj.device
-    _need(proj, dt, (B * T, geo.n_proj), "proj")
-    _need(conv_w, torch.float32, (3, H * D, geo.conv_kernel), "conv_w")
+    _need(proj, dt, (B * T, geo.proj_stride), "proj")
+    _need(conv_w, torch.float32, (3, geo.conv_kernel, H * D), "conv_w")
     _need(conv_b, torch.float32, (3, H * D), "conv_b")
     _need(gate_bias, torch.float32, (geo.n_gates - int(geo.has_retrieve), H), "gate_bias")
     p = geo.params(dt)

@@ -113,7 +113,10 @@ class AtlasMemoryLayer(nn.Module):
         if self.retrieve_gate is not None:
             lin.append(self.retrieve_gate)
         W = torch.cat([m.weight for m in lin], 0)
-        conv_w = torch.stack([c.weight[:, 0, :] for c in (self.conv_q, self.conv_k, self.conv_v)]).float()
+        pad = self.geometry(1, 1).proj_stride - W.shape[0]  # zero rows: 16-byte aligned projection rows
+        if pad:
+            W = torch.cat([W, W.new_zeros(pad, W.shape[1])], 0)
+        conv_w = torch.stack([c.weight[:, 0, :].t() for c in (self.conv_q, self.conv_k, self.conv_v)]).float()  # (3, K, di)
         conv_b = torch.stack([c.bias for c in (self.conv_q, self.conv_k, self.conv_v)]).float()
         gate_b = torch.stack([m.bias for m in gates]).float()
         poly = self.poly_coeffs.float() if self.poly_coeffs is not None else None

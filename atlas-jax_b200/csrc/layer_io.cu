@@ -28,6 +28,7 @@ constexpr int MAXP = 4;  // polynomial degree
 
 struct Geo {
   int B, T, H, D, K, P, G, di, NP, has_gamma, has_ret;
+  int ld;  // row stride of proj / dproj (elements)
   float max_lr;
 };
 
@@ -39,6 +40,7 @@ inline Geo geo(const AtlasLayerParams& p) {
   g.G = 3 + g.has_gamma + g.has_ret;
   g.di = p.H * p.D;
   g.NP = 3 * g.di + g.G * p.H;
+  g.ld = p.proj_stride > 0 ? p.proj_stride : g.NP;
   g.max_lr = p.max_lr;
   return g;
 }
@@ -74,14 +76,14 @@ __device__ __forceinline__ float poly_d(const float* a, int P, float x) {
 }
 
 // Causal depthwise conv of channel c at token t of batch b (memory_layer.py:318-329):
-//   out = bias[c] + sum_j w[c][j] * P[t - (K-1) + j][c]
+//   out = bias[c] + sum_j w[j][c] * P[t - (K-1) + j][c]   (weights tap-major)
 template <typename TA>
 __device__ __forceinline__ float conv_at(const TA* proj, const float* w, const float* bias, const Geo& g, int b,
                                          int t, int col, int c) {
   float acc = bias[c];
   for (int j = 0; j < g.K; ++j) {
     const int ts = t - (g.K - 1) + j;
-    if (ts >= 0) acc = fmaf(w[(size_t)c * g.K + j], ld_act(proj, ((size_t)b * g.T + ts) * g.NP + col), acc);
+    if (ts >= 0) acc = fmaf(w[(size_t)j * g.di + c], ld_act(proj, ((size_t)b * g.T + ts) * g.ld + col), acc);
   }
   return acc;
 }
@@ -147,7 +149,7 @@ __global__ void gates_fwd_kernel(Geo g, const TA* proj, const float* gate_bias, 
     const int col = (int)(i % (g.G * g.H)), gi = col / g.H, h = col % g.H;
     const long n = i / (g.G * g.H);
     const bool ret = g.has_ret && gi == g.G - 1;
-    float z = ld_act(proj, (size_t)n * g.NP + 3 * g.di + col);
+    float z = ld_act(proj, (size_t)n * g.ld + 3 * g.di + col);
     if (!ret) z += gate_bias[col];
     float s = sigmoidf_(z);
     if (gi == 1) s *= g.max_lr;
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(256) qkv_bwd2_kernel(Geo g, const TA* proj, co
   float wv[MAXK], dw[MAXK];
 #pragma unroll
   for (int j = 0; j < MAXK; ++j) {
-    wv[j] = j < g.K ? conv_w[((size_t)wsel * g.di + c) * g.K + j] : 0.f;
+    wv[j] = j < g.K ? conv_w[((size_t)wsel * g.K + j) * g.di + c] : 0.f;
     dw[j] = 0.f;
   }
   float db = 0.f;
@@ -317,15 +319,15 @@ __global__ void __launch_bounds__(256) qkv_bwd2_kernel(Geo g, const TA* proj, co
     for (int j = 0; j < MAXK; ++j)
       if (j < g.K) {
         const int ts = t - (g.K - 1) + j;  // input token feeding output t through tap j
-        if (ts >= 0) dw[j] = fmaf(d, ld_act(proj, ((size_t)b * g.T + ts) * g.NP + col), dw[j]);
+        if (ts >= 0) dw[j] = fmaf(d, ld_act(proj, ((size_t)b * g.T + ts) * g.ld + col), dw[j]);
         const int to = t + (g.K - 1) - j;  // output token that reads input t through tap j
         if (to < g.T) acc = fmaf(wv[j], dc[((size_t)b * g.T + to) * rowdc + col], acc);
       }
-    st_act(dproj, n * g.NP + col, acc);
+    st_act(dproj, n * g.ld + col, acc);
   }
 #pragma unroll
   for (int j = 0; j < MAXK; ++j)
-    if (j < g.K) atomicAdd(&dconv_w[((size_t)wsel * g.di + c) * g.K + j], dw[j]);
+    if (j < g.K) atomicAdd(&dconv_w[((size_t)wsel * g.K + j) * g.di + c], dw[j]);
   atomicAdd(&dconv_b[col], db);
 }
 
@@ -341,23 +343,236 @@ __global__ void gates_bwd_kernel(Geo g, const TA* proj, const float* gate_bias, 
   const int GH = g.G * g.H;
   for (int i = threadIdx.x; i < GH; i += blockDim.x) sb[i] = 0.f;
   __syncthreads();
-  const long items = (long)g.B * g.T * GH;
+  const int ncol = g.ld - 3 * g.di;  // gate columns, then the row padding (written 0)
+  const long items = (long)g.B * g.T * ncol;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += (long)gridDim.x * blockDim.x) {
-    const int col = (int)(i % GH), gi = col / g.H, h = col % g.H;
-    const long n = i / GH;
+    const int col = (int)(i % ncol), gi = col / g.H, h = col % g.H;
+    const long n = i / ncol;
+    if (col >= GH) {
+      st_act(dproj, (size_t)n * g.ld + 3 * g.di + col, 0.f);
+      continue;
+    }
     const bool ret = g.has_ret && gi == g.G - 1;
-    float z = ld_act(proj, (size_t)n * g.NP + 3 * g.di + col);
+    float z = ld_act(proj, (size_t)n * g.ld + 3 * g.di + col);
     if (!ret) z += gate_bias[col];
     const float s = sigmoidf_(z);
     float d = dg.p[gi] ? dg.p[gi][(size_t)n * g.H + h] : 0.f;
     if (gi == 1) d *= g.max_lr;
     const float dz = d * s * (1.f - s);
-    st_act(dproj, (size_t)n * g.NP + 3 * g.di + col, dz);
+    st_act(dproj, (size_t)n * g.ld + 3 * g.di + col, dz);
     if (!ret) atomicAdd(&sb[col], dz);
   }
   __syncthreads();
   const int nb = (g.G - g.has_ret) * g.H;
   for (int i = threadIdx.x; i < nb; i += blockDim.x) atomicAdd(&dbias[i], sb[i]);
+}
+
+
+// ---------------------------------------------------------------------------
+// 16-byte variants: one lane moves 8 consecutive channels, D / 8 lanes per head,
+// 32 / (D / 8) heads per warp (used when D / 8 divides 32 and the rows of proj are
+// 16-byte aligned)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ld8(const float* p, float* v) {
+  const float4 a = *(const float4*)p, b = *(const float4*)(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* v) {
+  const uint4 u = *(const uint4*)p;
+  const __nv_bfloat162* h = (const __nv_bfloat162*)&u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x, v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void st8(float* p, const float* v) {
+  *(float4*)p = make_float4(v[0], v[1], v[2], v[3]);
+  *(float4*)(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void st8(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = (__nv_bfloat162*)&u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+  *(uint4*)p = u;
+}
+// sum over the Lh lanes of one head (an aligned group of the warp)
+__device__ __forceinline__ float group_sum(float v, int Lh) {
+  for (int o = Lh >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+struct VecMap {
+  int Lh, hpw, ngroups;
+};
+inline VecMap vec_map(const Geo& g) {
+  VecMap m;
+  m.Lh = g.D / 8;
+  m.hpw = 32 / m.Lh;
+  m.ngroups = (g.H + m.hpw - 1) / m.hpw;
+  return m;
+}
+inline bool vec_ok(const Geo& g, int esize) {
+  return g.D % 8 == 0 && g.D >= 8 && 32 % (g.D / 8) == 0 && ((size_t)g.ld * esize) % 16 == 0 &&
+         ((size_t)g.di * esize) % 16 == 0;
+}
+
+// conv of channels c0..c0+7 (column col0 of proj) at token t of batch b
+template <typename TA>
+__device__ __forceinline__ void conv8(const TA* proj, const float* w, const float* bias, const Geo& g, int b, int t,
+                                      int col0, int c0, float* x) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = bias[c0 + i];
+  for (int j = 0; j < g.K; ++j) {
+    const int ts = t - (g.K - 1) + j;
+    if (ts < 0) continue;
+    float pv[8];
+    ld8(proj + ((size_t)b * g.T + ts) * g.ld + col0, pv);
+    const float4 w0 = *(const float4*)(w + (size_t)j * g.di + c0), w1 = *(const float4*)(w + (size_t)j * g.di + c0 + 4);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = fmaf(wv[i], pv[i], x[i]);
+  }
+}
+
+template <typename TA>
+__global__ void __launch_bounds__(256) qkv_fwd_vec_kernel(Geo g, VecMap m, const TA* proj, const float* conv_w,
+                                                          const float* conv_b, const float* poly, TA* q, TA* k,
+                                                          TA* v) {
+  __shared__ float pa[MAXP];
+  if (threadIdx.x < MAXP) pa[threadIdx.x] = threadIdx.x < g.P ? poly[threadIdx.x] : 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, hl = lane / m.Lh, part = lane % m.Lh;
+  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
+  const long items = (long)g.B * g.T * 3 * m.ngroups;
+  for (long it = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += nwarps) {
+    const int hg = (int)(it % m.ngroups), wsel = (int)((it / m.ngroups) % 3);
+    const long n = it / (3 * m.ngroups);
+    const int b = (int)(n / g.T), t = (int)(n % g.T), h = hg * m.hpw + hl;
+    const bool valid = h < g.H;
+    const int c0 = h * g.D + 8 * part;
+    float x[8];
+    if (valid)
+      conv8(proj, conv_w + (size_t)wsel * g.di * g.K, conv_b + (size_t)wsel * g.di, g, b, t, wsel * g.di + c0, c0, x);
+    else
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = 0.f;
+    if (wsel == 1 && g.P > 0)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = poly_f(pa, g.P, x[i]);
+    if (wsel < 2) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+      const float r = rsqrtf(group_sum(ss, m.Lh) / g.D + 1e-6f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] *= r;
+    }
+    if (wsel == 0 && g.P > 0)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = poly_f(pa, g.P, x[i]);
+    if (valid) {
+      TA* out = wsel == 0 ? q : (wsel == 1 ? k : v);
+      st8(out + (((size_t)b * g.T + t) * g.H + h) * g.D + 8 * part, x);
+    }
+  }
+}
+
+template <typename TA>
+__global__ void __launch_bounds__(256) qkv_bwd1_vec_kernel(Geo g, VecMap m, const TA* proj, const float* conv_w,
+                                                           const float* conv_b, const float* poly, const TA* dq,
+                                                           const TA* dk, const TA* dv, float* dc, float* dpoly) {
+  __shared__ float pa[MAXP], pacc[MAXP];
+  if (threadIdx.x < MAXP) {
+    pa[threadIdx.x] = threadIdx.x < g.P ? poly[threadIdx.x] : 0.f;
+    pacc[threadIdx.x] = 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, hl = lane / m.Lh, part = lane % m.Lh;
+  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
+  const long items = (long)g.B * g.T * 3 * m.ngroups;
+  float mypoly[MAXP] = {0.f, 0.f, 0.f, 0.f};
+  for (long it = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += nwarps) {
+    const int hg = (int)(it % m.ngroups), wsel = (int)((it / m.ngroups) % 3);
+    const long n = it / (3 * m.ngroups);
+    const int b = (int)(n / g.T), t = (int)(n % g.T), h = hg * m.hpw + hl;
+    const bool valid = h < g.H;
+    const int c0 = h * g.D + 8 * part;
+    const TA* dout = wsel == 0 ? dq : (wsel == 1 ? dk : dv);
+    float c[8], go[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = go[i] = 0.f;
+    if (valid) {
+      if (wsel < 2)
+        conv8(proj, conv_w + (size_t)wsel * g.di * g.K, conv_b + (size_t)wsel * g.di, g, b, t, wsel * g.di + c0, c0,
+              c);
+      if (dout) ld8(dout + (((size_t)b * g.T + t) * g.H + h) * g.D + 8 * part, go);
+    }
+    if (wsel == 0) {  // out = phi(u), u = c r
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(c[i], c[i], ss);
+      const float r = rsqrtf(group_sum(ss, m.Lh) / g.D + 1e-6f);
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (g.P > 0) {
+          const float u = c[i] * r;
+          float xp = u;
+          for (int j = 0; j < g.P; ++j) {
+            mypoly[j] = fmaf(go[i], xp, mypoly[j]);
+            xp *= u;
+          }
+          go[i] *= poly_d(pa, g.P, u);
+        }
+        dot = fmaf(go[i], c[i], dot);
+      }
+      dot = group_sum(dot, m.Lh);
+      const float r3 = r * r * r / g.D;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) go[i] = r * go[i] - r3 * c[i] * dot;
+    } else if (wsel == 1) {  // out = rms(p), p = phi(c)
+      float p[8], ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        p[i] = g.P > 0 ? poly_f(pa, g.P, c[i]) : c[i];
+        ss = fmaf(p[i], p[i], ss);
+      }
+      const float r = rsqrtf(group_sum(ss, m.Lh) / g.D + 1e-6f);
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot = fmaf(go[i], p[i], dot);
+      dot = group_sum(dot, m.Lh);
+      const float r3 = r * r * r / g.D;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float dp = r * go[i] - r3 * p[i] * dot;
+        if (g.P > 0) {
+          float xp = c[i];
+          for (int j = 0; j < g.P; ++j) {
+            mypoly[j] = fmaf(dp, xp, mypoly[j]);
+            xp *= c[i];
+          }
+          dp *= poly_d(pa, g.P, c[i]);
+        }
+        go[i] = dp;
+      }
+    }
+    if (valid) {
+      float* o = dc + (size_t)n * 3 * g.di + wsel * g.di + c0;
+      *(float4*)o = make_float4(go[0], go[1], go[2], go[3]);
+      *(float4*)(o + 4) = make_float4(go[4], go[5], go[6], go[7]);
+    }
+  }
+  if (g.P > 0) {
+    for (int j = 0; j < g.P; ++j) {
+      const float sm = warp_sum(mypoly[j]);
+      if (lane == 0) atomicAdd(&pacc[j], sm);
+    }
+    __syncthreads();
+    if (threadIdx.x < g.P) atomicAdd(&dpoly[threadIdx.x], pacc[threadIdx.x]);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -377,6 +592,8 @@ static int check(const AtlasLayerParams* p) {
     return report_error(ATLAS_ERR_INVALID_ARGUMENT, "conv_kernel must be in 1..8");
   if (p->poly_degree < 0 || p->poly_degree > MAXP)
     return report_error(ATLAS_ERR_INVALID_ARGUMENT, "poly_degree must be in 0..4");
+  if (p->proj_stride != 0 && p->proj_stride < 3 * p->H * p->D + (3 + !!p->has_gamma + !!p->has_retrieve) * p->H)
+    return report_error(ATLAS_ERR_INVALID_ARGUMENT, "proj_stride is smaller than the projection's width");
   if (p->act_dtype != ATLAS_F32 && p->act_dtype != ATLAS_BF16)
     return report_error(ATLAS_ERR_INVALID_ARGUMENT, "act_dtype must be ATLAS_F32 or ATLAS_BF16");
   clear_error();
@@ -391,8 +608,14 @@ static int cuda_status(cudaError_t e) {
 template <typename TA>
 static cudaError_t prologue_fwd_t(const Geo& g, const void* proj, const float* cw, const float* cb, const float* poly,
                                   const float* gb, void* q, void* k, void* v, GatePtrs gp, cudaStream_t s) {
-  const long witems = (long)g.B * g.T * 3 * g.H;
-  qkv_fwd_kernel<TA><<<warp_grid(witems), 256, 0, s>>>(g, (const TA*)proj, cw, cb, poly, (TA*)q, (TA*)k, (TA*)v);
+  if (vec_ok(g, sizeof(TA))) {
+    const VecMap m = vec_map(g);
+    qkv_fwd_vec_kernel<TA><<<warp_grid((long)g.B * g.T * 3 * m.ngroups), 256, 0, s>>>(
+        g, m, (const TA*)proj, cw, cb, poly, (TA*)q, (TA*)k, (TA*)v);
+  } else {
+    const long witems = (long)g.B * g.T * 3 * g.H;
+    qkv_fwd_kernel<TA><<<warp_grid(witems), 256, 0, s>>>(g, (const TA*)proj, cw, cb, poly, (TA*)q, (TA*)k, (TA*)v);
+  }
   const long gitems = (long)g.B * g.T * g.G * g.H;
   gates_fwd_kernel<TA><<<elem_grid(gitems), 256, 0, s>>>(g, (const TA*)proj, gb, gp);
   return cudaGetLastError();
@@ -409,9 +632,15 @@ static cudaError_t prologue_bwd_t(const Geo& g, const void* proj, const float* c
   if (g.P > 0 && (e = cudaMemsetAsync(dpoly, 0, (size_t)g.P * sizeof(float), s)) != cudaSuccess) return e;
   const int nb = (g.G - g.has_ret) * g.H;
   if ((e = cudaMemsetAsync(dgb, 0, (size_t)nb * sizeof(float), s)) != cudaSuccess) return e;
-  const long witems = (long)g.B * g.T * 3 * g.H;
-  qkv_bwd1_kernel<TA><<<warp_grid(witems), 256, 0, s>>>(g, (const TA*)proj, cw, cb, poly, (const TA*)dq,
-                                                         (const TA*)dk, (const TA*)dv, dc, dpoly);
+  if (vec_ok(g, sizeof(TA))) {
+    const VecMap m = vec_map(g);
+    qkv_bwd1_vec_kernel<TA><<<warp_grid((long)g.B * g.T * 3 * m.ngroups), 256, 0, s>>>(
+        g, m, (const TA*)proj, cw, cb, poly, (const TA*)dq, (const TA*)dk, (const TA*)dv, dc, dpoly);
+  } else {
+    const long witems = (long)g.B * g.T * 3 * g.H;
+    qkv_bwd1_kernel<TA><<<warp_grid(witems), 256, 0, s>>>(g, (const TA*)proj, cw, cb, poly, (const TA*)dq,
+                                                           (const TA*)dk, (const TA*)dv, dc, dpoly);
+  }
   const int tiles = (g.T + TT - 1) / TT;
   qkv_bwd2_kernel<TA><<<dim3((3 * g.di + 255) / 256, g.B * tiles), 256, 0, s>>>(g, (const TA*)proj, cw, dc,
                                                                                  (TA*)dproj, dcw, dcb);

@@ -230,8 +230,8 @@ def next_rows(dev, stream, peak_tf, hbm):
     del q, k, v, do, o, lse
     B, T, H, D = 8, 8192, 12, 64
     geo = LayerGeometry(B, T, H, D)
-    proj = torch.randn(B * T, geo.n_proj, device=dev, generator=g).to(torch.bfloat16)
-    cw = torch.randn(3, H * D, 4, device=dev, generator=g) * 0.3
+    proj = torch.randn(B * T, geo.proj_stride, device=dev, generator=g).to(torch.bfloat16)
+    cw = torch.randn(3, 4, H * D, device=dev, generator=g) * 0.3
     cb = torch.zeros(3, H * D, device=dev)
     poly = torch.ones(2, device=dev)
     gb = torch.zeros(4, H, device=dev)

@@ -14,15 +14,16 @@
  * launch and one scan call where the reference makes ~20 XLA ops with HBM
  * round trips between them.
  *
- * Layout.  x's projection "proj" is row-major (B*T, NP), NP = 3*H*D + G*H, in
- * act_dtype, with columns
+ * Layout.  x's projection "proj" is row-major (B*T, NP), NP = 3*H*D + G*H (rows
+ * proj_stride >= NP elements apart, extra columns ignored), in act_dtype, with columns
  *   [ q (H*D) | k (H*D) | v (H*D) | alpha (H) | eta (H) | theta (H) | gamma (H, if has_gamma)
  *     | retrieve (H, if has_retrieve) ]
  * (G = 3 + has_gamma + has_retrieve).  The pre-activation gate columns do not
  * include the gate biases; gate_bias holds them, (G-has_retrieve) x H float32, in
  * the same gate order (the retrieve gate has no bias, memory_layer.py:455-456).
- * conv_w is (3, H*D, K) float32 (q, k, v convolutions, the reference's (dim, 1, K)
- * weights stacked), conv_b (3, H*D), poly (poly_degree) float32.
+ * conv_w is (3, K, H*D) float32, tap-major: the q, k, v convolutions' (dim, 1, K)
+ * reference weights stacked and transposed, so one tap of consecutive channels is
+ * contiguous; conv_b (3, H*D), poly (poly_degree) float32.
  * Outputs: q, k, v (B, T, H, D) in act_dtype; alpha, eta, theta, gamma, retrieve
  * (B, T, H) float32, activated.  Pointers of absent gates may be NULL.
  *
@@ -50,6 +51,8 @@ typedef struct {
   int32_t has_gamma;    /* omega_window > 1 */
   int32_t has_retrieve; /* n_head > 1 */
   int32_t act_dtype;    /* ATLAS_F32 or ATLAS_BF16: proj, q, k, v, dproj, dq, dk, dv */
+  int32_t proj_stride;  /* elements between rows of proj / dproj (0 = NP); a multiple of 8
+                         * (bf16) or 4 (f32) lets the kernels move 16 bytes per lane */
   float max_lr;         /* eta = sigmoid(.) * max_lr */
 } AtlasLayerParams;
 
@@ -65,7 +68,7 @@ int atlas_layer_prologue_fwd(const AtlasLayerParams* p, const void* proj, const 
 /* VJP of atlas_layer_prologue_fwd.  Inputs: the forward's inputs and the cotangents of
  * its outputs (dgamma / dretrieve may be NULL when absent; NULL cotangents count as
  * zero).  Outputs: dproj (B*T, NP) in act_dtype (absent gates' columns are written 0),
- * and the parameter gradients dconv_w (3, H*D, K), dconv_b (3, H*D), dpoly
+ * and the parameter gradients dconv_w (3, K, H*D), dconv_b (3, H*D), dpoly
  * (poly_degree), dgate_bias (G - has_retrieve, H), all float32 and OVERWRITTEN. */
 int atlas_layer_prologue_bwd(const AtlasLayerParams* p, const void* proj, const float* conv_w,
                              const float* conv_b, const float* poly, const float* gate_bias, const void* dq,

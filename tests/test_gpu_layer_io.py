@@ -11,12 +11,14 @@ from oracle import atlas_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-CASES = [  # B, T, H, D, K, poly_degree, gamma, retrieve
-    (2, 70, 3, 64, 4, 2, True, True),
-    (1, 1, 2, 32, 4, 2, True, True),     # T < K
-    (2, 33, 1, 16, 3, 0, False, False),  # no poly, no gamma / retrieve, D < 32
-    (1, 40, 2, 128, 4, 3, False, True),
-    (1, 17, 2, 256, 8, 1, True, False),
+CASES = [  # B, T, H, D, K, poly_degree, gamma, retrieve, padded rows (16-byte lanes)
+    (2, 70, 3, 64, 4, 2, True, True, True),
+    (2, 70, 3, 64, 4, 2, True, True, False),   # unpadded rows: the per-channel kernels
+    (1, 1, 2, 32, 4, 2, True, True, True),     # T < K
+    (2, 33, 1, 16, 3, 0, False, False, True),  # no poly, no gamma / retrieve, D < 32
+    (1, 40, 2, 128, 4, 3, False, True, True),
+    (1, 17, 2, 256, 8, 1, True, False, True),
+    (1, 9, 3, 48, 4, 2, True, True, True),     # D / 8 does not divide 32: per-channel kernels
 ]
 
 
@@ -27,15 +29,16 @@ def rel(a, b):
 
 def _setup(case, dtype, seed=0):
     from atlas_b200.layer_io import LayerGeometry
-    B, T, H, D, K, P, hg, hr = case
-    geo = LayerGeometry(B, T, H, D, K, P, hg, hr, 0.1)
+    B, T, H, D, K, P, hg, hr, pad = case
+    geo = LayerGeometry(B, T, H, D, K, P, hg, hr, 0.1, pad)
     rng = np.random.default_rng(seed)
-    proj = rng.standard_normal((B * T, geo.n_proj)).astype(np.float32)
+    proj = rng.standard_normal((B * T, geo.proj_stride)).astype(np.float32)
     cw, cb, poly, gb = LR.make_params(H, D, K, P, geo.n_gates - int(hr), seed)
     tproj = torch.as_tensor(proj).cuda().to(dtype)
     proj = tproj.float().cpu().numpy()  # what the kernel sees
     dev = lambda x: None if x is None else torch.as_tensor(x).cuda()  # noqa: E731
-    return geo, proj, (cw, cb, poly, gb), tproj, [dev(x) for x in (cw, cb, poly, gb)]
+    cw_k = np.ascontiguousarray(cw.transpose(0, 2, 1))  # the kernel's tap-major layout (3, K, H*D)
+    return geo, proj, (cw, cb, poly, gb), tproj, [dev(x) for x in (cw_k, cb, poly, gb)]
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -44,7 +47,7 @@ def test_prologue_forward(case, dtype):
     from atlas_b200.layer_io import prologue_forward
     geo, proj, (cw, cb, poly, gb), tproj, dp = _setup(case, dtype)
     q, k, v, g = prologue_forward(geo, tproj, *dp)
-    qo, ko, vo, go = O.layer_prologue(proj.astype(np.float64), geo.B, geo.T, geo.H, geo.D, cw, cb, poly, gb,
+    qo, ko, vo, go = O.layer_prologue(proj[:, :geo.n_proj].astype(np.float64), geo.B, geo.T, geo.H, geo.D, cw, cb, poly, gb,
                                       geo.has_gamma, geo.has_retrieve, geo.max_lr)
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     for a, b in ((q, qo), (k, ko), (v, vo)):
@@ -73,6 +76,7 @@ def test_prologue_backward(case, dtype):
                                                     [cu(x) for x in dgs])
     # float64 autograd of the restatement, with the cotangents as the kernel saw them
     leaf = lambda x: None if x is None else torch.tensor(x, dtype=torch.float64, requires_grad=True)  # noqa: E731
+    proj = proj[:, :geo.n_proj]
     P_, cw_, cb_, poly_, gb_ = leaf(proj), leaf(cw), leaf(cb), leaf(poly), leaf(gb)
     q, k, v, g = LR.prologue(P_, B, T, H, D, cw_, cb_, poly_, gb_, geo.has_gamma, geo.has_retrieve, geo.max_lr)
     as64 = lambda x, dt: torch.as_tensor(x).to(dt).double()  # noqa: E731
@@ -80,8 +84,9 @@ def test_prologue_backward(case, dtype):
     loss = loss + sum((o * torch.as_tensor(c).double()).sum() for o, c in zip(g, dgs) if o is not None)
     loss.backward()
     tol = 1e-4 if dtype == torch.float32 else 1e-2
-    assert rel(dproj.float().cpu().numpy(), P_.grad.numpy()) < tol
-    assert rel(dcw.cpu().numpy(), cw_.grad.numpy()) < tol
+    assert rel(dproj[:, :geo.n_proj].float().cpu().numpy(), P_.grad.numpy()) < tol
+    assert float(dproj[:, geo.n_proj:].float().abs().max()) == 0.0 if geo.proj_stride > geo.n_proj else True
+    assert rel(dcw.cpu().numpy().transpose(0, 2, 1), cw_.grad.numpy()) < tol
     assert rel(dcb.cpu().numpy(), cb_.grad.numpy()) < tol
     assert rel(dgb.cpu().numpy(), gb_.grad.numpy()) < tol
     if poly is not None:

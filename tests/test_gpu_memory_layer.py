@@ -2,7 +2,9 @@
 atlas_jax/memory_layer.py:599, scan on the B200 kernels) against the same layer
 written entirely in torch float64 (prologue and epilogue as in
 memory_layer.py:606-633 / 720-725, scan from tests/torch_ref.py), forward and
-parameter gradients.  Exact path: 1e-4; tensor path: 2e-2 (relative, Frobenius)."""
+parameter gradients.  Exact path: 1e-4 (parameter gradients: max(1e-4, 2x the error of
+the same restatement in float32), since the float32 layer inputs to the scan carry
+their rounding into long gradient sums); tensor path: 2e-2 (relative, Frobenius)."""
 import numpy as np
 import pytest
 import torch
@@ -12,13 +14,14 @@ import torch_ref as TR
 pytestmark = pytest.mark.gpu
 
 
-def _reference(layer, x, state=None):
-    """float64 torch restatement of the whole layer with the module's weights."""
-    P = {n: p.detach().double().requires_grad_(True) for n, p in layer.named_parameters()}
+def _reference(layer, x, state=None, dtype=torch.float64):
+    """torch restatement of the whole layer with the module's weights (float64, or
+    float32 to measure the reference's own float32 error)."""
+    P = {n: p.detach().to(dtype).requires_grad_(True) for n, p in layer.named_parameters()}
     cfg = layer.config
     B, T, C = x.shape
     H, D, E = layer.n_head, layer.head_dim, layer.expand_dim
-    xd = x.double()
+    xd = x.to(dtype)
 
     def conv(name, z):
         zt = torch.nn.functional.pad(z.transpose(1, 2), (cfg.conv_kernel - 1, 0))
@@ -61,10 +64,14 @@ def test_memory_layer_forward_and_param_grads(prec, D, tol):
     (y * gy).sum().backward()
     y_ref, P = _reference(layer, x)
     (y_ref * gy.double()).sum().backward()
-    rel = lambda a, b: float((a.double() - b).norm() / b.norm())  # noqa: E731
+    rel = lambda a, b: float((a.double() - b.double()).norm() / b.double().norm())  # noqa: E731
     assert rel(y.detach(), y_ref.detach()) < tol
+    if prec == 0:  # parameter gradients: within 2x the float32 restatement's own error
+        y32, P32 = _reference(layer, x, dtype=torch.float32)
+        (y32 * gy).sum().backward()
     for n, p in layer.named_parameters():
         if P[n].grad is None or P[n].grad.norm() == 0:
             continue
-        assert rel(p.grad, P[n].grad) < tol, n
+        bound = max(tol, 2.0 * rel(P32[n].grad, P[n].grad)) if prec == 0 else tol
+        assert rel(p.grad, P[n].grad) < bound, (n, rel(p.grad, P[n].grad), bound)
     assert state.W1.shape == (2, H, D, 4 * D) and state.W2.shape == (2, H, 4 * D, D)
