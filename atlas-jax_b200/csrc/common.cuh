@@ -10,13 +10,17 @@
 namespace atlas {
 
 // Polar Express coefficients, atlas_jax/memory_layer.py:34-40.
-__constant__ double kPE[5][3] = {
-    {8.156554524902461, -22.48329292557795, 15.878769915207462},
-    {4.042929935166739, -2.808917465908714, 0.5000178451051316},
-    {3.8916678022926607, -2.772484153217685, 0.5060648178503393},
-    {3.285753657755655, -2.3681294933425376, 0.46449024233003106},
-    {2.3465413258596377, -1.7097828382687081, 0.42323551169305323},
-};
+#define ATLAS_PE_COEFFS                                        \
+  {                                                            \
+    {8.156554524902461, -22.48329292557795, 15.878769915207462},   \
+    {4.042929935166739, -2.808917465908714, 0.5000178451051316},   \
+    {3.8916678022926607, -2.772484153217685, 0.5060648178503393},  \
+    {3.285753657755655, -2.3681294933425376, 0.46449024233003106}, \
+    {2.3465413258596377, -1.7097828382687081, 0.42323551169305323} \
+  }
+__constant__ double kPE[5][3] = ATLAS_PE_COEFFS;
+// host copy (launch-time epilogue coefficients)
+constexpr double kPEHost[5][3] = ATLAS_PE_COEFFS;
 
 // Kernels whose bounded waits expire record ATLAS_ERR_DEVICE_TIMEOUT in the
 // library's device status word (passed to them as a pointer) and return

@@ -22,6 +22,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "pe_tma.h"
 #include "scan_internal.h"
 #include "tc_ops.cuh"
 
@@ -287,14 +288,91 @@ static cudaError_t gemm(const GemmArgs& g, int64_t batch, cudaStream_t s) {
 
 namespace tcpe {
 
+// Matrices with a short side >= 128 take the TMA path (pe_tma.cu): float32 X ping-pong
+// and A, plus split operands X (row-major and transposed, ping-pong), A and B.
 size_t workspace_bytes(int64_t batch, int rows, int cols) {
   const size_t D = std::min(rows, cols), DE = (size_t)rows * cols;
+  if (pet2::usable(rows, cols)) return (size_t)batch * ((6 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
   return (size_t)batch * (2 * DE + 2 * D * D) * sizeof(float);
+}
+
+// typical |entry| of a unit-Frobenius n-element matrix is n^-1/2: scale it to ~2
+static float operand_scale(double n, float cap) {
+  float sc = 256.f;
+  while (sc < cap && sc * sc < 4.0 * n) sc *= 2.f;
+  return sc;
+}
+
+// Polar Express on pre-split operands: per step A = X X^T (float32 A and split A),
+// B = c A A + b A (split B only), X' = B X + a X (float32 X' and its split, row-major
+// for the next Gram and transposed for the next B X).
+static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
+                              void* ws, cudaStream_t s) {
+  const int D = std::min(rows, cols), E = std::max(rows, cols);
+  const size_t DE = (size_t)D * E, DD = (size_t)D * D;
+  float* xf[2];
+  xf[0] = (float*)ws;
+  xf[1] = xf[0] + batch * DE;
+  float* Af = xf[1] + batch * DE;
+  __half* xs[2];
+  __half* xt[2];
+  xs[0] = (__half*)(Af + batch * DD);  // each split array is 2 x n halves = n floats of space
+  xs[1] = xs[0] + 2 * batch * DE;
+  xt[0] = xs[1] + 2 * batch * DE;
+  xt[1] = xt[0] + 2 * batch * DE;
+  __half* as = xt[1] + 2 * batch * DE;
+  __half* bs = as + 2 * batch * DD;
+  double* part = (double*)(bs + 2 * batch * DD);
+  const float sx = operand_scale((double)DE, 16384.f), sa = operand_scale((double)DD, 16384.f),
+              sbm = operand_scale((double)DD, 512.f);
+  cudaError_t e = pet2::normalize_split(X, xf[0], xs[0], xt[0], part, batch, rows, cols, eps, sx, s);
+  if (e != cudaSuccess) return e;
+  int* status = device_status_ptr();
+  int cur = 0;
+  for (int st = 0; st < steps; ++st) {
+    const float ca = (float)kPEHost[st][0], cb = (float)kPEHost[st][1], cc = (float)kPEHost[st][2];
+    const bool last = st + 1 == steps;
+    pet2::EpiArgs g{};
+    g.status = status;
+    // A = X X^T (D x D, K = E)
+    g.M = D; g.N = D; g.K = E;
+    g.alpha = 1.f / (sx * sx); g.beta = 0.f; g.so = sa;
+    g.Cf = Af; g.sC = DD; g.ldc = D; g.Cs = as;
+    if ((e = pet2::gemm(xs[cur], xs[cur], g, batch, s)) != cudaSuccess) return e;
+    // B = c A A + b A (A symmetric, so A itself is its K-major B operand)
+    g = pet2::EpiArgs{};
+    g.status = status;
+    g.M = D; g.N = D; g.K = D;
+    g.alpha = cc / (sa * sa); g.beta = cb; g.so = sbm;
+    g.Dm = Af; g.sD = DD; g.ldd = D; g.Cs = bs;
+    if ((e = pet2::gemm(as, as, g, batch, s)) != cudaSuccess) return e;
+    // X' = B X + a X (D x E, K = D; B symmetric; X's K-major B operand is X^T)
+    g = pet2::EpiArgs{};
+    g.status = status;
+    g.M = D; g.N = E; g.K = D;
+    g.alpha = 1.f / (sbm * sx); g.beta = ca; g.so = sx;
+    g.Dm = xf[cur]; g.sD = DE; g.ldd = E;
+    g.Cf = xf[cur ^ 1]; g.sC = DE; g.ldc = E;
+    g.Cs = last ? nullptr : xs[cur ^ 1];
+    g.Ct = last ? nullptr : xt[cur ^ 1];
+    if (last) {  // the last step writes the result in the caller's orientation
+      g.Cf = rows > cols ? nullptr : Y;
+      g.CfT = rows > cols ? Y : nullptr;
+    }
+    if ((e = pet2::gemm(bs, xt[cur], g, batch, s)) != cudaSuccess) return e;
+    cur ^= 1;
+  }
+  if (steps > 0) return cudaSuccess;
+  const size_t total = (size_t)batch * DE;
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
+  pet::unwide_kernel<<<blocks, 256, 0, s>>>(xf[cur], Y, batch, rows, cols);
+  return cudaGetLastError();
 }
 
 cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps, void* ws,
                    cudaStream_t s) {
   using pet::GemmArgs;
+  if (pet2::usable(rows, cols)) return launch_tma(X, Y, batch, rows, cols, steps, eps, ws, s);
   const int D = std::min(rows, cols), E = std::max(rows, cols);
   const size_t DE = (size_t)D * E, DD = (size_t)D * D;
   float* xa = (float*)ws;
@@ -308,12 +386,6 @@ cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, 
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int* status = device_status_ptr();
-  // typical |entry| of a unit-Frobenius n-element matrix is n^-1/2: scale it to ~2
-  auto operand_scale = [](double n, float cap) {
-    float sc = 256.f;
-    while (sc < cap && sc * sc < 4.0 * n) sc *= 2.f;
-    return sc;
-  };
   const float sx = operand_scale((double)DE, 16384.f), sa = operand_scale((double)DD, 16384.f),
               sbm = operand_scale((double)DD, 512.f);
   for (int st = 0; st < steps; ++st) {

@@ -1,0 +1,450 @@
+// TMA-fed tcgen05 GEMM for the batched Polar Express of large matrices (the Muon
+// stacks of atlas_jax/optim.py:56-108, iteration of memory_layer.py:43-71).
+//
+// Every operand is pre-split once, by the epilogue that produces it, into fp16 hi / lo
+// parts of a power-of-two multiple of its value, stored K-major as [batch][part][rows][K].
+// The main loop then moves no float32 data and does no conversion work: a TMA warp
+// loads both parts of a 128 x 64 A tile and a BN x 64 B tile per stage (one
+// cp.async.bulk.tensor each, 128-byte swizzle, no multicast), an MMA warp issues the
+// three split terms hi*hi + hi*lo + lo*hi as M=128 x N=BN x K=16 tcgen05 MMAs into a
+// float32 TMEM accumulator, and four epilogue warps turn the accumulator into
+// alpha * acc + beta * addend, written as float32 and / or as the next product's split
+// operand (row-major or transposed).  One CTA per output tile and batch entry; every
+// wait is bounded and records ATLAS_ERR_DEVICE_TIMEOUT instead of hanging.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "pe_tma.h"
+#include "tc_ops.cuh"
+
+namespace atlas {
+namespace pet2 {
+using namespace tcx;
+
+constexpr int BM = 128, TK = 64, NTH = 192;  // warps 0-3 epilogue, 4 TMA, 5 MMA
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 2 : 3;
+  static constexpr int A_BYTES = 2 * BM * TK * 2;  // hi + lo, 128 B per row
+  static constexpr int B_BYTES = 2 * BN * TK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(2 * BN <= 512, "two accumulators must fit TMEM");
+};
+
+// SM100 shared-memory descriptor of a K-major operand in the 128-byte swizzled
+// layout TMA writes: rows of 128 bytes (64 fp16 of K), 8-row atoms of 1024 bytes.
+// Stepping K by 16 inside the atom adds 32 bytes to the start address.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;              // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset: next 8-row atom
+  d |= (uint64_t)1 << 46;              // version
+  d |= (uint64_t)2 << 61;              // layout: SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load3(void* sdst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(sdst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Writes fp16 hi / lo parts of so * v for 8 consecutive values into a split array.
+__device__ __forceinline__ void split8_g(__half* hi, __half* lo, const float* v, float so) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float y0 = v[2 * k] * so, y1 = v[2 * k + 1] * so;
+    const __half2 hv = __floats2half2_rn(y0, y1);
+    const float2 hf = __half22float2(hv);
+    const __half2 lv = __floats2half2_rn(y0 - hf.x, y1 - hf.y);
+    h[k] = *reinterpret_cast<const uint32_t*>(&hv);
+    l[k] = *reinterpret_cast<const uint32_t*>(&lv);
+  }
+  *(uint4*)hi = make_uint4(h[0], h[1], h[2], h[3]);
+  *(uint4*)lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Persistent: each CTA walks output tiles (batch entry, n tile, m tile) with stride
+// gridDim.x.  Two TMEM accumulators (2 * BN columns) let the epilogue of one tile run
+// while the MMAs of the next accumulate.
+template <int BN>
+__global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CUtensorMap mapA,
+                                                        const __grid_constant__ CUtensorMap mapB, const EpiArgs g,
+                                                        int z0, int nz) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* bad = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+  const int nk = (g.K + TK - 1) / TK;
+  const int tiles_m = (g.M + BM - 1) / BM, tiles_n = (g.N + BN - 1) / BN;
+  const int ntiles = tiles_m * tiles_n * nz;
+  auto tile_coords = [&](int tile, int& m0, int& n0, int& z) {
+    m0 = (tile % tiles_m) * BM;
+    const int r = tile / tiles_m;
+    n0 = (r % tiles_n) * BN;
+    z = z0 + r / tiles_n;
+  };
+
+  if (w == 0) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  if (t == 32) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    *bad = 0;
+    fence_mbar_init();
+  }
+  if (t == 64) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&mapB) : "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tm = *tmem_slot;
+
+  if (w == 4) {  // TMA producer
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*bad; tile += gridDim.x) {
+        int m0, n0, z;
+        tile_coords(tile, m0, n0, z);
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % C::STAGES;
+          if (it >= C::STAGES && !mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1)) {
+            set_status(g.status, ATLAS_ERR_DEVICE_TIMEOUT);
+            *bad = 1;
+            break;
+          }
+          uint8_t* sa = base + s * C::STAGE_BYTES;
+          mbar_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
+          tma_load3(sa, &mapA, i * TK, m0, 2 * z, &full[s]);
+          tma_load3(sa + C::A_BYTES, &mapB, i * TK, n0, 2 * z, &full[s]);
+        }
+      }
+    }
+  } else if (w == 5) {  // MMA issuer (whole warp; one elected lane issues)
+    const uint32_t idesc = idesc_f16(BM, BN, false, false);
+    int it = 0, lt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++lt) {
+      const int a = lt & 1;
+      if (lt >= 2 && !mbar_wait(&acc_empty[a], ((lt >> 1) - 1) & 1)) ok = false;
+      fence_after();
+      const uint32_t acc = tm + (uint32_t)(a * BN);
+      for (int i = 0; i < nk && ok; ++i, ++it) {
+        const int s = it % C::STAGES;
+        if (!mbar_wait(&full[s], (it / C::STAGES) & 1)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t sa = smem_u32(base + s * C::STAGE_BYTES);
+        const uint32_t sb = sa + C::A_BYTES;
+        const uint64_t da[2] = {desc_sw128(sa), desc_sw128(sa + BM * 128)};
+        const uint64_t db[2] = {desc_sw128(sb), desc_sw128(sb + BN * 128)};
+        const int ta[3] = {0, 0, 1}, tb[3] = {0, 1, 0};  // hi*hi, hi*lo, lo*hi
+#pragma unroll
+        for (int term = 0; term < 3; ++term)
+#pragma unroll
+          for (int ks = 0; ks < TK / 16; ++ks)
+            mma_kf16(acc, da[ta[term]] + 2 * ks, db[tb[term]] + 2 * ks, idesc, (i || term || ks) ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(&acc_full[a]);
+    }
+    if (!ok && lane == 0) {
+      set_status(g.status, ATLAS_ERR_DEVICE_TIMEOUT);
+      *bad = 1;
+    }
+  } else {  // epilogue warps 0-3: TMEM lane quadrant w = rows m0 + 32w .. +31
+    const size_t MN = (size_t)g.M * g.N;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
+      int m0, n0, z;
+      tile_coords(tile, m0, n0, z);
+      const int a = lt & 1;
+      const bool ok = mbar_wait(&acc_full[a], (lt >> 1) & 1) && !*bad;
+      fence_after();
+      if (!ok) {
+        if (lane == 0) {
+          set_status(g.status, ATLAS_ERR_DEVICE_TIMEOUT);
+          *bad = 1;
+        }
+        break;
+      }
+      const int m = m0 + 32 * w + lane;
+      const bool mrow = m < g.M;
+      const size_t zz = (size_t)z;
+      const float* Dm = g.Dm ? g.Dm + zz * g.sD : nullptr;
+      float* Cf = g.Cf ? g.Cf + zz * g.sC : nullptr;
+      float* CfT = g.CfT ? g.CfT + zz * MN : nullptr;
+      __half* sh = g.Cs ? g.Cs + zz * 2 * MN : nullptr;
+      __half* th = g.Ct ? g.Ct + zz * 2 * MN : nullptr;
+      const uint32_t tacc = tm + (uint32_t)(a * BN) + ((uint32_t)(32 * w) << 16);
+#pragma unroll 1
+      for (int cb = 0; cb < BN / 32; ++cb) {
+        const int nb = n0 + 32 * cb;
+        if (nb >= g.N) break;  // warp-uniform
+        float v[32];
+        tmem_ld16(tacc + 32 * cb, v);
+        tmem_ld16(tacc + 32 * cb + 16, v + 16);
+        tmem_wait_ld();
+        if (!mrow) continue;
+        const bool full32 = nb + 32 <= g.N;
+        if (Dm) {
+          const float* dp = Dm + (size_t)m * g.ldd + nb;
+          if (full32 && (g.ldd & 3) == 0) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 d = *(const float4*)(dp + 4 * j4);
+              v[4 * j4 + 0] = fmaf(g.alpha, v[4 * j4 + 0], g.beta * d.x);
+              v[4 * j4 + 1] = fmaf(g.alpha, v[4 * j4 + 1], g.beta * d.y);
+              v[4 * j4 + 2] = fmaf(g.alpha, v[4 * j4 + 2], g.beta * d.z);
+              v[4 * j4 + 3] = fmaf(g.alpha, v[4 * j4 + 3], g.beta * d.w);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaf(g.alpha, v[j], nb + j < g.N ? g.beta * dp[j] : 0.f);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= g.alpha;
+        }
+        if (Cf) {
+          float* cp = Cf + (size_t)m * g.ldc + nb;
+          if (full32 && (g.ldc & 3) == 0) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4)
+              *(float4*)(cp + 4 * j4) = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < g.N) cp[j] = v[j];
+          }
+        }
+        if (CfT) {  // [N][M], column m: lanes write consecutive m
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < g.N) CfT[(size_t)(nb + j) * g.M + m] = v[j];
+        }
+        if (sh) {  // [part][M][N], row m
+          __half* hp = sh + (size_t)m * g.N + nb;
+          if (full32 && (g.N & 7) == 0) {
+#pragma unroll
+            for (int k8 = 0; k8 < 4; ++k8) split8_g(hp + 8 * k8, hp + MN + 8 * k8, v + 8 * k8, g.so);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < g.N) {
+                const float y = v[j] * g.so;
+                const __half h = __float2half_rn(y);
+                hp[j] = h;
+                hp[MN + j] = __float2half_rn(y - __half2float(h));
+              }
+          }
+        }
+        if (th) {  // [part][N][M], column m
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < g.N) {
+              const float y = v[j] * g.so;
+              const __half h = __float2half_rn(y);
+              const size_t o = (size_t)(nb + j) * g.M + m;
+              th[o] = h;
+              th[MN + o] = __float2half_rn(y - __half2float(h));
+            }
+        }
+      }
+      // accumulator a is free for the tile after next
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (w == 0) tmem_dealloc(tm, 2 * BN);
+}
+
+constexpr int NPART = 64;  // partial sums of squares per matrix
+
+__global__ void __launch_bounds__(256) sumsq_kernel(const float* S, double* part, size_t n, int vec) {
+  __shared__ double red[8];
+  const float* s = S + (size_t)blockIdx.y * n;
+  double acc = 0;
+  if (vec) {
+    for (size_t i = ((size_t)blockIdx.x * 256 + threadIdx.x) * 4; i < n; i += (size_t)gridDim.x * 1024) {
+      const float4 x = *(const float4*)(s + i);
+      acc += (double)x.x * x.x + (double)x.y * x.y + (double)x.z * x.z + (double)x.w * x.w;
+    }
+  } else {
+    for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (size_t)gridDim.x * 256)
+      acc += (double)s[i] * s[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    part[(size_t)blockIdx.y * NPART + blockIdx.x] = tot;
+  }
+}
+
+__device__ __forceinline__ void split1(__half* o, size_t lo_off, float y) {
+  const __half h = __float2half_rn(y);
+  o[0] = h;
+  o[lo_off] = __float2half_rn(y - __half2float(h));
+}
+
+// One 32 x 32 tile (wide rows d, columns e) per block, through shared memory so every
+// read and write is coalesced.
+__global__ void __launch_bounds__(256) norm_split_kernel(const float* S, float* Xf, __half* Xs, __half* Xt,
+                                                         const double* part, int D, int E, int tall, float eps,
+                                                         float sx) {
+  __shared__ float tile[32][33];
+  __shared__ float s_inv;
+  const size_t DE = (size_t)D * E;
+  const size_t z = blockIdx.z;
+  const float* s = S + z * DE;
+  if (threadIdx.x == 0) {
+    double tot = 0;
+    for (int i = 0; i < NPART; ++i) tot += part[z * NPART + i];
+    s_inv = (float)(1.0 / (sqrt(tot + (double)eps) * 1.01 + 1e-6));
+  }
+  const int e0 = blockIdx.x * 32, d0 = blockIdx.y * 32, tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (tall) {  // S is E x D
+      const int e = e0 + ty + 8 * k, d = d0 + tx;
+      tile[tx][ty + 8 * k] = (e < E && d < D) ? s[(size_t)e * D + d] : 0.f;
+    } else {  // S is D x E
+      const int d = d0 + ty + 8 * k, e = e0 + tx;
+      tile[ty + 8 * k][tx] = (e < E && d < D) ? s[(size_t)d * E + e] : 0.f;
+    }
+  }
+  __syncthreads();
+  const float inv = s_inv;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int d = d0 + ty + 8 * k, e = e0 + tx;
+    if (d < D && e < E) {
+      const float x = tile[ty + 8 * k][tx] * inv;
+      Xf[z * DE + (size_t)d * E + e] = x;
+      split1(Xs + z * 2 * DE + (size_t)d * E + e, DE, x * sx);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int e = e0 + ty + 8 * k, d = d0 + tx;
+    if (d < D && e < E) split1(Xt + z * 2 * DE + (size_t)e * D + d, DE, tile[tx][ty + 8 * k] * inv * sx);
+  }
+}
+
+cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, double* part, int64_t batch, int rows,
+                            int cols, float eps, float sx, cudaStream_t st) {
+  const int D = rows < cols ? rows : cols, E = rows < cols ? cols : rows;
+  const size_t DE = (size_t)D * E;
+  const int vec = (reinterpret_cast<uintptr_t>(S) & 15) == 0 && DE % 4 == 0;
+  for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
+    const int nz = (int)std::min<int64_t>(65535, batch - z0);
+    sumsq_kernel<<<dim3(NPART, nz), 256, 0, st>>>(S + z0 * DE, part + z0 * NPART, DE, vec);
+    norm_split_kernel<<<dim3((E + 31) / 32, (D + 31) / 32, nz), 256, 0, st>>>(
+        S + z0 * DE, Xf + z0 * DE, Xs + z0 * 2 * DE, Xt + z0 * 2 * DE, part + z0 * NPART, D, E, rows > cols, eps, sx);
+  }
+  return cudaGetLastError();
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map of a split operand [batch][part][rows][K] (fp16): box of 64 K x box_rows
+// rows x both parts, 128-byte swizzle, out-of-range elements read as zero.
+static bool make_map(CUtensorMap* map, const __half* base, int64_t batch, int rows, int K, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)(2 * batch)};
+  const cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)rows * K * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)TK, (cuuint32_t)box_rows, 2};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+static cudaError_t gemm_bn(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, As, batch, g.M, g.K, BM) || !make_map(&mb, Bs, batch, g.N, g.K, BN))
+    return cudaErrorInvalidValue;
+  const size_t smem = Cfg<BN>::SMEM;
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t per_z = (int64_t)((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+  const int64_t zmax = std::max<int64_t>(1, (int64_t)1 << 30) / per_z;  // tile index fits an int
+  for (int64_t z0 = 0; z0 < batch; z0 += zmax) {
+    const int nz = (int)std::min<int64_t>(zmax, batch - z0);
+    const int64_t tiles = per_z * nz;
+    const int grid = (int)std::min<int64_t>(tiles, sms);
+    gemm_kernel<BN><<<grid, NTH, smem, s>>>(ma, mb, g, (int)z0, nz);
+  }
+  return cudaGetLastError();
+}
+
+bool usable(int rows, int cols) {
+  const int D = std::min(rows, cols);
+  // K-major rows of the split arrays are TMA strides: a multiple of 16 bytes
+  return D >= 128 && D % 8 == 0 && std::max(rows, cols) % 8 == 0 && encode_fn() != nullptr;
+}
+
+cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s) {
+  return g.N >= 256 ? gemm_bn<256>(As, Bs, g, batch, s) : gemm_bn<128>(As, Bs, g, batch, s);
+}
+
+}  // namespace pet2
+}  // namespace atlas

@@ -1,0 +1,40 @@
+// TMA-fed tcgen05 GEMM over pre-split fp16 hi / lo operands (pe_tma.cu), used by the
+// batched Polar Express for matrices whose short side is >= 128.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace atlas {
+namespace pet2 {
+
+// C = alpha * sum_k A[m][k] B[n][k] + beta * Dm[m][n] for every batch entry, with A and B
+// given as split arrays [batch][hi, lo][rows][K] (K-major, rows M resp. N).  Outputs (each
+// may be null): Cf float32 (ldc, batch stride sC); Cs split [batch][part][M][N] and
+// Ct split [batch][part][N][M], both of so * C.
+struct EpiArgs {
+  int M, N, K;
+  float alpha, beta, so;
+  const float* Dm;
+  int64_t sD;
+  int ldd;
+  float* Cf;
+  int64_t sC;
+  int ldc;
+  __half* Cs;
+  __half* Ct;
+  float* CfT;  // float32 transposed [batch][N][M]
+  int* status;
+};
+
+bool usable(int rows, int cols);
+cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s);
+// Frobenius normalisation of the Polar Express input, X = S / (1.01 sqrt(sum S^2 + eps) + 1e-6),
+// S given as rows x cols (wide X = S, tall X = S^T, D x E): writes X as float32 (Xf) and
+// as splits of sx * X, row-major (Xs, D x E) and transposed (Xt, E x D).  part: batch * 64
+// doubles of scratch.
+cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, double* part, int64_t batch, int rows,
+                            int cols, float eps, float sx, cudaStream_t s);
+
+}  // namespace pet2
+}  // namespace atlas

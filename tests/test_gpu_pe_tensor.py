@@ -47,6 +47,9 @@ def _rel(a, b):
     ((1, 4096, 768), 5, 0.0),
     ((2, 256, 96), 2, 0.0),
     ((2, 256, 96), 0, 0.0),
+    ((2, 264, 200), 5, 0.0),
+    ((3, 136, 1000), 5, 1e-12),
+    ((4, 512, 128), 5, 0.0),
 ])
 def test_tensor_pe_matches_float64(shape, steps, eps):
     from atlas_b200 import polar_express, ATLAS_PREC_TENSOR, device_status
