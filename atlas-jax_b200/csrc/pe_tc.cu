@@ -288,11 +288,12 @@ static cudaError_t gemm(const GemmArgs& g, int64_t batch, cudaStream_t s) {
 
 namespace tcpe {
 
-// Matrices with a short side >= 128 take the TMA path (pe_tma.cu): float32 X ping-pong
-// and A, plus split operands X (row-major and transposed, ping-pong), A and B.
+// Matrices with a short side >= 128 take the TMA path (pe_tma.cu): float32 A, and
+// split operands X (row-major and transposed, ping-pong), A and B; float32 X only when
+// there are no Newton-Schulz steps.
 size_t workspace_bytes(int64_t batch, int rows, int cols) {
   const size_t D = std::min(rows, cols), DE = (size_t)rows * cols;
-  if (pet2::usable(rows, cols)) return (size_t)batch * ((6 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
+  if (pet2::usable(rows, cols)) return (size_t)batch * ((5 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
   return (size_t)batch * (2 * DE + 2 * D * D) * sizeof(float);
 }
 
@@ -304,19 +305,18 @@ static float operand_scale(double n, float cap) {
 }
 
 // Polar Express on pre-split operands: per step A = X X^T (float32 A and split A),
-// B = c A A + b A (split B only), X' = B X + a X (float32 X' and its split, row-major
-// for the next Gram and transposed for the next B X).
+// B = c A A + b A (split B only), X' = B X + a X (X' split row-major for the next Gram
+// and transposed for the next B X; a X read from the split of X).  The last step writes
+// the result in the caller's orientation.
 static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
                               void* ws, cudaStream_t s) {
   const int D = std::min(rows, cols), E = std::max(rows, cols);
   const size_t DE = (size_t)D * E, DD = (size_t)D * D;
-  float* xf[2];
-  xf[0] = (float*)ws;
-  xf[1] = xf[0] + batch * DE;
-  float* Af = xf[1] + batch * DE;
+  float* Af = (float*)ws;
+  float* xf = Af + batch * DD;  // steps == 0 only
   __half* xs[2];
   __half* xt[2];
-  xs[0] = (__half*)(Af + batch * DD);  // each split array is 2 x n halves = n floats of space
+  xs[0] = (__half*)(xf + batch * DE);  // each split array is 2 x n halves = n floats of space
   xs[1] = xs[0] + 2 * batch * DE;
   xt[0] = xs[1] + 2 * batch * DE;
   xt[1] = xt[0] + 2 * batch * DE;
@@ -325,7 +325,8 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
   double* part = (double*)(bs + 2 * batch * DD);
   const float sx = operand_scale((double)DE, 16384.f), sa = operand_scale((double)DD, 16384.f),
               sbm = operand_scale((double)DD, 512.f);
-  cudaError_t e = pet2::normalize_split(X, xf[0], xs[0], xt[0], part, batch, rows, cols, eps, sx, s);
+  cudaError_t e =
+      pet2::normalize_split(X, steps == 0 ? xf : nullptr, xs[0], xt[0], part, batch, rows, cols, eps, sx, s);
   if (e != cudaSuccess) return e;
   int* status = device_status_ptr();
   int cur = 0;
@@ -351,13 +352,14 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
     g.status = status;
     g.M = D; g.N = E; g.K = D;
     g.alpha = 1.f / (sbm * sx); g.beta = ca; g.so = sx;
-    g.Dm = xf[cur]; g.sD = DE; g.ldd = E;
-    g.Cf = xf[cur ^ 1]; g.sC = DE; g.ldc = E;
-    g.Cs = last ? nullptr : xs[cur ^ 1];
-    g.Ct = last ? nullptr : xt[cur ^ 1];
-    if (last) {  // the last step writes the result in the caller's orientation
+    g.Ds = xs[cur]; g.dscale_inv = 1.f / sx;
+    if (last) {  // the result, in the caller's orientation
       g.Cf = rows > cols ? nullptr : Y;
+      g.sC = DE; g.ldc = E;
       g.CfT = rows > cols ? Y : nullptr;
+    } else {
+      g.Cs = xs[cur ^ 1];
+      g.Ct = xt[cur ^ 1];
     }
     if ((e = pet2::gemm(bs, xt[cur], g, batch, s)) != cudaSuccess) return e;
     cur ^= 1;
@@ -365,7 +367,7 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
   if (steps > 0) return cudaSuccess;
   const size_t total = (size_t)batch * DE;
   const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
-  pet::unwide_kernel<<<blocks, 256, 0, s>>>(xf[cur], Y, batch, rows, cols);
+  pet::unwide_kernel<<<blocks, 256, 0, s>>>(xf, Y, batch, rows, cols);
   return cudaGetLastError();
 }
 

@@ -7,10 +7,12 @@
 // loads both parts of a 128 x 64 A tile and a BN x 64 B tile per stage (one
 // cp.async.bulk.tensor each, 128-byte swizzle, no multicast), an MMA warp issues the
 // three split terms hi*hi + hi*lo + lo*hi as M=128 x N=BN x K=16 tcgen05 MMAs into a
-// float32 TMEM accumulator, and four epilogue warps turn the accumulator into
-// alpha * acc + beta * addend, written as float32 and / or as the next product's split
-// operand (row-major or transposed).  One CTA per output tile and batch entry; every
-// wait is bounded and records ATLAS_ERR_DEVICE_TIMEOUT instead of hanging.
+// float32 TMEM accumulator, and eight epilogue warps (two per TMEM lane quadrant, one
+// column half each) turn the accumulator into alpha * acc + beta * addend, written as
+// float32 and / or as the next product's split operand (row-major or transposed).  The
+// kernel is persistent (one CTA per SM walking the output tiles) with two TMEM
+// accumulators, so one tile's epilogue overlaps the next tile's MMAs.  Every wait is
+// bounded and records ATLAS_ERR_DEVICE_TIMEOUT instead of hanging.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -26,7 +28,8 @@ namespace atlas {
 namespace pet2 {
 using namespace tcx;
 
-constexpr int BM = 128, TK = 64, NTH = 192;  // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int BM = 128, TK = 64, NTH = 320;  // warps 0-7 epilogue, 8 TMA, 9 MMA
+constexpr int NEPI = 8;
 
 template <int BN>
 struct Cfg {
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[a], NEPI);  // one arrival per epilogue warp
     }
     *bad = 0;
     fence_mbar_init();
@@ -132,7 +135,7 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
   fence_after();
   const uint32_t tm = *tmem_slot;
 
-  if (w == 4) {  // TMA producer
+  if (w == NEPI) {  // TMA producer
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*bad; tile += gridDim.x) {
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
         }
       }
     }
-  } else if (w == 5) {  // MMA issuer (whole warp; one elected lane issues)
+  } else if (w == NEPI + 1) {  // MMA issuer (whole warp; one elected lane issues)
     const uint32_t idesc = idesc_f16(BM, BN, false, false);
     int it = 0, lt = 0;
     bool ok = true;
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
       set_status(g.status, ATLAS_ERR_DEVICE_TIMEOUT);
       *bad = 1;
     }
-  } else {  // epilogue warps 0-3: TMEM lane quadrant w = rows m0 + 32w .. +31
+  } else {  // epilogue warps 0-7: TMEM lane quadrant w % 4 = rows m0 + 32 (w % 4) .. +31, column half w / 4
     const size_t MN = (size_t)g.M * g.N;
     int lt = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
@@ -202,7 +205,8 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
         }
         break;
       }
-      const int m = m0 + 32 * w + lane;
+      const int qd = w & 3, half = w >> 2;
+      const int m = m0 + 32 * qd + lane;
       const bool mrow = m < g.M;
       const size_t zz = (size_t)z;
       const float* Dm = g.Dm ? g.Dm + zz * g.sD : nullptr;
@@ -210,9 +214,9 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
       float* CfT = g.CfT ? g.CfT + zz * MN : nullptr;
       __half* sh = g.Cs ? g.Cs + zz * 2 * MN : nullptr;
       __half* th = g.Ct ? g.Ct + zz * 2 * MN : nullptr;
-      const uint32_t tacc = tm + (uint32_t)(a * BN) + ((uint32_t)(32 * w) << 16);
+      const uint32_t tacc = tm + (uint32_t)(a * BN) + ((uint32_t)(32 * qd) << 16);
 #pragma unroll 1
-      for (int cb = 0; cb < BN / 32; ++cb) {
+      for (int cb = half * (BN / 64); cb < (half + 1) * (BN / 64); ++cb) {
         const int nb = n0 + 32 * cb;
         if (nb >= g.N) break;  // warp-uniform
         float v[32];
@@ -235,6 +239,28 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = fmaf(g.alpha, v[j], nb + j < g.N ? g.beta * dp[j] : 0.f);
+          }
+        } else if (g.Ds) {
+          const __half* dh = g.Ds + zz * 2 * MN + (size_t)m * g.N + nb;
+          if (full32 && (g.N & 7) == 0) {
+#pragma unroll
+            for (int k8 = 0; k8 < 4; ++k8) {
+              const uint4 h4 = *(const uint4*)(dh + 8 * k8), l4 = *(const uint4*)(dh + MN + 8 * k8);
+              const uint32_t hw[4] = {h4.x, h4.y, h4.z, h4.w}, lw[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[q]));
+                const float2 lf = __half22float2(*reinterpret_cast<const __half2*>(&lw[q]));
+                const float bs = g.beta * g.dscale_inv;
+                v[8 * k8 + 2 * q] = fmaf(g.alpha, v[8 * k8 + 2 * q], bs * (hf.x + lf.x));
+                v[8 * k8 + 2 * q + 1] = fmaf(g.alpha, v[8 * k8 + 2 * q + 1], bs * (hf.y + lf.y));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] = fmaf(g.alpha, v[j],
+                          nb + j < g.N ? g.beta * g.dscale_inv * (__half2float(dh[j]) + __half2float(dh[MN + j])) : 0.f);
           }
         } else {
 #pragma unroll
@@ -362,7 +388,7 @@ __global__ void __launch_bounds__(256) norm_split_kernel(const float* S, float* 
     const int d = d0 + ty + 8 * k, e = e0 + tx;
     if (d < D && e < E) {
       const float x = tile[ty + 8 * k][tx] * inv;
-      Xf[z * DE + (size_t)d * E + e] = x;
+      if (Xf) Xf[z * DE + (size_t)d * E + e] = x;
       split1(Xs + z * 2 * DE + (size_t)d * E + e, DE, x * sx);
     }
   }
@@ -382,7 +408,7 @@ cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, d
     const int nz = (int)std::min<int64_t>(65535, batch - z0);
     sumsq_kernel<<<dim3(NPART, nz), 256, 0, st>>>(S + z0 * DE, part + z0 * NPART, DE, vec);
     norm_split_kernel<<<dim3((E + 31) / 32, (D + 31) / 32, nz), 256, 0, st>>>(
-        S + z0 * DE, Xf + z0 * DE, Xs + z0 * 2 * DE, Xt + z0 * 2 * DE, part + z0 * NPART, D, E, rows > cols, eps, sx);
+        S + z0 * DE, Xf ? Xf + z0 * DE : nullptr, Xs + z0 * 2 * DE, Xt + z0 * 2 * DE, part + z0 * NPART, D, E, rows > cols, eps, sx);
   }
   return cudaGetLastError();
 }

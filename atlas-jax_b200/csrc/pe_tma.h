@@ -18,6 +18,8 @@ struct EpiArgs {
   const float* Dm;
   int64_t sD;
   int ldd;
+  const __half* Ds;  // addend as a split [batch][part][M][N] of dscale * Dm (used when Dm is null)
+  float dscale_inv;
   float* Cf;
   int64_t sC;
   int ldc;
@@ -30,8 +32,8 @@ struct EpiArgs {
 bool usable(int rows, int cols);
 cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s);
 // Frobenius normalisation of the Polar Express input, X = S / (1.01 sqrt(sum S^2 + eps) + 1e-6),
-// S given as rows x cols (wide X = S, tall X = S^T, D x E): writes X as float32 (Xf) and
-// as splits of sx * X, row-major (Xs, D x E) and transposed (Xt, E x D).  part: batch * 64
+// S given as rows x cols (wide X = S, tall X = S^T, D x E): writes X as float32 (Xf, may be
+// null) and as splits of sx * X, row-major (Xs, D x E) and transposed (Xt, E x D).  part: batch * 64
 // doubles of scratch.
 cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, double* part, int64_t batch, int rows,
                             int cols, float eps, float sx, cudaStream_t s);
