@@ -289,11 +289,11 @@ static cudaError_t gemm(const GemmArgs& g, int64_t batch, cudaStream_t s) {
 namespace tcpe {
 
 // Matrices with a short side >= 128 take the TMA path (pe_tma.cu): float32 A, and
-// split operands X (row-major and transposed, ping-pong), A and B; float32 X only when
-// there are no Newton-Schulz steps.
+// split operands X (ping-pong), A and B; float32 X only when there are no
+// Newton-Schulz steps.
 size_t workspace_bytes(int64_t batch, int rows, int cols) {
   const size_t D = std::min(rows, cols), DE = (size_t)rows * cols;
-  if (pet2::usable(rows, cols)) return (size_t)batch * ((5 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
+  if (pet2::usable(rows, cols)) return (size_t)batch * ((3 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
   return (size_t)batch * (2 * DE + 2 * D * D) * sizeof(float);
 }
 
@@ -305,8 +305,8 @@ static float operand_scale(double n, float cap) {
 }
 
 // Polar Express on pre-split operands: per step A = X X^T (float32 A and split A),
-// B = c A A + b A (split B only), X' = B X + a X (X' split row-major for the next Gram
-// and transposed for the next B X; a X read from the split of X).  The last step writes
+// B = c A A + b A (split B only), X' = B X + a X (X' split, read K-major by the next Gram
+// and MN-major by the next B X; a X read from the split of X).  The last step writes
 // the result in the caller's orientation.
 static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
                               void* ws, cudaStream_t s) {
@@ -315,18 +315,15 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
   float* Af = (float*)ws;
   float* xf = Af + batch * DD;  // steps == 0 only
   __half* xs[2];
-  __half* xt[2];
   xs[0] = (__half*)(xf + batch * DE);  // each split array is 2 x n halves = n floats of space
   xs[1] = xs[0] + 2 * batch * DE;
-  xt[0] = xs[1] + 2 * batch * DE;
-  xt[1] = xt[0] + 2 * batch * DE;
-  __half* as = xt[1] + 2 * batch * DE;
+  __half* as = xs[1] + 2 * batch * DE;
   __half* bs = as + 2 * batch * DD;
   double* part = (double*)(bs + 2 * batch * DD);
   const float sx = operand_scale((double)DE, 16384.f), sa = operand_scale((double)DD, 16384.f),
               sbm = operand_scale((double)DD, 512.f);
   cudaError_t e =
-      pet2::normalize_split(X, steps == 0 ? xf : nullptr, xs[0], xt[0], part, batch, rows, cols, eps, sx, s);
+      pet2::normalize_split(X, steps == 0 ? xf : nullptr, xs[0], nullptr, part, batch, rows, cols, eps, sx, s);
   if (e != cudaSuccess) return e;
   int* status = device_status_ptr();
   int cur = 0;
@@ -347,7 +344,7 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
     g.alpha = cc / (sa * sa); g.beta = cb; g.so = sbm;
     g.Dm = Af; g.sD = DD; g.ldd = D; g.Cs = bs;
     if ((e = pet2::gemm(as, as, g, batch, s)) != cudaSuccess) return e;
-    // X' = B X + a X (D x E, K = D; B symmetric; X's K-major B operand is X^T)
+    // X' = B X + a X (D x E, K = D; B symmetric; X read MN-major as the B operand)
     g = pet2::EpiArgs{};
     g.status = status;
     g.M = D; g.N = E; g.K = D;
@@ -359,9 +356,8 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
       g.CfT = rows > cols ? Y : nullptr;
     } else {
       g.Cs = xs[cur ^ 1];
-      g.Ct = xt[cur ^ 1];
     }
-    if ((e = pet2::gemm(bs, xt[cur], g, batch, s)) != cudaSuccess) return e;
+    if ((e = pet2::gemm(bs, xs[cur], g, batch, s, true)) != cudaSuccess) return e;
     cur ^= 1;
   }
   if (steps > 0) return cudaSuccess;

@@ -54,6 +54,19 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// MN-major operand as TMA writes it for a (64 n x TK k x 2 parts) box per 64-column chunk:
+// each k row is 128 bytes of n, 8-row atoms of 1024 bytes; chunk j of a part at
+// j * 2 * TK * 128 bytes (leading byte offset), next 8 k rows at 1024 (stride byte offset).
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((2 * TK * 128) >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -85,7 +98,7 @@ __device__ __forceinline__ void split8_g(__half* hi, __half* lo, const float* v,
 // Persistent: each CTA walks output tiles (batch entry, n tile, m tile) with stride
 // gridDim.x.  Two TMEM accumulators (2 * BN columns) let the epilogue of one tile run
 // while the MMAs of the next accumulate.
-template <int BN>
+template <int BN, bool BMN>
 __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CUtensorMap mapA,
                                                         const __grid_constant__ CUtensorMap mapB, const EpiArgs g,
                                                         int z0, int nz) {
@@ -151,12 +164,18 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
           uint8_t* sa = base + s * C::STAGE_BYTES;
           mbar_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
           tma_load3(sa, &mapA, i * TK, m0, 2 * z, &full[s]);
-          tma_load3(sa + C::A_BYTES, &mapB, i * TK, n0, 2 * z, &full[s]);
+          if (BMN) {  // 64-column chunks [j][part][k][64 n]
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load3(sa + C::A_BYTES + j * (2 * TK * 128), &mapB, n0 + 64 * j, i * TK, 2 * z, &full[s]);
+          } else {
+            tma_load3(sa + C::A_BYTES, &mapB, i * TK, n0, 2 * z, &full[s]);
+          }
         }
       }
     }
   } else if (w == NEPI + 1) {  // MMA issuer (whole warp; one elected lane issues)
-    const uint32_t idesc = idesc_f16(BM, BN, false, false);
+    const uint32_t idesc = idesc_f16(BM, BN, false, BMN);
     int it = 0, lt = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++lt) {
@@ -174,13 +193,15 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
         const uint32_t sa = smem_u32(base + s * C::STAGE_BYTES);
         const uint32_t sb = sa + C::A_BYTES;
         const uint64_t da[2] = {desc_sw128(sa), desc_sw128(sa + BM * 128)};
-        const uint64_t db[2] = {desc_sw128(sb), desc_sw128(sb + BN * 128)};
+        const uint64_t db[2] = {BMN ? desc_sw128_mn(sb) : desc_sw128(sb),
+                                BMN ? desc_sw128_mn(sb + TK * 128) : desc_sw128(sb + BN * 128)};
+        constexpr uint64_t bstep = BMN ? (16 * 128) >> 4 : 2;  // K = 16: 16 rows (MN-major) or 32 bytes
         const int ta[3] = {0, 0, 1}, tb[3] = {0, 1, 0};  // hi*hi, hi*lo, lo*hi
 #pragma unroll
         for (int term = 0; term < 3; ++term)
 #pragma unroll
           for (int ks = 0; ks < TK / 16; ++ks)
-            mma_kf16(acc, da[ta[term]] + 2 * ks, db[tb[term]] + 2 * ks, idesc, (i || term || ks) ? 1u : 0u);
+            mma_kf16(acc, da[ta[term]] + 2 * ks, db[tb[term]] + bstep * ks, idesc, (i || term || ks) ? 1u : 0u);
         mma_commit(&empty[s]);
       }
       mma_commit(&acc_full[a]);
@@ -395,7 +416,7 @@ __global__ void __launch_bounds__(256) norm_split_kernel(const float* S, float* 
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int e = e0 + ty + 8 * k, d = d0 + tx;
-    if (d < D && e < E) split1(Xt + z * 2 * DE + (size_t)e * D + d, DE, tile[tx][ty + 8 * k] * inv * sx);
+    if (Xt && d < D && e < E) split1(Xt + z * 2 * DE + (size_t)e * D + d, DE, tile[tx][ty + 8 * k] * inv * sx);
   }
 }
 
@@ -408,7 +429,7 @@ cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, d
     const int nz = (int)std::min<int64_t>(65535, batch - z0);
     sumsq_kernel<<<dim3(NPART, nz), 256, 0, st>>>(S + z0 * DE, part + z0 * NPART, DE, vec);
     norm_split_kernel<<<dim3((E + 31) / 32, (D + 31) / 32, nz), 256, 0, st>>>(
-        S + z0 * DE, Xf ? Xf + z0 * DE : nullptr, Xs + z0 * 2 * DE, Xt + z0 * 2 * DE, part + z0 * NPART, D, E, rows > cols, eps, sx);
+        S + z0 * DE, Xf ? Xf + z0 * DE : nullptr, Xs + z0 * 2 * DE, Xt ? Xt + z0 * 2 * DE : nullptr, part + z0 * NPART, D, E, rows > cols, eps, sx);
   }
   return cudaGetLastError();
 }
@@ -440,13 +461,29 @@ static bool make_map(CUtensorMap* map, const __half* base, int64_t batch, int ro
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
+// Tensor map of a split operand stored [batch][part][K][cols] (MN-major use): box of
+// 64 columns x TK K rows x both parts.
+static bool make_map_mn(CUtensorMap* map, const __half* base, int64_t batch, int cols, int K) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)K, (cuuint64_t)(2 * batch)};
+  const cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)cols * K * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)TK, 2};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, bool BMN>
 static cudaError_t gemm_bn(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s) {
   CUtensorMap ma, mb;
-  if (!make_map(&ma, As, batch, g.M, g.K, BM) || !make_map(&mb, Bs, batch, g.N, g.K, BN))
+  if (!make_map(&ma, As, batch, g.M, g.K, BM) ||
+      !(BMN ? make_map_mn(&mb, Bs, batch, g.N, g.K) : make_map(&mb, Bs, batch, g.N, g.K, BN)))
     return cudaErrorInvalidValue;
   const size_t smem = Cfg<BN>::SMEM;
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e =
+      cudaFuncSetAttribute(gemm_kernel<BN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -457,7 +494,7 @@ static cudaError_t gemm_bn(const __half* As, const __half* Bs, const EpiArgs& g,
     const int nz = (int)std::min<int64_t>(zmax, batch - z0);
     const int64_t tiles = per_z * nz;
     const int grid = (int)std::min<int64_t>(tiles, sms);
-    gemm_kernel<BN><<<grid, NTH, smem, s>>>(ma, mb, g, (int)z0, nz);
+    gemm_kernel<BN, BMN><<<grid, NTH, smem, s>>>(ma, mb, g, (int)z0, nz);
   }
   return cudaGetLastError();
 }
@@ -468,8 +505,9 @@ bool usable(int rows, int cols) {
   return D >= 128 && D % 8 == 0 && std::max(rows, cols) % 8 == 0 && encode_fn() != nullptr;
 }
 
-cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s) {
-  return g.N >= 256 ? gemm_bn<256>(As, Bs, g, batch, s) : gemm_bn<128>(As, Bs, g, batch, s);
+cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s, bool b_mn) {
+  if (b_mn) return g.N >= 256 ? gemm_bn<256, true>(As, Bs, g, batch, s) : gemm_bn<128, true>(As, Bs, g, batch, s);
+  return g.N >= 256 ? gemm_bn<256, false>(As, Bs, g, batch, s) : gemm_bn<128, false>(As, Bs, g, batch, s);
 }
 
 }  // namespace pet2

@@ -9,7 +9,8 @@ namespace atlas {
 namespace pet2 {
 
 // C = alpha * sum_k A[m][k] B[n][k] + beta * Dm[m][n] for every batch entry, with A and B
-// given as split arrays [batch][hi, lo][rows][K] (K-major, rows M resp. N).  Outputs (each
+// given as split arrays [batch][hi, lo][rows][K] (K-major, rows M resp. N; B may also be
+// MN-major, see gemm()).  Outputs (each
 // may be null): Cf float32 (ldc, batch stride sC); Cs split [batch][part][M][N] and
 // Ct split [batch][part][N][M], both of so * C.
 struct EpiArgs {
@@ -30,10 +31,12 @@ struct EpiArgs {
 };
 
 bool usable(int rows, int cols);
-cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s);
+// b_mn: B given as a split array [batch][part][K][N] (MN-major) instead of [batch][part][N][K]
+cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s,
+                 bool b_mn = false);
 // Frobenius normalisation of the Polar Express input, X = S / (1.01 sqrt(sum S^2 + eps) + 1e-6),
 // S given as rows x cols (wide X = S, tall X = S^T, D x E): writes X as float32 (Xf, may be
-// null) and as splits of sx * X, row-major (Xs, D x E) and transposed (Xt, E x D).  part: batch * 64
+// null) and as splits of sx * X, row-major (Xs, D x E) and transposed (Xt, E x D; may be null).  part: batch * 64
 // doubles of scratch.
 cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, double* part, int64_t batch, int rows,
                             int cols, float eps, float sx, cudaStream_t s);
