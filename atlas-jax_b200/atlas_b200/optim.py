@@ -64,3 +64,18 @@ def muon_leaf_update(grad, state, param, learning_rate, momentum=0.95, beta2=0.9
     else:
         update = -learning_rate * lr_scale * g
     return update, MuonState(new_m, new_sm)
+
+
+if __name__ == "__main__":
+    # Profiling case: a seeded float32 stack (default 12 x 768 x 2048, or "NxRxC" as the
+    # first argument), five-step tensor-path Polar Express twice
+    # (python -m atlas_b200.optim from atlas-jax_b200/).
+    import sys
+    shape = tuple(int(x) for x in (sys.argv[1] if len(sys.argv) > 1 else "12x768x2048").split("x"))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    X = torch.randn(*shape, device="cuda", generator=gen)
+    for _ in range(2):
+        muon_polar_express(X, 5)
+    torch.cuda.synchronize()
+    print("ok")

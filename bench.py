@@ -196,8 +196,9 @@ def next_rows(dev, stream, peak_tf, hbm):
     """Device-timed figures for the rows beyond the headline scan (rank 0, one GPU):
     the MAG sliding-window attention at config 3's shape (B=2, T=32768, 12 heads x 64,
     window 1024) forward+backward, and the fused layer prologue forward+backward at
-    the 170M layer shape (B=8, T=8192, C=768).  3 untimed + 5 timed passes each;
-    every input is larger than L2."""
+    the 170M layer shape (B=8, T=8192, C=768), the Muon Polar Express of the 12 x 4096 x 768
+    stack, and config 4's head_dim-128 forward scan (B x H = 96, a 2048-token sample).
+    3 untimed + 5 (2 for the scan) timed passes each; every input is larger than L2."""
     import torch
     from atlas_b200.swa import swa_backward, swa_forward
     from atlas_b200.layer_io import LayerGeometry, prologue_backward, prologue_forward
@@ -244,6 +245,30 @@ def next_rows(dev, stream, peak_tf, hbm):
     out["layer_prologue"] = {"workload": f"prologue B={B} T={T} H={H} D={D} (bf16)", "fwd_ms": pf, "bwd_ms": pb,
                              "fwd_gbs": fbytes / pf / 1e6, "bwd_gbs": bbytes / pb / 1e6,
                              "frac_hbm_fwd": fbytes / pf / 1e6 / hbm, "unit": "GB/s (algorithmic bytes)"}
+    del proj, qo, ko, vo, gates
+    # Muon orthogonalisation of the 170M model's largest stack (optim.py:68-83)
+    from atlas_b200 import ATLAS_PREC_TENSOR, ScanConfig, polar_express, scan_forward
+    nb, rows, cols, ns = 12, 4096, 768, 5
+    X = torch.randn(nb, rows, cols, device=dev, generator=g)
+    pe_ms = timed(lambda: polar_express(X, ns, 0.0, precision=ATLAS_PREC_TENSOR))
+    Dm, Em = min(rows, cols), max(rows, cols)
+    pe_fl = nb * ns * (4 * Dm * Dm * Em + 2 * Dm ** 3)
+    out["muon_pe"] = {"workload": f"Polar Express {ns} steps of {nb} x {rows} x {cols} float32",
+                      "ms": pe_ms, "tflops": pe_fl / pe_ms / 1e9, "frac": pe_fl / pe_ms / 1e9 / peak_tf,
+                      "unit": "TFLOP/s (algorithmic)", "kernels": "pe_tma gemm_kernel, sumsq, norm_split"}
+    del X
+    # config 4's head_dim-128 sweep point (B x H = 96), forward only, a 2048-token sample
+    B, T, H, D, E = 8, 2048, 12, 128, 512
+    nrm = lambda x: x / x.norm(dim=-1, keepdim=True)  # noqa: E731
+    q, k, v = (nrm(torch.randn(B, T, H, D, device=dev, generator=g)).to(torch.bfloat16) for _ in range(3))
+    gate = lambda m: torch.sigmoid(m + 0.5 * torch.randn(B, T, H, device=dev, generator=g))  # noqa: E731
+    ga, ge, gt = gate(3.0), gate(-3.0), gate(1.0)
+    cfg = ScanConfig(chunk=64, omega=16, ns_steps=5, precision=ATLAS_PREC_TENSOR)
+    c4 = timed(lambda: scan_forward(q, k, v, ga, ge, gt, None, None, cfg, need_saved=False), n=2)
+    c4_fl = B * T * H * 2 * ns * (4 * D * D * E + 2 * D ** 3)  # Polar Express of W1 and W2 per token-head
+    out["config4_d128"] = {"workload": f"forward scan B={B} H={H} T={T} (sample) D={D} E={E} chunk=64 bf16",
+                           "ms": c4, "tokens_per_s": B * T / c4 * 1e3, "pe_tflops": c4_fl / c4 / 1e9,
+                           "unit": "tokens/s", "kernels": "scan_gen frozen/momentum/memory kernels + pe_tma GEMMs"}
     return out
 
 

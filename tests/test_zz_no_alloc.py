@@ -60,9 +60,14 @@ def test_noalloc_forward_matches_regular_forward_twice():
         torch.cuda.synchronize()
         device_status()
         assert rel(to_np(y_n), to_np(y_r)) < TOL
-        for x_n, x_r in zip(out_n, out_r):
-            assert to_np(x_r).any()  # every final state is non-zero on these inputs
-            assert rel(to_np(x_n), to_np(x_r)) < TOL
+        for i, (x_n, x_r) in enumerate(zip(out_n, out_r)):
+            r, n = to_np(x_r), to_np(x_n)
+            if i < 2:  # W1, W2 are non-zero on these inputs
+                assert r.any()
+            if r.any():
+                assert rel(n, r) < TOL
+            else:  # the momentum leaves the padded last chunk at zero (theta = 0 on padding)
+                assert not n.any()
 
 
 def test_noalloc_rejects_too_many_chains():
