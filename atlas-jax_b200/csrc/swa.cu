@@ -380,14 +380,19 @@ __global__ void delta_kernel(Args a) {
 }
 
 struct KVSmem {
-  uint8_t K[TILE], V[TILE], Q[2][TILE], dO[2][TILE], Pt[PTILE], dSt[PTILE];
-  float lse2[2][BR], delta[2][BR];
-  uint64_t bar;
+  uint8_t K[TILE], V[TILE], Q[3][TILE], dO[3][TILE], Pt[PTILE], dSt[PTILE];
+  float lse2[3][BR], delta[3][BR];
+  uint64_t bar;   // S^T / dP^T group
+  uint64_t barv;  // dV / dK group
   uint32_t tmem;
   volatile int bad;
 };
 
-// dK, dV of one block of 128 keys over the query blocks that see it
+// dK, dV of one block of 128 keys over the query blocks that see it.  Software
+// pipelined over the query blocks (three Q / dO buffers): once the threads hold query
+// block qb's S^T and dP^T in registers, the MMAs of block qb + 1's S^T and dP^T are
+// issued into the same TMEM columns, so they run while the threads form P^T and dS^T
+// of block qb; block qb's dV / dK MMAs follow them on the tensor pipe.
 __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
   extern __shared__ uint8_t raw[];
   KVSmem& s = *(KVSmem*)align128(raw);
@@ -395,6 +400,10 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
   const int T = P.T, H = P.H, W = P.window, tid = threadIdx.x;
   const int b = blockIdx.y / H, h = blockIdx.y % H, k0 = blockIdx.x * BR;
   const Roles u = setup(s, 512);
+  if (tid == 0) {
+    mbar_init(&s.barv, 1);
+    fence_mbar_init();
+  }
   const int kr = k0 + u.rloc, ch = u.ch;
   const int qb0 = k0 / BR, qb1 = min(T - 1, k0 + BR - 1 + W) / BR;
   const size_t bh = (size_t)b * H + h;
@@ -407,60 +416,78 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
       s.delta[buf][tid] = t < T ? a.delta[bh * T + t] : 0.f;
     }
   };
+  auto issue_sdp = [&](int buf) {
+    if (u.w == 0) {
+      mma_tiles(u.tm, s.K, HD, s.Q[buf], HD, false, BR, HD, false);         // S^T = K Q^T
+      mma_tiles(u.tm + 128, s.V, HD, s.dO[buf], HD, false, BR, HD, false);  // dP^T = V dO^T
+      mma_commit(&s.bar);
+    }
+    __syncwarp();
+  };
   load_tile_async(s.K, a.kr, b, h, k0, T, H);
   load_tile_async(s.V, a.v, b, h, k0, T, H);
   stage(qb0, 0);
   cp_async_commit();
+  if (qb0 + 1 <= qb1) stage(qb0 + 1, 1);
+  cp_async_commit();
+  cp_async_wait<1>();  // K, V and block qb0's tiles
+  fence_async_smem();
+  cta_sync();
+  issue_sdp(0);
   const float sl2 = rsqrtf((float)HD) * LOG2E;
-  uint32_t phase = 0;
+  uint32_t phase = 0, phase_v = 0;
   bool done = true;
   for (int qb = qb0; qb <= qb1; ++qb) {
-    const int q0 = qb * BR, cur = (qb - qb0) & 1;
+    const int q0 = qb * BR, cur = (qb - qb0) % 3;
     const bool full = k0 + BR - 1 <= q0 && q0 + BR - 1 - k0 <= W && q0 + BR <= T;  // no mask needed
-    tiles_ready();
-    if (u.w == 0) {
-      mma_tiles(u.tm, s.K, HD, s.Q[cur], HD, false, BR, HD, false);         // S^T = K Q^T
-      mma_tiles(u.tm + 128, s.V, HD, s.dO[cur], HD, false, BR, HD, false);  // dP^T = V dO^T
-      mma_commit(&s.bar);
-    }
-    if (qb < qb1) stage(qb + 1, cur ^ 1);
-    cp_async_commit();
-    __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {  // S^T, dP^T of block qb
       done = false;
       break;
     }
+    float sv[64], dp[64];
 #pragma unroll
     for (int c = 0; c < 64; c += 16) {
-      const int cc = 64 * ch + c;
-      float sv[16], dp[16];
-      tmem_ld16(u.tm + u.lane + cc, sv);
-      tmem_ld16(u.tm + u.lane + 128 + cc, dp);
-      tmem_wait_ld();
+      tmem_ld16(u.tm + u.lane + 64 * ch + c, sv + c);
+      tmem_ld16(u.tm + u.lane + 128 + 64 * ch + c, dp + c);
+    }
+    tmem_wait_ld();
+    // dV / dK of block qb - 1 read Q / dO buffer (qb + 2) % 3 and Pt / dSt
+    if (qb > qb0 && !wait_mma(&s.barv, phase_v, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
+    if (qb + 2 <= qb1) stage(qb + 2, (qb + 2 - qb0) % 3);
+    cp_async_commit();
+    if (qb < qb1) {
+      cp_async_wait<1>();  // block qb + 1's tiles (the newest group is block qb + 2)
+      fence_async_smem();
+      cta_sync();          // also: every thread's S^T / dP^T loads of block qb are done
+      issue_sdp((qb + 1 - qb0) % 3);
+    }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int qq = q0 + cc + j;
-        const bool ok = full || (kr <= qq && qq - kr <= W && qq < T && kr < T);
-        const float pr = ok ? ex2(fmaf(sv[j], sl2, -s.lse2[cur][cc + j])) : 0.f;
-        sv[j] = pr;
-        dp[j] = pr * (dp[j] - s.delta[cur][cc + j]);
-      }
-      store16(s.Pt, u.rloc, cc, sv);
-      store16(s.dSt, u.rloc, cc, dp);
+    for (int j = 0; j < 64; ++j) {
+      const int cc = 64 * ch + j;
+      const int qq = q0 + cc;
+      const bool ok = full || (kr <= qq && qq - kr <= W && qq < T && kr < T);
+      const float pr = ok ? ex2(fmaf(sv[j], sl2, -s.lse2[cur][cc])) : 0.f;
+      sv[j] = pr;
+      dp[j] = pr * (dp[j] - s.delta[cur][cc]);
+    }
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
+      store16(s.Pt, u.rloc, 64 * ch + c, sv + c);
+      store16(s.dSt, u.rloc, 64 * ch + c, dp + c);
     }
     fence_async_smem();
     cta_sync();
     if (u.w == 0) {
       mma_tiles(u.tm + 256, s.Pt, BR, s.dO[cur], HD, true, HD, BR, qb > qb0);  // dV += P^T dO
       mma_tiles(u.tm + 320, s.dSt, BR, s.Q[cur], HD, true, HD, BR, qb > qb0);  // dK += dS^T Q
-      mma_commit(&s.bar);
+      mma_commit(&s.barv);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
-      done = false;
-      break;
-    }
   }
+  if (done && !wait_mma(&s.barv, phase_v, &s.bad, a.status)) done = false;
   cp_async_wait<0>();
   if (done) {
     float v[32];
@@ -479,81 +506,102 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
 }
 
 struct QSmem {
-  uint8_t Q[TILE], dO[TILE], K[2][TILE], V[2][TILE], dS[PTILE];
-  uint64_t bar;
+  uint8_t Q[TILE], dO[TILE], K[3][TILE], V[3][TILE], dS[PTILE];
+  uint64_t bar;   // S / dP group
+  uint64_t barq;  // dQ group
   uint32_t tmem;
   volatile int bad;
 };
 
-// dQ of one block of 128 queries over its band of key blocks
+// dQ of one block of 128 queries over its band of key blocks, software pipelined
+// like dkv_kernel (three K / V buffers; key block kb + 1's S and dP MMAs run while the
+// threads form dS of block kb).
 __global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
   extern __shared__ uint8_t raw[];
   QSmem& s = *(QSmem*)align128(raw);
   const AtlasSwaParams& P = a.p;
-  const int T = P.T, H = P.H, W = P.window;
+  const int T = P.T, H = P.H, W = P.window, tid = threadIdx.x;
   const int b = blockIdx.y / H, h = blockIdx.y % H, q0 = blockIdx.x * BR;
   const Roles u = setup(s, 512);
+  if (tid == 0) {
+    mbar_init(&s.barq, 1);
+    fence_mbar_init();
+  }
   const int row = q0 + u.rloc, ch = u.ch;
   const size_t bh = (size_t)b * H + h;
   const float lse2 = row < T ? a.lse[bh * T + row] * LOG2E : 0.f;
   const float dl = row < T ? a.delta[bh * T + row] : 0.f;
   const int kb0 = max(0, q0 - W) / BR, kb1 = min(T - 1, q0 + BR - 1) / BR;
-  load_tile_async(s.Q, a.qr, b, h, q0, T, H);
-  load_tile_async(s.dO, a.dout, b, h, q0, T, H);
-  load_tile_async(s.K[0], a.kr, b, h, kb0 * BR, T, H);
-  load_tile_async(s.V[0], a.v, b, h, kb0 * BR, T, H);
-  cp_async_commit();
-  const float sl2 = rsqrtf((float)HD) * LOG2E;
-  uint32_t phase = 0;
-  bool done = true;
-  for (int kb = kb0; kb <= kb1; ++kb) {
-    const int k0 = kb * BR, cur = (kb - kb0) & 1;
-    const bool full = k0 + BR - 1 <= q0 && q0 + BR - 1 - k0 <= W && q0 + BR <= T;  // no mask needed
-    tiles_ready();
+  auto stage = [&](int kb, int buf) {
+    load_tile_async(s.K[buf], a.kr, b, h, kb * BR, T, H);
+    load_tile_async(s.V[buf], a.v, b, h, kb * BR, T, H);
+  };
+  auto issue_sdp = [&](int buf) {
     if (u.w == 0) {
-      mma_tiles(u.tm, s.Q, HD, s.K[cur], HD, false, BR, HD, false);         // S = Q K^T
-      mma_tiles(u.tm + 128, s.dO, HD, s.V[cur], HD, false, BR, HD, false);  // dP = dO V^T
+      mma_tiles(u.tm, s.Q, HD, s.K[buf], HD, false, BR, HD, false);         // S = Q K^T
+      mma_tiles(u.tm + 128, s.dO, HD, s.V[buf], HD, false, BR, HD, false);  // dP = dO V^T
       mma_commit(&s.bar);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
+  };
+  load_tile_async(s.Q, a.qr, b, h, q0, T, H);
+  load_tile_async(s.dO, a.dout, b, h, q0, T, H);
+  stage(kb0, 0);
+  cp_async_commit();
+  if (kb0 + 1 <= kb1) stage(kb0 + 1, 1);
+  cp_async_commit();
+  cp_async_wait<1>();
+  fence_async_smem();
+  cta_sync();
+  issue_sdp(0);
+  const float sl2 = rsqrtf((float)HD) * LOG2E;
+  uint32_t phase = 0, phase_q = 0;
+  bool done = true;
+  for (int kb = kb0; kb <= kb1; ++kb) {
+    const int k0 = kb * BR, cur = (kb - kb0) % 3;
+    const bool full = k0 + BR - 1 <= q0 && q0 + BR - 1 - k0 <= W && q0 + BR <= T;  // no mask needed
+    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {  // S, dP of block kb
       done = false;
       break;
     }
-    // K[cur ^ 1] and V[cur ^ 1] were last read by the previous block's MMAs (complete)
-    if (kb < kb1) {
-      load_tile_async(s.K[cur ^ 1], a.kr, b, h, k0 + BR, T, H);
-      load_tile_async(s.V[cur ^ 1], a.v, b, h, k0 + BR, T, H);
-    }
-    cp_async_commit();
+    float sv[64], dp[64];
 #pragma unroll
     for (int c = 0; c < 64; c += 16) {
-      const int cc = 64 * ch + c;
-      float sv[16], dp[16];
-      tmem_ld16(u.tm + u.lane + cc, sv);
-      tmem_ld16(u.tm + u.lane + 128 + cc, dp);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int key = k0 + cc + j;
-        const bool ok = full || (key <= row && row - key <= W && key < T && row < T);
-        const float pr = ok ? ex2(fmaf(sv[j], sl2, -lse2)) : 0.f;
-        dp[j] = pr * (dp[j] - dl);
-      }
-      store16(s.dS, u.rloc, cc, dp);
+      tmem_ld16(u.tm + u.lane + 64 * ch + c, sv + c);
+      tmem_ld16(u.tm + u.lane + 128 + 64 * ch + c, dp + c);
     }
+    tmem_wait_ld();
+    // dQ of block kb - 1 read K buffer (kb + 2) % 3 and dS
+    if (kb > kb0 && !wait_mma(&s.barq, phase_q, &s.bad, a.status)) {
+      done = false;
+      break;
+    }
+    if (kb + 2 <= kb1) stage(kb + 2, (kb + 2 - kb0) % 3);
+    cp_async_commit();
+    if (kb < kb1) {
+      cp_async_wait<1>();
+      fence_async_smem();
+      cta_sync();  // also: every thread's S / dP loads of block kb are done
+      issue_sdp((kb + 1 - kb0) % 3);
+    }
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const int key = k0 + 64 * ch + j;
+      const bool ok = full || (key <= row && row - key <= W && key < T && row < T);
+      const float pr = ok ? ex2(fmaf(sv[j], sl2, -lse2)) : 0.f;
+      dp[j] = pr * (dp[j] - dl);
+    }
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) store16(s.dS, u.rloc, 64 * ch + c, dp + c);
     fence_async_smem();
     cta_sync();
     if (u.w == 0) {
       mma_tiles(u.tm + 256, s.dS, BR, s.K[cur], HD, true, HD, BR, kb > kb0);  // dQ += dS K
-      mma_commit(&s.bar);
+      mma_commit(&s.barq);
     }
     __syncwarp();
-    if (!wait_mma(&s.bar, phase, &s.bad, a.status)) {
-      done = false;
-      break;
-    }
   }
+  if (done && !wait_mma(&s.barq, phase_q, &s.bad, a.status)) done = false;
   cp_async_wait<0>();
   if (done) {
     float v[32];

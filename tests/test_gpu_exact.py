@@ -102,3 +102,29 @@ def test_exact_polar_express(shape):
     # optim.py:68-83 (Muon) has no 1e-12 inside the square root
     Y0 = to_np(polar_express(to_dev(X), 5, 0.0))
     assert rel(Y0, Y) < 1e-6
+
+
+@pytest.mark.parametrize("chunk", [16, 128])
+def test_exact_head_dim_128_forward_and_backward(chunk):
+    """Config 4's head_dim: D=128, E=512 (1 MB of float32 state per chain), forward and
+    backward on the float64 path, chunk 16 (several chunks) and 128 (one padded chunk)."""
+    from atlas_b200 import scan_backward
+    T, D, E, B, H, w = 40, 128, 512, 1, 1, 8
+    ins = O.make_inputs(B, T, H, D, seed=11, gamma_mode="random")
+    st = O.make_xavier_state(B, H, D, E, seed=12)
+    st = (st[0], st[1], 0.1 * st[0], 0.1 * st[1])
+    cfg = _cfg(chunk=chunk, omega=w)
+    y, out, saved = _run(ins, st, cfg)
+    y_o, fin = O.scan_forward(*ins, st, chunk, w, 5, dtype=np.float64)
+    assert rel(y, y_o) < 1e-6
+    for a, b in zip(out, fin):
+        assert rel(a, b) < 1e-6 or np.abs(b).max() == 0
+    rng = np.random.default_rng(13)
+    dy = rng.standard_normal(y.shape).astype(np.float32)
+    q, k, v, a, e, t, g = ins
+    res = scan_backward(to_dev(q), to_dev(k), to_dev(v), to_dev(a), to_dev(e), to_dev(t), to_dev(g), saved,
+                        to_dev(dy), None, cfg, E)
+    torch.cuda.synchronize()
+    grads, _ = O.scan_backward(*ins, st, dy, None, chunk, w, 5)
+    for name, val in zip(("q", "k", "v", "alpha", "eta", "theta", "gamma"), res[:7]):
+        assert rel(to_np(val), grads[name]) < 1e-6, name
