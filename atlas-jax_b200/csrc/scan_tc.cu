@@ -4,8 +4,8 @@
 //   A (b, h) pair is a "chain" of chunks that must run in order.  A 2-CTA
 //   cluster processes one (chain, chunk) item at a time: CTA rank 0 owns the
 //   memory matrix W1 (and its momentum S1), rank 1 owns W2 / S2.  Items are
-//   dealt to a persistent grid of clusters in chunk-major order
-//   (item k -> chain k % NC, chunk k / NC), so a chain migrates between
+//   taken by a persistent grid of clusters from a ticket counter in chunk-major
+//   order (ticket k -> chain k % NC, chunk k / NC), so a chain migrates between
 //   clusters from chunk to chunk and every SM stays busy even when the number
 //   of chains is not a multiple of the number of clusters.  The carry between
 //   chunks goes through global memory (it is the `saved` buffer the backward
@@ -64,6 +64,7 @@ struct __align__(1024) Smem {
   uint64_t ready[2];  // ready[s]: slot s operand tiles published by the 8 epilogue warps
   uint32_t tmem;
   int bad;
+  int item;  // current work item (next_item)
 };
 
 __device__ __forceinline__ PESlot make_slot(Smem& s, int j, uint32_t tmem) {
@@ -174,6 +175,7 @@ struct KArgs {
   int nchains, nch;
   float* carries;  // used when a.saved == nullptr: one slot per chain
   int* flags;      // chunks completed per chain (zeroed before launch)
+  int* ticket;     // next work item (zeroed before launch)
   WaitHooks hooks;
   float* fscr;     // per cluster, per rank: the chunk's row factors (MAXCS x E)
 };
@@ -193,7 +195,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   const int qd = w & 3, ch = w >> 2;
   const int e0 = 32 * qd + l, e1 = e0 + 128, dc = 32 * ch;
   const uint32_t rank = cluster_rank();
-  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int cluster = blockIdx.x >> 1;  // indexes this cluster's scratch
   const int cs = P.chunk, T = P.T, H = P.H, nch = K.nch;
   const float sc = 2.0f / D;
   const bool win = P.omega > 1;
@@ -231,7 +233,9 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   // 2 * 128 * 240 + 128 * 24 = 64512.
   if (w >= 8) {  // ---- producer warpgroup: warp 8 issues every MMA; all four mirror the cluster barriers ----
     asm volatile("setmaxnreg.dec.sync.aligned.u32 24;");
-    for (long k = cluster; k < total; k += nclusters) {
+    for (;;) {
+      const long k = next_item(K.ticket, &s.item);
+      if (k >= total) break;
       cluster_sync();
       cluster_sync();
       for (int r0 = 0; r0 < cs; r0 += npair) {
@@ -244,7 +248,9 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   } else {  // ---- 8 epilogue warps ----
   asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
   float Sv[2][32], Wv[2][32];
-  for (long k = cluster; k < total; k += nclusters) {
+  for (;;) {
+    const long k = next_item(K.ticket, &s.item);
+    if (k >= total) break;
     const int q = (int)(k % K.nchains), c = (int)(k / K.nchains);
     const int b = q / H, hh = q % H;
     PROF_T(titem)
@@ -453,7 +459,8 @@ bool supported(const AtlasScanParams& p, const char** why) {
 size_t saved_bytes(const AtlasScanParams& p) { return (size_t)p.B * p.H * n_chunks(p) * 4 * DE * sizeof(float); }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-static size_t flags_bytes(const AtlasScanParams& p) { return align256((size_t)p.B * p.H * sizeof(int)); }
+// per-chain completion counters, then the item ticket
+static size_t flags_bytes(const AtlasScanParams& p) { return align256(((size_t)p.B * p.H + 1) * sizeof(int)); }
 static size_t fwd_clusters(const AtlasScanParams& p) {
   return std::min((size_t)p.B * p.H, (size_t)max_clusters_bound());
 }
@@ -502,6 +509,7 @@ cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
   k.hooks = wait_hooks();
   uint8_t* ws = (uint8_t*)a.ws;
   k.flags = (int*)ws;
+  k.ticket = k.flags + k.nchains;
   k.carries = (float*)(ws + flags_bytes(a.p));
   k.fscr = k.carries + (size_t)k.nchains * 4 * DE;
   cudaError_t e = cudaMemsetAsync(k.flags, 0, flags_bytes(a.p), st);

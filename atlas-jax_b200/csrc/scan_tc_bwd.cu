@@ -3,8 +3,8 @@
 // from JAX autodiff of the per-chunk jax.checkpoint'ed lax.scan, 675 / 711).
 //
 // Work decomposition mirrors the forward: a 2-CTA cluster (rank 0: W1/S1,
-// rank 1: W2/S2) processes one (chain, chunk) item at a time, items dealt in
-// reverse chunk order to a persistent grid; the cotangent of the carry flows
+// rank 1: W2/S2) processes one (chain, chunk) item at a time, items taken in
+// reverse chunk order from a ticket counter by a persistent grid; the cotangent of the carry flows
 // from chunk c+1 to chunk c through a per-chain global slot ordered by a
 // released counter.
 //
@@ -72,6 +72,7 @@ struct __align__(1024) Smem {
   uint64_t ready[2];     // operand tiles of slot s published by the 8 epilogue warps
   uint32_t tmem;
   int bad;
+  int item;  // current work item (next_item)
 };
 // P in float32 for the transpose (and the chunk's k / derr in phases A and D)
 // lives in the Sym tiles' 16 KB, free at those times.  16-byte chunks of a row
@@ -118,6 +119,7 @@ struct KArgs {
   BwdArgs a;
   int nchains, nch;
   int* flags;        // chunks finished per chain, counted from the end
+  int* ticket;       // next work item (zeroed before launch)
   WaitHooks hooks;
   float* cot;        // per chain: carry cotangent [m][W, S][E x D]
   float* cws;        // per cluster scratch
@@ -408,7 +410,7 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   const int e0 = 32 * qd + l, e1 = e0 + 128, dc = 32 * ch;
   const int rr = 16 * qd + (l & 15), d0 = dc + (l & 16);  // stack_finish row / columns of this lane
   const uint32_t rank = cluster_rank();
-  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int cluster = blockIdx.x >> 1;  // indexes this cluster's scratch
   const int cs = P.chunk, T = P.T, H = P.H, nch = K.nch;
   const float sc = 2.0f / D;
   const bool win = P.omega > 1;
@@ -462,7 +464,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
   // 2 * 128 * 240 + 128 * 24 = 64512.
   if (wp >= 8) {  // ---- producer warpgroup: warp 8 issues every MMA; all four mirror the cluster barriers ----
     asm volatile("setmaxnreg.dec.sync.aligned.u32 24;");
-    for (long kk = cluster; kk < total; kk += nclusters) {
+    for (;;) {
+      const long kk = next_item(K.ticket, &s.item);
+      if (kk >= total) break;
       cluster_sync();  // frozen pass (rank 0 done)
       cluster_sync();  // frozen pass (rank 1 done)
       for (int r0 = 0; r0 < cs; r0 += npair) {
@@ -482,7 +486,9 @@ __global__ void __launch_bounds__(NT + 128, 1) bwd_kernel(KArgs K) {
     }
   } else {  // ---- 8 epilogue warps ----
   asm volatile("setmaxnreg.inc.sync.aligned.u32 240;");
-  for (long kk = cluster; kk < total; kk += nclusters) {
+  for (;;) {
+    const long kk = next_item(K.ticket, &s.item);
+    if (kk >= total) break;
     const int q = (int)(kk % K.nchains), j = (int)(kk / K.nchains), c = nch - 1 - j;
     const int b = q / H, hh = q % H;
     PROF_T(titem)
@@ -1261,7 +1267,7 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 size_t bwd_workspace_bytes(const AtlasScanParams& p) {
   const size_t nc = (size_t)p.B * p.H;
   const size_t ncl = std::min(nc, (size_t)max_clusters_bound());
-  return align256(nc * sizeof(int)) + nc * 4 * DE * sizeof(float) + ncl * bwd::CLUSTER_FLOATS * sizeof(float);
+  return align256((nc + 1) * sizeof(int)) + nc * 4 * DE * sizeof(float) + ncl * bwd::CLUSTER_FLOATS * sizeof(float);
 }
 
 static DeviceCache g_bwd_max_clusters;  // resident 2-CTA clusters, per device
@@ -1300,10 +1306,11 @@ cudaError_t launch_bwd(const BwdArgs& a, cudaStream_t st) {
   k.nch = n_chunks(a.p);
   k.hooks = wait_hooks();
   uint8_t* ws = (uint8_t*)a.ws;
-  k.flags = (int*)ws;
-  k.cot = (float*)(ws + align256((size_t)k.nchains * sizeof(int)));
+  k.flags = (int*)ws;  // per-chain counters, then the item ticket
+  k.ticket = k.flags + k.nchains;
+  k.cot = (float*)(ws + align256(((size_t)k.nchains + 1) * sizeof(int)));
   k.cws = k.cot + (size_t)k.nchains * 4 * DE;
-  cudaError_t e = cudaMemsetAsync(k.flags, 0, (size_t)k.nchains * sizeof(int), st);
+  cudaError_t e = cudaMemsetAsync(k.flags, 0, ((size_t)k.nchains + 1) * sizeof(int), st);
   if (e != cudaSuccess) return e;
   const int ncl = std::min(k.nchains, max_clusters_bound());
   return a.p.act_dtype == ATLAS_BF16 ? launch_bwd_t<__nv_bfloat16>(k, ncl, st) : launch_bwd_t<float>(k, ncl, st);

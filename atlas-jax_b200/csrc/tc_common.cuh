@@ -45,6 +45,24 @@ __device__ __forceinline__ void st_remote_f32(const float* local_addr, uint32_t 
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
+// Dynamic work distribution of the persistent scan kernels: thread 0 of cluster rank 0
+// takes the next item ticket and publishes it to both CTAs' `slot`; every thread of the
+// cluster reads it after the cluster barrier.  Items are numbered so that an item's
+// predecessor (the same chain's neighbouring chunk) has a smaller ticket, so it was taken
+// by a cluster that is already running: a cluster that starts late, or never, cannot
+// hold up the others.  The slot is rewritten only at the next call, after the item's
+// own cluster barriers.
+__device__ __forceinline__ long next_item(int* ticket, int* slot) {
+  if (threadIdx.x == 0 && cluster_rank() == 0) {
+    const int t = atomicAdd(ticket, 1);
+    *slot = t;
+    uint32_t la = smem_u32(slot), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(1));
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(ra), "r"(t) : "memory");
+  }
+  cluster_sync();
+  return *(volatile int*)slot;
+}
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -33,13 +33,12 @@
  *    status word per GPU, shared by every stream and thread on that GPU: a
  *    bounded wait that expires in any call sets it, and atlas_scan_status()
  *    reads and clears it for everyone.
- *  - The tensor-path kernels are persistent: clusters of one launch wait on each
- *    other's chunks, so every cluster of the grid must be resident at once.  The
- *    grid is sized to the device's resident-cluster capacity; kernels of other
- *    work running concurrently on the same GPU can keep clusters from starting,
- *    in which case the waits expire (ATLAS_ERR_DEVICE_TIMEOUT in the status
- *    word) instead of hanging.  Run the scan without concurrent kernels on its
- *    GPU.
+ *  - The tensor-path kernels are persistent: a cluster that finishes a (chain,
+ *    chunk) item takes the next one from a ticket counter, and waits until the
+ *    chain's neighbouring chunk is done.  That chunk always holds a smaller ticket,
+ *    taken by a cluster that is already running, so the scan makes progress with
+ *    any number of resident clusters: kernels running concurrently on the same GPU
+ *    only slow it down.
  */
 #ifndef ATLAS_SCAN_H_
 #define ATLAS_SCAN_H_

@@ -49,12 +49,14 @@ def test_noalloc_forward_matches_regular_forward_twice():
         if call == 1:  # second call also passes an explicit initial state
             s0 = O.make_xavier_state(B, H, D, E, seed=seed)
             st = [to_dev(x) for x in (s0[0], s0[1], 0.05 * s0[0], 0.05 * s0[1])]
+        if call == 1:  # same call once first, so that lazily loaded kernels are resident
+            _noalloc(lib, L, p, ins, st)
         torch.cuda.synchronize()
         free0 = torch.cuda.mem_get_info()[0]
         y_n, out_n = _noalloc(lib, L, p, ins, st)
         torch.cuda.synchronize()
         free1 = torch.cuda.mem_get_info()[0]
-        if call == 1:  # kernels are loaded by now: the call itself must not take device memory
+        if call == 1:  # the call itself must not take device memory
             assert free1 == free0, (free0, free1)
         y_r, out_r, _ = scan_forward(*ins, st, cfg, need_saved=False)
         torch.cuda.synchronize()
