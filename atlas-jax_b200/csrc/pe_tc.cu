@@ -294,6 +294,8 @@ namespace tcpe {
 size_t workspace_bytes(int64_t batch, int rows, int cols) {
   const size_t D = std::min(rows, cols), DE = (size_t)rows * cols;
   if (pet2::usable(rows, cols)) return (size_t)batch * ((3 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
+  if (pet2::usable_packed(rows, cols))
+    return (size_t)batch * ((3 * DE + 2 * D * D + D * 128) * sizeof(float) + 64 * sizeof(double));
   return (size_t)batch * (2 * DE + 2 * D * D) * sizeof(float);
 }
 
@@ -367,10 +369,73 @@ static cudaError_t launch_tma(const float* X, float* Y, int64_t batch, int rows,
   return cudaGetLastError();
 }
 
+// D = 64: the same three products with two matrices per 128-row tile (pe_tma.cu's packed
+// mode): the Gram and A A keep the block diagonal of a 128 x 128 product, and
+// B' = a I + b A + c A A times X runs as one K = 128 product of the block-diagonal
+// [B'_z 0; 0 B'_z+1] with the stacked X's (the a X term rides in B', as in the fused scan).
+static cudaError_t launch_packed(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
+                                 void* ws, cudaStream_t s) {
+  const int D = std::min(rows, cols), E = std::max(rows, cols);
+  const size_t DE = (size_t)D * E, DD = (size_t)D * D;
+  float* Af = (float*)ws;
+  float* xf = Af + batch * DD;  // steps == 0 only
+  __half* xs[2];
+  xs[0] = (__half*)(xf + batch * DE);
+  xs[1] = xs[0] + 2 * batch * DE;
+  __half* as = xs[1] + 2 * batch * DE;
+  __half* bpad = as + 2 * batch * DD;
+  double* part = (double*)(bpad + 2 * batch * D * 128);
+  const float sx = operand_scale((double)DE, 16384.f), sa = operand_scale((double)DD, 16384.f),
+              sbm = operand_scale((double)DD, 512.f);
+  cudaError_t e = pet2::normalize_split(X, steps == 0 ? xf : nullptr, xs[0], nullptr, part, batch, rows, cols, eps,
+                                        sx, s, true);
+  if (e != cudaSuccess) return e;
+  int* status = device_status_ptr();
+  int cur = 0;
+  for (int st = 0; st < steps; ++st) {
+    const float ca = (float)kPEHost[st][0], cb = (float)kPEHost[st][1], cc = (float)kPEHost[st][2];
+    const bool last = st + 1 == steps;
+    pet2::EpiArgs g{};
+    g.status = status;
+    g.pack = 128 / D;
+    g.diag = 1;
+    g.M = D; g.N = D; g.K = E;  // A = X X^T
+    g.alpha = 1.f / (sx * sx); g.beta = 0.f; g.so = sa;
+    g.Cf = Af; g.Cs = as;
+    if ((e = pet2::gemm(xs[cur], xs[cur], g, batch, s)) != cudaSuccess) return e;
+    g.Cf = nullptr; g.Cs = nullptr;
+    g.K = D;  // B = c A A + b A, block-diagonal padded
+    g.alpha = cc / (sa * sa); g.beta = cb; g.so = sbm;
+    g.Dm = Af; g.Cpad = bpad;
+    g.diag_add = ca;  // B' = a I + b A + c A A, so X' = B' X needs no addend
+    if ((e = pet2::gemm(as, as, g, batch, s)) != cudaSuccess) return e;
+    g = pet2::EpiArgs{};
+    g.status = status;
+    g.pack = 128 / D;
+    g.diag = 0;
+    g.M = D; g.N = E; g.K = 128;  // X' = B' X
+    g.alpha = 1.f / (sbm * sx); g.so = sx;
+    if (last) {
+      g.Cf = rows > cols ? nullptr : Y;
+      g.CfT = rows > cols ? Y : nullptr;
+    } else {
+      g.Cs = xs[cur ^ 1];
+    }
+    if ((e = pet2::gemm(bpad, xs[cur], g, batch, s, true)) != cudaSuccess) return e;
+    cur ^= 1;
+  }
+  if (steps > 0) return cudaSuccess;
+  const size_t total = (size_t)batch * DE;
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
+  pet::unwide_kernel<<<blocks, 256, 0, s>>>(xf, Y, batch, rows, cols);
+  return cudaGetLastError();
+}
+
 cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps, void* ws,
                    cudaStream_t s) {
   using pet::GemmArgs;
   if (pet2::usable(rows, cols)) return launch_tma(X, Y, batch, rows, cols, steps, eps, ws, s);
+  if (pet2::usable_packed(rows, cols)) return launch_packed(X, Y, batch, rows, cols, steps, eps, ws, s);
   const int D = std::min(rows, cols), E = std::max(rows, cols);
   const size_t DE = (size_t)D * E, DD = (size_t)D * D;
   float* xa = (float*)ws;

@@ -95,6 +95,140 @@ __device__ __forceinline__ void split8_g(__half* hi, __half* lo, const float* v,
   *(uint4*)lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+__device__ __forceinline__ void split_pair(float y, __half* hi, __half* lo) {
+  const __half h = __float2half_rn(y);
+  *hi = h;
+  *lo = __float2half_rn(y - __half2float(h));
+}
+
+// Epilogue of the packed mode for the TMEM row of packed row R (batch entry R / D,
+// row R % D).  Diagonal products (g.diag): only the row's own D x D block (columns
+// D (R % 128 / D) ..) is kept: alpha acc + beta Dm as float32 [z][D][D] (Cf), as a packed
+// split [part][batch D][D] (Cs), and / or as a packed split of row length 128 with
+// the block at columns D (z % P) and zeros elsewhere (Cpad: the block-diagonal A operand
+// of the row product).  Row product: alpha acc + beta (split addend Ds) over N = E
+// columns, written as the packed split (Cs), or as float32 rows (Cf, wide) / columns
+// (CfT, tall) of the caller's matrices.
+template <int BN>
+__device__ __forceinline__ void packed_epilogue(const EpiArgs& g, uint32_t tacc, int R, int n0, int half,
+                                                int batch) {
+  const int D = g.M, P = g.pack;
+  const int z = R / D, r = R % D;
+  const bool live = z < batch;
+  const size_t rows = (size_t)batch * D;
+  if (g.diag) {
+    const int blk = (R % BM) / D;  // this row's diagonal block within the tile
+    // column chunks of 32 that hold the block (D >= 32: uniform across the warp)
+#pragma unroll 1
+    for (int cb = 0; cb < BN / 32; ++cb) {
+      if (cb / 2 != half) continue;  // column half of this warp
+      const int c0 = 32 * cb;
+      if (c0 < blk * D || c0 >= blk * D + D) continue;  // warp-uniform (32 rows share blk)
+      float v[32];
+      tmem_ld16(tacc + c0, v);
+      tmem_ld16(tacc + c0 + 16, v + 16);
+      tmem_wait_ld();
+      if (!live) continue;
+      const int cc = c0 - blk * D;  // column within the D x D block
+      const size_t o = (size_t)z * D * D + (size_t)r * D + cc;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        v[j] = fmaf(g.alpha, v[j], g.Dm ? g.beta * g.Dm[o + j] : 0.f) + (r == cc + j ? g.diag_add : 0.f);
+      if (g.Cf) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          *(float4*)(g.Cf + o + 4 * j4) = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+      }
+      if (g.Cs) {
+        __half* hp = g.Cs + (size_t)R * D + cc;
+#pragma unroll
+        for (int k8 = 0; k8 < 4; ++k8) split8_g(hp + 8 * k8, hp + rows * D + 8 * k8, v + 8 * k8, g.so);
+      }
+      if (g.Cpad) {
+        __half* hp = g.Cpad + (size_t)R * BM;
+        const size_t lo = rows * BM;
+#pragma unroll
+        for (int k8 = 0; k8 < 4; ++k8) split8_g(hp + (z % P) * D + cc + 8 * k8, hp + lo + (z % P) * D + cc + 8 * k8,
+                                               v + 8 * k8, g.so);
+        if (cc == 0) {  // zeros outside the block (this thread's row)
+          const uint4 zero = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < BM; c += 8)
+            if (c < (z % P) * D || c >= (z % P) * D + D) {
+              *(uint4*)(hp + c) = zero;
+              *(uint4*)(hp + lo + c) = zero;
+            }
+        }
+      }
+    }
+    return;
+  }
+  const int E = g.N;
+#pragma unroll 1
+  for (int cb = half * (BN / 64); cb < (half + 1) * (BN / 64); ++cb) {
+    const int nb = n0 + 32 * cb;
+    if (nb >= E) break;  // warp-uniform
+    float v[32];
+    tmem_ld16(tacc + 32 * cb, v);
+    tmem_ld16(tacc + 32 * cb + 16, v + 16);
+    tmem_wait_ld();
+    if (!live) continue;
+    const bool full32 = nb + 32 <= E;
+    const size_t o = (size_t)R * E + nb;
+    if (g.Ds) {
+      const float bs = g.beta * g.dscale_inv;
+      if (full32 && (E & 7) == 0) {
+#pragma unroll
+        for (int k8 = 0; k8 < 4; ++k8) {
+          const uint4 h4 = *(const uint4*)(g.Ds + o + 8 * k8), l4 = *(const uint4*)(g.Ds + rows * E + o + 8 * k8);
+          const uint32_t hw[4] = {h4.x, h4.y, h4.z, h4.w}, lw[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[q]));
+            const float2 lf = __half22float2(*reinterpret_cast<const __half2*>(&lw[q]));
+            v[8 * k8 + 2 * q] = fmaf(g.alpha, v[8 * k8 + 2 * q], bs * (hf.x + lf.x));
+            v[8 * k8 + 2 * q + 1] = fmaf(g.alpha, v[8 * k8 + 2 * q + 1], bs * (hf.y + lf.y));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          v[j] = fmaf(g.alpha, v[j],
+                      nb + j < E ? bs * (__half2float(g.Ds[o + j]) + __half2float(g.Ds[rows * E + o + j])) : 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= g.alpha;
+    }
+    if (g.Cs) {
+      __half* hp = g.Cs + o;
+      if (full32 && (E & 7) == 0) {
+#pragma unroll
+        for (int k8 = 0; k8 < 4; ++k8) split8_g(hp + 8 * k8, hp + rows * E + 8 * k8, v + 8 * k8, g.so);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (nb + j < E) split_pair(v[j] * g.so, hp + j, hp + rows * E + j);
+      }
+    }
+    if (g.Cf) {
+      if (full32 && (E & 3) == 0) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          *(float4*)(g.Cf + o + 4 * j4) = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (nb + j < E) g.Cf[o + j] = v[j];
+      }
+    }
+    if (g.CfT) {  // tall caller matrices: Y[z] is E x D
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (nb + j < E) g.CfT[(size_t)z * D * E + (size_t)(nb + j) * D + r] = v[j];
+    }
+  }
+}
+
 // Persistent: each CTA walks output tiles (batch entry, n tile, m tile) with stride
 // gridDim.x.  Two TMEM accumulators (2 * BN columns) let the epilogue of one tile run
 // while the MMAs of the next accumulate.
@@ -114,13 +248,30 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
 
   const int t = threadIdx.x, w = t >> 5, lane = t & 31;
   const int nk = (g.K + TK - 1) / TK;
-  const int tiles_m = (g.M + BM - 1) / BM, tiles_n = (g.N + BN - 1) / BN;
-  const int ntiles = tiles_m * tiles_n * nz;
-  auto tile_coords = [&](int tile, int& m0, int& n0, int& z) {
+  // Packed mode (g.pack = P matrices of D = 128 / P rows per 128-row tile): tile t of
+  // the diagonal products covers matrices [tP, tP + P) on both operands; tile (t, n) of
+  // the row product reads A rows [128 t, 128 t + 128) and B's K rows from the same offset.
+  const int tiles_m = g.pack ? (nz + g.pack - 1) / g.pack : (g.M + BM - 1) / BM;
+  const int tiles_n = g.pack && g.diag ? 1 : (g.N + BN - 1) / BN;
+  const int ntiles = g.pack ? tiles_m * tiles_n : tiles_m * tiles_n * nz;
+  // m0: A row coordinate; n0: B row (K-major) or column (MN-major) coordinate; kb: B's
+  // K coordinate base (MN-major); c2: third coordinate of both maps; z: batch entry
+  auto tile_coords = [&](int tile, int& m0, int& n0, int& z, int& kb, int& c2) {
+    if (g.pack) {
+      const int tm_ = tile % tiles_m;
+      m0 = BM * tm_;
+      n0 = g.diag ? m0 : (tile / tiles_m) * BN;
+      kb = g.diag ? 0 : m0;
+      c2 = 0;
+      z = tm_ * g.pack;
+      return;
+    }
     m0 = (tile % tiles_m) * BM;
     const int r = tile / tiles_m;
     n0 = (r % tiles_n) * BN;
     z = z0 + r / tiles_n;
+    kb = 0;
+    c2 = 2 * z;
   };
 
   if (w == 0) {
@@ -152,8 +303,8 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*bad; tile += gridDim.x) {
-        int m0, n0, z;
-        tile_coords(tile, m0, n0, z);
+        int m0, n0, z, kb, c2;
+        tile_coords(tile, m0, n0, z, kb, c2);
         for (int i = 0; i < nk; ++i, ++it) {
           const int s = it % C::STAGES;
           if (it >= C::STAGES && !mbar_wait(&empty[s], ((it / C::STAGES) - 1) & 1)) {
@@ -163,13 +314,13 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
           }
           uint8_t* sa = base + s * C::STAGE_BYTES;
           mbar_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
-          tma_load3(sa, &mapA, i * TK, m0, 2 * z, &full[s]);
+          tma_load3(sa, &mapA, i * TK, m0, c2, &full[s]);
           if (BMN) {  // 64-column chunks [j][part][k][64 n]
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load3(sa + C::A_BYTES + j * (2 * TK * 128), &mapB, n0 + 64 * j, i * TK, 2 * z, &full[s]);
+              tma_load3(sa + C::A_BYTES + j * (2 * TK * 128), &mapB, n0 + 64 * j, kb + i * TK, c2, &full[s]);
           } else {
-            tma_load3(sa + C::A_BYTES, &mapB, i * TK, n0, 2 * z, &full[s]);
+            tma_load3(sa + C::A_BYTES, &mapB, i * TK, n0, c2, &full[s]);
           }
         }
       }
@@ -214,8 +365,8 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
     const size_t MN = (size_t)g.M * g.N;
     int lt = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
-      int m0, n0, z;
-      tile_coords(tile, m0, n0, z);
+      int m0, n0, z, kb, c2;
+      tile_coords(tile, m0, n0, z, kb, c2);
       const int a = lt & 1;
       const bool ok = mbar_wait(&acc_full[a], (lt >> 1) & 1) && !*bad;
       fence_after();
@@ -227,6 +378,14 @@ __global__ void __launch_bounds__(NTH, 1) gemm_kernel(const __grid_constant__ CU
         break;
       }
       const int qd = w & 3, half = w >> 2;
+      if (g.pack) {
+        packed_epilogue<BN>(g, tm + (uint32_t)(a * BN) + ((uint32_t)(32 * qd) << 16), m0 + 32 * qd + lane, n0,
+                            half, nz);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[a]);
+        continue;
+      }
       const int m = m0 + 32 * qd + lane;
       const bool mrow = m < g.M;
       const size_t zz = (size_t)z;
@@ -380,7 +539,7 @@ __device__ __forceinline__ void split1(__half* o, size_t lo_off, float y) {
 // read and write is coalesced.
 __global__ void __launch_bounds__(256) norm_split_kernel(const float* S, float* Xf, __half* Xs, __half* Xt,
                                                          const double* part, int D, int E, int tall, float eps,
-                                                         float sx) {
+                                                         float sx, int64_t packed_z0, int64_t packed_batch) {
   __shared__ float tile[32][33];
   __shared__ float s_inv;
   const size_t DE = (size_t)D * E;
@@ -410,7 +569,10 @@ __global__ void __launch_bounds__(256) norm_split_kernel(const float* S, float* 
     if (d < D && e < E) {
       const float x = tile[ty + 8 * k][tx] * inv;
       if (Xf) Xf[z * DE + (size_t)d * E + e] = x;
-      split1(Xs + z * 2 * DE + (size_t)d * E + e, DE, x * sx);
+      if (packed_batch)  // [part][batch * D][E]
+        split1(Xs + (packed_z0 + z) * DE + (size_t)d * E + e, (size_t)packed_batch * DE, x * sx);
+      else
+        split1(Xs + z * 2 * DE + (size_t)d * E + e, DE, x * sx);
     }
   }
 #pragma unroll
@@ -421,7 +583,7 @@ __global__ void __launch_bounds__(256) norm_split_kernel(const float* S, float* 
 }
 
 cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, double* part, int64_t batch, int rows,
-                            int cols, float eps, float sx, cudaStream_t st) {
+                            int cols, float eps, float sx, cudaStream_t st, bool packed) {
   const int D = rows < cols ? rows : cols, E = rows < cols ? cols : rows;
   const size_t DE = (size_t)D * E;
   const int vec = (reinterpret_cast<uintptr_t>(S) & 15) == 0 && DE % 4 == 0;
@@ -429,7 +591,8 @@ cudaError_t normalize_split(const float* S, float* Xf, __half* Xs, __half* Xt, d
     const int nz = (int)std::min<int64_t>(65535, batch - z0);
     sumsq_kernel<<<dim3(NPART, nz), 256, 0, st>>>(S + z0 * DE, part + z0 * NPART, DE, vec);
     norm_split_kernel<<<dim3((E + 31) / 32, (D + 31) / 32, nz), 256, 0, st>>>(
-        S + z0 * DE, Xf ? Xf + z0 * DE : nullptr, Xs + z0 * 2 * DE, Xt ? Xt + z0 * 2 * DE : nullptr, part + z0 * NPART, D, E, rows > cols, eps, sx);
+        S + z0 * DE, Xf ? Xf + z0 * DE : nullptr, packed ? Xs : Xs + z0 * 2 * DE, Xt ? Xt + z0 * 2 * DE : nullptr,
+        part + z0 * NPART, D, E, rows > cols, eps, sx, z0, packed ? batch : 0);
   }
   return cudaGetLastError();
 }
@@ -478,9 +641,6 @@ static bool make_map_mn(CUtensorMap* map, const __half* base, int64_t batch, int
 template <int BN, bool BMN>
 static cudaError_t gemm_bn(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s) {
   CUtensorMap ma, mb;
-  if (!make_map(&ma, As, batch, g.M, g.K, BM) ||
-      !(BMN ? make_map_mn(&mb, Bs, batch, g.N, g.K) : make_map(&mb, Bs, batch, g.N, g.K, BN)))
-    return cudaErrorInvalidValue;
   const size_t smem = Cfg<BN>::SMEM;
   cudaError_t e =
       cudaFuncSetAttribute(gemm_kernel<BN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -488,6 +648,19 @@ static cudaError_t gemm_bn(const __half* As, const __half* Bs, const EpiArgs& g,
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (g.pack) {  // packed arrays: [part][batch * rows][K]
+    if (batch * g.M >= ((int64_t)1 << 31)) return cudaErrorInvalidValue;
+    const int rows = (int)(batch * g.M);
+    if (!make_map(&ma, As, 1, rows, g.K, BM) ||
+        !(g.diag ? make_map(&mb, Bs, 1, rows, g.K, BN) : make_map_mn(&mb, Bs, 1, g.N, rows)))
+      return cudaErrorInvalidValue;
+    const int64_t tiles = ((batch + g.pack - 1) / g.pack) * (g.diag ? 1 : (g.N + BN - 1) / BN);
+    gemm_kernel<BN, BMN><<<(int)std::min<int64_t>(tiles, sms), NTH, smem, s>>>(ma, mb, g, 0, (int)batch);
+    return cudaGetLastError();
+  }
+  if (!make_map(&ma, As, batch, g.M, g.K, BM) ||
+      !(BMN ? make_map_mn(&mb, Bs, batch, g.N, g.K) : make_map(&mb, Bs, batch, g.N, g.K, BN)))
+    return cudaErrorInvalidValue;
   const int64_t per_z = (int64_t)((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
   const int64_t zmax = std::max<int64_t>(1, (int64_t)1 << 30) / per_z;  // tile index fits an int
   for (int64_t z0 = 0; z0 < batch; z0 += zmax) {
@@ -505,7 +678,13 @@ bool usable(int rows, int cols) {
   return D >= 128 && D % 8 == 0 && std::max(rows, cols) % 8 == 0 && encode_fn() != nullptr;
 }
 
+bool usable_packed(int rows, int cols) {
+  const int D = std::min(rows, cols), E = std::max(rows, cols);
+  return D == 64 && E % 8 == 0 && encode_fn() != nullptr;
+}
+
 cudaError_t gemm(const __half* As, const __half* Bs, const EpiArgs& g, int64_t batch, cudaStream_t s, bool b_mn) {
+  if (g.pack && g.diag) return gemm_bn<128, false>(As, Bs, g, batch, s);
   if (b_mn) return g.N >= 256 ? gemm_bn<256, true>(As, Bs, g, batch, s) : gemm_bn<128, true>(As, Bs, g, batch, s);
   return g.N >= 256 ? gemm_bn<256, false>(As, Bs, g, batch, s) : gemm_bn<128, false>(As, Bs, g, batch, s);
 }

@@ -50,6 +50,11 @@ def _rel(a, b):
     ((2, 264, 200), 5, 0.0),
     ((3, 136, 1000), 5, 1e-12),
     ((4, 512, 128), 5, 0.0),
+    ((3, 64, 256), 5, 0.0),
+    ((5, 256, 64), 5, 1e-12),
+    ((5, 64, 200), 5, 0.0),
+    ((2, 64, 64), 5, 0.0),
+    ((3, 64, 256), 0, 0.0),
 ])
 def test_tensor_pe_matches_float64(shape, steps, eps):
     from atlas_b200 import polar_express, ATLAS_PREC_TENSOR, device_status
