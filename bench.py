@@ -133,26 +133,30 @@ class Clocks:
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def f32_mode(lib, L, dev, stream, sp, p_bf16, nws, ws, g, world, layers=2, reps=2):
-    """The same scan with float32 activations (the reference's float32 path, held to
-    its float32 accuracy): `layers` layers of fwd+bwd, one untimed pass, then `reps`
-    timed passes; tokens/s of the 12-layer step implied by the per-layer time."""
+def f32_mode(lib, L, dev, stream, sp, p_bf16, nws, ws, g, world, layers=2, reps=2, f32=True, pe_ste=0):
+    """A variant of the headline scan: float32 activations (the reference's float32
+    path, held to its float32 accuracy), or pe_ste=True (the straight-through Polar
+    Express backward, memory_layer.py:74-76).  `layers` layers of fwd+bwd, one untimed
+    pass, then `reps` timed passes; tokens/s of the 12-layer step implied by the
+    per-layer time."""
     import torch
     c = CFG
     B, T, H, D, E = c["B"], c["T"], c["H"], c["D"], c["E"]
     p = L.AtlasScanParams(*[getattr(p_bf16, n) for n, _ in L.AtlasScanParams._fields_])
-    p.act_dtype = L.ATLAS_F32
+    p.act_dtype = L.ATLAS_F32 if f32 else L.ATLAS_BF16
+    p.pe_ste = pe_ste
+    act = torch.float32 if f32 else torch.bfloat16
     pp = ctypes.byref(p)
     if lib.atlas_scan_workspace_bytes(pp) > nws:
         return None
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     Ls = []
     for _ in range(layers):
-        Ld = {n: torch.nn.functional.normalize(torch.randn(B, T, H, D, device=dev, generator=g), dim=-1)
+        Ld = {n: torch.nn.functional.normalize(torch.randn(B, T, H, D, device=dev, generator=g), dim=-1).to(act)
               for n in ("q", "k", "v")}
         for n, mu in (("alpha", 3.0), ("eta", -3.0), ("theta", 1.0), ("gamma", 0.0)):
             Ld[n] = torch.sigmoid(mu + 0.5 * torch.randn(B, T, H, device=dev, generator=g))
-        Ld["dy"] = torch.randn(B, T, H, D, device=dev, generator=g) * 0.01
+        Ld["dy"] = (torch.randn(B, T, H, D, device=dev, generator=g) * 0.01).to(act)
         for n in ("y", "dq", "dk", "dv"):
             Ld[n] = torch.empty_like(Ld["q"])
         for n in ("dalpha", "deta", "dtheta", "dgamma"):
@@ -186,10 +190,10 @@ def f32_mode(lib, L, dev, stream, sp, p_bf16, nws, ws, g, world, layers=2, reps=
     from atlas_b200 import dp
     ms_layer = dp.max_over_ranks(t0.elapsed_time(t1)) / (reps * layers)
     step_ms = ms_layer * c["layers"]
-    return {"value": B * T * world / (step_ms / 1e3), "unit": "tokens/s", "dtype": "f32",
-            "ms_per_layer_fwd_bwd": ms_layer,
-            "how": f"{layers} layers fwd+bwd x {reps} timed passes with float32 q/k/v/dy, per-layer time x "
-                   f"{c['layers']} layers (no all-reduce)"}
+    return {"value": B * T * world / (step_ms / 1e3), "unit": "tokens/s", "dtype": "f32" if f32 else "bf16",
+            "pe_ste": bool(pe_ste), "ms_per_layer_fwd_bwd": ms_layer,
+            "how": f"{layers} layers fwd+bwd x {reps} timed passes with {'float32' if f32 else 'bf16'} q/k/v/dy, "
+                   f"per-layer time x {c['layers']} layers (no all-reduce)"}
 
 
 def next_rows(dev, stream, peak_tf, hbm):
@@ -341,20 +345,34 @@ def gpu_arm(args, rank, world):
             e1.record(stream)
             bwd_ev.append((e0, e1))
 
+    copy_stream = torch.cuda.Stream(dev)
+
     def step(timed=False, host=None):
+        # End-to-end steps move every layer's inputs host -> device and its gradients
+        # device -> host on a copy stream, overlapped with the scan kernels; the step
+        # ends only when the last gradient has reached the host.
+        if host is not None:
+            copy_stream.wait_stream(stream)  # the previous step is done with the buffers
+            ready = []
+            with torch.cuda.stream(copy_stream):
+                for Ld in layers:
+                    for n in ("q", "k", "v", "alpha", "eta", "theta", "gamma", "dy"):
+                        Ld[n].copy_(host[n], non_blocking=True)
+                    ready.append(copy_stream.record_event())
         for i, Ld in enumerate(layers):
             if host is not None:
-                for n in ("q", "k", "v", "alpha", "eta", "theta", "gamma"):
-                    Ld[n].copy_(host[n], non_blocking=True)
+                stream.wait_event(ready[i])
             fwd(Ld, timed)
         for Ld in reversed(layers):
-            if host is not None:
-                Ld["dy"].copy_(host["dy"], non_blocking=True)
             bwd(Ld, timed)
             if host is not None:
-                for n in ("dq", "dk", "dv", "dalpha", "deta", "dtheta", "dgamma"):
-                    host["out_" + n].copy_(Ld[n], non_blocking=True)
+                copy_stream.wait_stream(stream)
+                with torch.cuda.stream(copy_stream):
+                    for n in ("dq", "dk", "dv", "dalpha", "deta", "dtheta", "dgamma"):
+                        host["out_" + n].copy_(Ld[n], non_blocking=True)
         dp.allreduce_mean_(grad_buf)
+        if host is not None:
+            stream.wait_stream(copy_stream)
 
     def barrier():
         if world > 1:
@@ -406,6 +424,7 @@ def gpu_arm(args, rank, world):
         e2e = tokens / (e2e_ms / 1e3)
 
     f32 = None if args.no_f32 else f32_mode(lib, L, dev, stream, sp, p, nws, ws, g, world)
+    ste = None if args.no_f32 else f32_mode(lib, L, dev, stream, sp, p, nws, ws, g, world, f32=False, pe_ste=1)
     peak_tf, hbm, peak_kind = _peaks()
     f_bwd = B * T * H * F_BWD(D, c["ns_steps"])
     f_fwd = B * T * H * F_FWD(D, c["ns_steps"])
@@ -431,6 +450,7 @@ def gpu_arm(args, rank, world):
         "gpu_launches": 2 * NL * args.steps,
         "clocks": ck,
         "f32_activations": f32,
+        "pe_ste": ste,
     }
     if rank == 0 and world == 1 and not args.no_next:
         out["next_rows"] = next_rows(dev, stream, peak_tf, hbm)
@@ -452,7 +472,7 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"], help="profiling only: fewer layers")
     ap.add_argument("--seq", type=int, default=CFG["T"], help="profiling only: shorter sequences")
     ap.add_argument("--no-e2e", action="store_true", help="profiling only: skip the end-to-end leg")
-    ap.add_argument("--no-f32", action="store_true", help="skip the float32-activation leg")
+    ap.add_argument("--no-f32", action="store_true", help="skip the float32-activation and pe_ste legs")
     ap.add_argument("--no-next", action="store_true", help="skip the attention / prologue leg")
     args = ap.parse_args()
     if args.layers != CFG["layers"] or args.seq != CFG["T"]:
