@@ -2,10 +2,11 @@
 // cores: the attention core of atlas_jax/model.py:77-135 for the MAG hybrid.
 //
 // Tiles are 128 queries x 128 keys x D = 64, bf16 operands in shared memory in the
-// core-matrix layout of tc_ops.cuh, float32 accumulators in TMEM.  One CTA of eight
-// warps owns one 128-row block.  Warp w reads TMEM lane quadrant w % 4 (rows
-// 32 (w % 4) ..) and column half w / 4, so each row is shared by two threads, and the
-// softmax statistics of a row need one exchange through shared memory per key block.
+// core-matrix layout of tc_ops.cuh, float32 accumulators in TMEM.  One CTA owns one
+// 128-row block.  Warp w reads TMEM lane quadrant w % 4 (rows 32 (w % 4) ..): in the
+// forward eight warps split a row's columns in halves (w / 4), so the softmax
+// statistics of a row need one exchange through shared memory per key block; the
+// backward kernels run sixteen warps, a column quarter (w / 4) each.
 // Only the band's key blocks are visited: ceil((window + 128) / 128) + 1 of them per
 // row block instead of T / 128.
 //
@@ -36,6 +37,7 @@ using namespace tcx;
 constexpr int HD = 64;   // head dim
 constexpr int BR = 128;  // rows per block (queries or keys)
 constexpr int NTH = 256;
+constexpr int NTB = 512;  // backward kernels: four warps per TMEM lane quadrant, a column quarter each
 constexpr int TILE = BR * HD * 2;   // one 128 x 64 bf16 tile
 constexpr int PTILE = BR * BR * 2;  // one 128 x 128 bf16 tile
 constexpr float LOG2E = 1.4426950408889634f;
@@ -393,7 +395,7 @@ struct KVSmem {
 // block qb's S^T and dP^T in registers, the MMAs of block qb + 1's S^T and dP^T are
 // issued into the same TMEM columns, so they run while the threads form P^T and dS^T
 // of block qb; block qb's dV / dK MMAs follow them on the tensor pipe.
-__global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
+__global__ void __launch_bounds__(NTB, 1) dkv_kernel(Args a) {
   extern __shared__ uint8_t raw[];
   KVSmem& s = *(KVSmem*)align128(raw);
   const AtlasSwaParams& P = a.p;
@@ -444,11 +446,11 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
       done = false;
       break;
     }
-    float sv[64], dp[64];
+    float sv[32], dp[32];  // this thread's column quarter [32 ch, 32 ch + 32) of the row
 #pragma unroll
-    for (int c = 0; c < 64; c += 16) {
-      tmem_ld16(u.tm + u.lane + 64 * ch + c, sv + c);
-      tmem_ld16(u.tm + u.lane + 128 + 64 * ch + c, dp + c);
+    for (int c = 0; c < 32; c += 16) {
+      tmem_ld16(u.tm + u.lane + 32 * ch + c, sv + c);
+      tmem_ld16(u.tm + u.lane + 128 + 32 * ch + c, dp + c);
     }
     tmem_wait_ld();
     // dV / dK of block qb - 1 read Q / dO buffer (qb + 2) % 3 and Pt / dSt
@@ -465,8 +467,8 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
       issue_sdp((qb + 1 - qb0) % 3);
     }
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const int cc = 64 * ch + j;
+    for (int j = 0; j < 32; ++j) {
+      const int cc = 32 * ch + j;
       const int qq = q0 + cc;
       const bool ok = full || (kr <= qq && qq - kr <= W && qq < T && kr < T);
       const float pr = ok ? ex2(fmaf(sv[j], sl2, -s.lse2[cur][cc])) : 0.f;
@@ -474,9 +476,9 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
       dp[j] = pr * (dp[j] - s.delta[cur][cc]);
     }
 #pragma unroll
-    for (int c = 0; c < 64; c += 16) {
-      store16(s.Pt, u.rloc, 64 * ch + c, sv + c);
-      store16(s.dSt, u.rloc, 64 * ch + c, dp + c);
+    for (int c = 0; c < 32; c += 16) {
+      store16(s.Pt, u.rloc, 32 * ch + c, sv + c);
+      store16(s.dSt, u.rloc, 32 * ch + c, dp + c);
     }
     fence_async_smem();
     cta_sync();
@@ -489,7 +491,7 @@ __global__ void __launch_bounds__(NTH) dkv_kernel(Args a) {
   }
   if (done && !wait_mma(&s.barv, phase_v, &s.bad, a.status)) done = false;
   cp_async_wait<0>();
-  if (done) {
+  if (done && ch < 2) {  // two warps per lane quadrant write dV / dK (column halves)
     float v[32];
     tmem_ld_half(u.tm + u.lane + 256, ch, v);
     tmem_wait_ld();
@@ -516,7 +518,7 @@ struct QSmem {
 // dQ of one block of 128 queries over its band of key blocks, software pipelined
 // like dkv_kernel (three K / V buffers; key block kb + 1's S and dP MMAs run while the
 // threads form dS of block kb).
-__global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
+__global__ void __launch_bounds__(NTB, 1) dq_kernel(Args a) {
   extern __shared__ uint8_t raw[];
   QSmem& s = *(QSmem*)align128(raw);
   const AtlasSwaParams& P = a.p;
@@ -564,11 +566,11 @@ __global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
       done = false;
       break;
     }
-    float sv[64], dp[64];
+    float sv[32], dp[32];  // this thread's column quarter [32 ch, 32 ch + 32) of the row
 #pragma unroll
-    for (int c = 0; c < 64; c += 16) {
-      tmem_ld16(u.tm + u.lane + 64 * ch + c, sv + c);
-      tmem_ld16(u.tm + u.lane + 128 + 64 * ch + c, dp + c);
+    for (int c = 0; c < 32; c += 16) {
+      tmem_ld16(u.tm + u.lane + 32 * ch + c, sv + c);
+      tmem_ld16(u.tm + u.lane + 128 + 32 * ch + c, dp + c);
     }
     tmem_wait_ld();
     // dQ of block kb - 1 read K buffer (kb + 2) % 3 and dS
@@ -585,14 +587,14 @@ __global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
       issue_sdp((kb + 1 - kb0) % 3);
     }
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const int key = k0 + 64 * ch + j;
+    for (int j = 0; j < 32; ++j) {
+      const int key = k0 + 32 * ch + j;
       const bool ok = full || (key <= row && row - key <= W && key < T && row < T);
       const float pr = ok ? ex2(fmaf(sv[j], sl2, -lse2)) : 0.f;
       dp[j] = pr * (dp[j] - dl);
     }
 #pragma unroll
-    for (int c = 0; c < 64; c += 16) store16(s.dS, u.rloc, 64 * ch + c, dp + c);
+    for (int c = 0; c < 32; c += 16) store16(s.dS, u.rloc, 32 * ch + c, dp + c);
     fence_async_smem();
     cta_sync();
     if (u.w == 0) {
@@ -603,7 +605,7 @@ __global__ void __launch_bounds__(NTH) dq_kernel(Args a) {
   }
   if (done && !wait_mma(&s.barq, phase_q, &s.bad, a.status)) done = false;
   cp_async_wait<0>();
-  if (done) {
+  if (done && ch < 2) {  // two warps per lane quadrant write dQ (column halves)
     float v[32];
     tmem_ld_half(u.tm + u.lane + 256, ch, v);
     tmem_wait_ld();
@@ -720,10 +722,10 @@ extern "C" int atlas_swa_bwd(const AtlasSwaParams* p, const void* q, const void*
   size_t sm = std::max(sizeof(KVSmem) + 128, (size_t)120 * 1024);
   cudaError_t e = set_smem<KVSmem>((const void*)dkv_kernel, sm);
   if (e != cudaSuccess) return launch_status(e);
-  dkv_kernel<<<grid, NTH, sm, s>>>(a);
+  dkv_kernel<<<grid, NTB, sm, s>>>(a);
   sm = std::max(sizeof(QSmem) + 128, (size_t)120 * 1024);
   e = set_smem<QSmem>((const void*)dq_kernel, sm);
   if (e != cudaSuccess) return launch_status(e);
-  dq_kernel<<<grid, NTH, sm, s>>>(a);
+  dq_kernel<<<grid, NTB, sm, s>>>(a);
   return launch_status(cudaGetLastError());
 }
