@@ -34,7 +34,7 @@ def build(force=False, verbose=False):
     os.makedirs(OBJ, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers += [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h")]
-    objs = []
+    objs, cmds = [], []
     for src in sources():
         obj = os.path.join(OBJ, os.path.basename(src) + ".o")
         objs.append(obj)
@@ -43,7 +43,12 @@ def build(force=False, verbose=False):
             if verbose:
                 cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)
-            subprocess.check_call(cmd)
+            cmds.append(cmd)
+    # translation units compile independently: run them side by side
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for f in [ex.submit(subprocess.check_call, c) for c in cmds]:
+            f.result()
     if force or _stale(OUT, objs):
         cmd = [NVCC] + ARCH + ["-shared", "-o", OUT] + objs + ["-lcudart"]
         print(" ".join(cmd), flush=True)

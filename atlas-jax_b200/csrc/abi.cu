@@ -45,7 +45,7 @@ enum Impl { IMPL_EXACT, IMPL_FUSED, IMPL_BATCHED };
 Impl impl_of(const AtlasScanParams& p) {
   if (p.precision == ATLAS_PREC_EXACT) return IMPL_EXACT;
   const char* why = "";
-  if (p.precision == ATLAS_PREC_TENSOR && atlas::tc::supported(p, &why)) return IMPL_FUSED;
+  if (p.precision == ATLAS_PREC_TENSOR && atlas::tc::supported_fwd(p, &why)) return IMPL_FUSED;
   return IMPL_BATCHED;
 }
 
@@ -66,7 +66,8 @@ int check_params(const AtlasScanParams* p, int dir = 0) {
                 "precision must be ATLAS_PREC_EXACT, ATLAS_PREC_TENSOR or ATLAS_PREC_TENSOR_BATCHED");
   if (p->precision != ATLAS_PREC_EXACT) {
     const char* why = "";
-    const bool fused = p->precision == ATLAS_PREC_TENSOR && atlas::tc::supported(*p, &why);
+    const bool fused = p->precision == ATLAS_PREC_TENSOR &&
+                       (dir == 1 ? atlas::tc::supported(*p, &why) : atlas::tc::supported_fwd(*p, &why));
     if (dir == 1 && !fused)
       return fail(ATLAS_ERR_UNSUPPORTED,
                   "tensor path: the backward needs D=64, E=256, chunk<=64 and ATLAS_PREC_TENSOR (%s); "

@@ -113,7 +113,8 @@ cudaError_t launch_fwd(const FwdArgs& a, int kind, cudaStream_t s);
 }  // namespace gen
 
 namespace tc {
-bool supported(const AtlasScanParams& p, const char** why);
+bool supported(const AtlasScanParams& p, const char** why);      // forward and backward
+bool supported_fwd(const AtlasScanParams& p, const char** why);  // forward (also chunk <= 128)
 size_t saved_bytes(const AtlasScanParams& p);
 size_t workspace_bytes(const AtlasScanParams& p);
 cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t s);

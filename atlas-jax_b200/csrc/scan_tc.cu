@@ -51,10 +51,15 @@ namespace atlas {
 namespace tc {
 using namespace tcx;
 
+// Chunks of up to MAXCS_F tokens: a chunk longer than MAXCS runs its frozen pass in
+// MAXCS-token parts (the frozen state is the chunk's entry carry for every part) and
+// keeps its column factors in global scratch beside the row factors.
+constexpr int MAXCS_F = 2 * MAXCS;
+
 struct __align__(1024) Smem {
   uint8_t slot[2][NS_TILE_BYTES];  // per in-flight token: stacked X~, stacked A, B' hi/lo (frozen pass: scratch)
-  float G[MAXCS * D];              // per-token column factor: err (rank 0) or k (rank 1)
-  float gate[4][MAXCS];            // alpha, eta, theta, gamma
+  float G[MAXCS * D];              // per-token column factor: err (rank 0) or k (rank 1), chunks <= MAXCS
+  float gate[4][MAXCS_F];          // alpha, eta, theta, gamma
   float qv[D];
   float zbuf[2][E];
   float pbuf[2][E];                // gelu(W2 q) written by rank 1 into rank 0
@@ -91,10 +96,12 @@ __device__ __forceinline__ float* carry_slot(const FwdArgs& a, float* carries, i
 
 // Frozen-state pass of one chunk (memory_layer.py:504-520), float32 CUDA cores.
 // Writes this CTA's row factor (act on rank 0, chain on rank 1) to Fg (cs x E,
-// global scratch) and its column factor (err / k) to s.G.
+// global scratch) and its column factor (err / k) to s.G, or to Gg (cs x D, global
+// scratch) when the chunk is longer than MAXCS; such a chunk is processed in parts of
+// MAXCS tokens, all against the chunk's entry carry.
 template <typename TA>
-__device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float* Fg, int b, int hh, int c,
-                            int cs, uint32_t rank) {
+__device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float* Fg, float* Gg, int b, int hh,
+                            int c, int cs, uint32_t rank) {
   const AtlasScanParams& P = a.p;
   const int T = P.T, H = P.H;
   const TA* kp = (const TA*)a.k;
@@ -108,10 +115,6 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
   const int tid = threadIdx.x;
   const uint64_t pol = l2_evict_last_policy();  // Fg is re-read by every token of the chunk
   for (int i = tid; i < DE / 4; i += NT) ((float4*)W1s)[i] = ((const float4*)W1t)[i];
-  for (int i = tid; i < cs * D; i += NT) {
-    int r = i / D, d = i % D, t = c * cs + r;
-    kbuf[i] = t < T ? ld_act(kp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
-  }
   for (int r = tid; r < cs; r += NT) {
     Gates g = load_gates(a.alpha, a.eta, a.theta, a.gamma, T, H, b, hh, c * cs + r);
     s.gate[0][r] = g.a;
@@ -119,19 +122,26 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
     s.gate[2][r] = g.t;
     s.gate[3][r] = g.g;
   }
+  for (int rb = 0; rb < cs; rb += MAXCS) {  // parts of at most MAXCS tokens
+  const int n = min(MAXCS, cs - rb);
+  float* Fp = Fg + (size_t)rb * E;
+  for (int i = tid; i < n * D; i += NT) {
+    int r = i / D, d = i % D, t = c * cs + rb + r;
+    kbuf[i] = t < T ? ld_act(kp, (((size_t)b * T + t) * H + hh) * D + d) : 0.f;
+  }
   epi_sync();
   {  // h = W2 k ; thread e
     const int e = tid;
     float w[D];
 #pragma unroll
     for (int d = 0; d < D; ++d) w[d] = W2[e * D + d];
-    for (int r = 0; r < cs; ++r) {
+    for (int r = 0; r < n; ++r) {
       float hv = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) hv = fmaf(w[d], kbuf[r * D + d], hv);
       const float av = gelu_tanh(hv);
       actb[tsw(e, r)] = av;
-      st_hint(&Fg[r * E + e], rank ? hv : av, pol);  // rank 1 keeps h for gelu'(h)
+      st_hint(&Fp[r * E + e], rank ? hv : av, pol);  // rank 1 keeps h for gelu'(h)
     }
   }
   epi_sync();
@@ -141,8 +151,8 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
     tile_tok_d(W1s, actb, dq, iq, acc);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int r = 4 * iq + u, t = c * cs + r;
-      if (r < cs)
+      const int r = 4 * iq + u, t = c * cs + rb + r;
+      if (r < n)
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           const int d = 4 * dq + v;
@@ -157,15 +167,17 @@ __device__ void frozen_pass(const FwdArgs& a, Smem& s, const float* slot, float*
     float w[D];
 #pragma unroll
     for (int d = 0; d < D; ++d) w[d] = W1t[e * D + d];
-    for (int r = 0; r < cs; ++r) {
+    for (int r = 0; r < n; ++r) {
       float rv = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) rv = fmaf(w[d], errb[r * D + d], rv);
-      st_hint(&Fg[r * E + e], rv * gelu_erf_prime(Fg[r * E + e]), pol);
+      st_hint(&Fp[r * E + e], rv * gelu_erf_prime(Fp[r * E + e]), pol);
     }
   }
-  for (int i = tid; i < cs * D; i += NT) s.G[i] = rank ? kbuf[i] : errb[i];
+  float* Gd = Gg ? Gg + (size_t)rb * D : s.G;
+  for (int i = tid; i < n * D; i += NT) Gd[i] = rank ? kbuf[i] : errb[i];
   epi_sync();
+  }  // parts
 }
 
 size_t bwd_workspace_bytes(const AtlasScanParams& p);
@@ -177,14 +189,16 @@ struct KArgs {
   int* flags;      // chunks completed per chain (zeroed before launch)
   int* ticket;     // next work item (zeroed before launch)
   WaitHooks hooks;
-  float* fscr;     // per cluster, per rank: the chunk's row factors (MAXCS x E)
+  float* fscr;     // per cluster, per rank: the chunk's row factors (cs x E) [, column factors (cs x D)]
+  size_t fstride;  // floats of fscr per cluster rank
 };
 
 #ifdef ATLAS_PHASE_PROF
 __device__ unsigned long long g_prof_fwd[32];
 #endif
 
-template <typename TA>
+// LONGC: chunks longer than MAXCS (column factors in global scratch)
+template <typename TA, bool LONGC>
 __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   PROF_DECL
   extern __shared__ uint8_t smem_raw[];
@@ -200,7 +214,9 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
   const float sc = 2.0f / D;
   const bool win = P.omega > 1;
   const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
-  float* Fg = K.fscr + ((size_t)cluster * 2 + rank) * MAXCS * E;
+  float* Fg = K.fscr + ((size_t)cluster * 2 + rank) * K.fstride;
+  float* Gg = LONGC ? Fg + (size_t)MAXCS_F * E : nullptr;  // column factors of a long chunk
+  const float* Gsrc = LONGC ? Gg : s.G;
 
   if (w == 0) {
     tmem_alloc(&s.tmem, TMEM_COLS);
@@ -290,7 +306,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
     }
     cluster_sync();
     PROF_T(tfz)
-    frozen_pass<TA>(a, s, slot, Fg, b, hh, c, cs, rank);
+    frozen_pass<TA>(a, s, slot, Fg, Gg, b, hh, c, cs, rank);
     PROF_ADD(5, tfz)
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -311,7 +327,7 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
         const int r = r0 + j;
         const float et = s.gate[1][r], th = s.gate[2][r];
         // ---- momentum: S <- theta S - eta * s * sum_i gamma_i f_i g_i^T ----
-        window_sum(Gv, Fg, s.G, s.gate[3], r, P.omega, win, j > 0, e0, e1, dc);
+        window_sum(Gv, Fg, Gsrc, s.gate[3], r, P.omega, win, j > 0, e0, e1, dc);
         const float wg = -et * sc;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -451,7 +467,18 @@ bool supported(const AtlasScanParams& p, const char** why) {
     return false;
   }
   if (p.chunk > MAXCS) {
-    *why = "tcgen05 path supports chunk <= 64";
+    *why = "tcgen05 backward supports chunk <= 64";
+    return false;
+  }
+  return true;
+}
+bool supported_fwd(const AtlasScanParams& p, const char** why) {
+  if (p.D != D || p.E != E) {
+    *why = "tcgen05 path is built for head_dim 64, memory hidden 256";
+    return false;
+  }
+  if (p.chunk > MAXCS_F) {
+    *why = "tcgen05 forward supports chunk <= 128";
     return false;
   }
   return true;
@@ -464,21 +491,26 @@ static size_t flags_bytes(const AtlasScanParams& p) { return align256(((size_t)p
 static size_t fwd_clusters(const AtlasScanParams& p) {
   return std::min((size_t)p.B * p.H, (size_t)max_clusters_bound());
 }
+// factor scratch per cluster rank: row factors, plus column factors for chunks > MAXCS
+static size_t fscr_floats(const AtlasScanParams& p) {
+  return p.chunk > MAXCS ? (size_t)MAXCS_F * (E + D) : (size_t)MAXCS * E;
+}
 size_t fwd_workspace_bytes(const AtlasScanParams& p) {
   return flags_bytes(p) + (size_t)p.B * p.H * 4 * DE * sizeof(float) +
-         fwd_clusters(p) * 2 * MAXCS * E * sizeof(float);
+         fwd_clusters(p) * 2 * fscr_floats(p) * sizeof(float);
 }
 size_t workspace_bytes(const AtlasScanParams& p) {
-  // one buffer serves the forward and the backward
+  // one buffer serves the forward and the backward (chunks > MAXCS are forward-only)
+  if (p.chunk > MAXCS) return fwd_workspace_bytes(p);
   return std::max(fwd_workspace_bytes(p), bwd_workspace_bytes(p));
 }
 
 static DeviceCache g_max_clusters;  // resident 2-CTA clusters, per device
 
-template <typename TA>
+template <typename TA, bool LONGC>
 static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) {
   size_t smem = sizeof(Smem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(fwd_kernel<TA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(fwd_kernel<TA, LONGC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(NT + 128);  // 8 epilogue warps + a producer warpgroup (1 MMA warp, 3 idle)
@@ -494,11 +526,11 @@ static cudaError_t launch_fwd_t(const KArgs& k, int nclusters, cudaStream_t st) 
   const int maxc = g_max_clusters.get([&] {
     int n = 0;
     cfg.gridDim = dim3(2);
-    if (cudaOccupancyMaxActiveClusters(&n, fwd_kernel<TA>, &cfg) != cudaSuccess || n <= 0) n = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, fwd_kernel<TA, LONGC>, &cfg) != cudaSuccess || n <= 0) n = 1;
     return n;
   });
   cfg.gridDim = dim3(2 * std::min(nclusters, maxc));
-  return cudaLaunchKernelEx(&cfg, fwd_kernel<TA>, k);
+  return cudaLaunchKernelEx(&cfg, fwd_kernel<TA, LONGC>, k);
 }
 
 cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
@@ -512,10 +544,15 @@ cudaError_t launch_fwd(const FwdArgs& a, cudaStream_t st) {
   k.ticket = k.flags + k.nchains;
   k.carries = (float*)(ws + flags_bytes(a.p));
   k.fscr = k.carries + (size_t)k.nchains * 4 * DE;
+  k.fstride = fscr_floats(a.p);
   cudaError_t e = cudaMemsetAsync(k.flags, 0, flags_bytes(a.p), st);
   if (e != cudaSuccess) return e;
   const int ncl = (int)fwd_clusters(a.p);
-  return a.p.act_dtype == ATLAS_BF16 ? launch_fwd_t<__nv_bfloat16>(k, ncl, st) : launch_fwd_t<float>(k, ncl, st);
+  if (a.p.chunk > MAXCS)
+    return a.p.act_dtype == ATLAS_BF16 ? launch_fwd_t<__nv_bfloat16, true>(k, ncl, st)
+                                       : launch_fwd_t<float, true>(k, ncl, st);
+  return a.p.act_dtype == ATLAS_BF16 ? launch_fwd_t<__nv_bfloat16, false>(k, ncl, st)
+                                     : launch_fwd_t<float, false>(k, ncl, st);
 }
 
 }  // namespace tc

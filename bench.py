@@ -273,6 +273,17 @@ def next_rows(dev, stream, peak_tf, hbm):
     out["config4_d128"] = {"workload": f"forward scan B={B} H={H} T={T} (sample) D={D} E={E} chunk=64 bf16",
                            "ms": c4, "tokens_per_s": B * T / c4 * 1e3, "pe_tflops": c4_fl / c4 / 1e9,
                            "unit": "tokens/s", "kernels": "scan_gen frozen/momentum/memory kernels + pe_tma GEMMs"}
+    del q, k, v, ga, ge, gt
+    # config 4's chunk-128 sweep point at head_dim 64 (B x H = 96) on the fused forward
+    B, T, H, D = 8, 8192, 12, 64
+    q, k, v = (nrm(torch.randn(B, T, H, D, device=dev, generator=g)).to(torch.bfloat16) for _ in range(3))
+    ga, ge, gt = gate(3.0), gate(-3.0), gate(1.0)
+    cfg = ScanConfig(chunk=128, omega=16, ns_steps=5, precision=ATLAS_PREC_TENSOR)
+    c128 = timed(lambda: scan_forward(q, k, v, ga, ge, gt, None, None, cfg, need_saved=False), n=2)
+    out["config4_chunk128"] = {"workload": f"forward scan B={B} H={H} T={T} D={D} E=256 chunk=128 bf16",
+                               "ms": c128, "tokens_per_s": B * T / c128 * 1e3,
+                               "fwd_tflops": B * T * H * F_FWD(D, 5) / c128 / 1e9,
+                               "unit": "tokens/s", "kernels": "tc fwd_kernel (128-token chunks)"}
     return out
 
 

@@ -74,7 +74,8 @@ enum {
    * (hi + lo of a power-of-two multiple of the value, float32 accumulation),
    * float32 carries: as accurate as the reference's float32 arithmetic.  The
    * production path: the fused kernels for D=64, E=256, chunk <= 64 (forward and
-   * backward); other shapes run the batched forward below (forward only). */
+   * backward) and 64 < chunk <= 128 (forward only); other shapes run the batched
+   * forward below (forward only). */
   ATLAS_PREC_TENSOR = 1,
   /* Token-parallel batched forward on the tensor cores for any D in {32, 64, 128,
    * 256}, E <= 2048, chunk <= 4096: the chunk's momenta first, then one batched

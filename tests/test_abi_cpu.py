@@ -55,9 +55,12 @@ def test_polar_express_rejects_empty():
 
 def test_polar_express_precisions():
     lib = L.load()
-    # tensor path: two wide X buffers and two D x D buffers per matrix, float32
-    assert lib.atlas_polar_express_workspace_bytes(12, 4096, 768, 5, L.ATLAS_PREC_TENSOR) == \
-        12 * (2 * 4096 * 768 + 2 * 768 * 768) * 4
+    # tensor path: the TMA GEMMs (where the driver offers tensor-map encoding) keep three
+    # wide and three D x D float32 buffers plus 64 partial sums per matrix; the
+    # register-staged GEMMs two of each
+    tma = 12 * ((3 * 4096 * 768 + 3 * 768 * 768) * 4 + 64 * 8)
+    staged = 12 * (2 * 4096 * 768 + 2 * 768 * 768) * 4
+    assert lib.atlas_polar_express_workspace_bytes(12, 4096, 768, 5, L.ATLAS_PREC_TENSOR) in (tma, staged)
     assert lib.atlas_polar_express_workspace_bytes(12, 768, 768, 5, L.ATLAS_PREC_EXACT) > 0
     # an unknown precision is refused before any device work (the pointers are never read)
     dummy = ctypes.c_void_p(16)
@@ -118,6 +121,25 @@ def test_batched_forward_sizes_and_backward_refusal():
     bad = _p(D=48, precision=L.ATLAS_PREC_TENSOR_BATCHED)
     assert lib.atlas_scan_workspace_bytes(ctypes.byref(bad)) == 0
     assert b"head_dim" in lib.atlas_last_error_string()
+
+
+def test_fused_forward_chunk_128_sizes_and_backward_refusal():
+    """D=64, E=256 with chunk 128 runs the fused forward (factor scratch for 128-token
+    chunks, no backward workspace); the backward refuses it before touching the GPU, and
+    the no-alloc forward (sized for chunks <= 64) refuses it too."""
+    lib = L.load()
+    p64 = _p(D=64, E=256, chunk=64, precision=L.ATLAS_PREC_TENSOR)
+    p128 = _p(D=64, E=256, chunk=128, precision=L.ATLAS_PREC_TENSOR)
+    ws128 = lib.atlas_scan_workspace_bytes(ctypes.byref(p128))
+    assert 0 < ws128 < lib.atlas_scan_workspace_bytes(ctypes.byref(p64))  # forward-only: no backward scratch
+    nch = -(-100 // 128)
+    assert lib.atlas_scan_saved_bytes(ctypes.byref(p128)) == 2 * 3 * nch * 4 * 64 * 256 * 4
+    rc = lib.atlas_scan_bwd(ctypes.byref(p128), *([None] * 25), 0, None)
+    assert rc == L.ATLAS_ERR_UNSUPPORTED and b"chunk" in lib.atlas_last_error_string()
+    rc = lib.atlas_scan_fwd_noalloc(ctypes.byref(p128), *([None] * 16), None)
+    assert rc == L.ATLAS_ERR_UNSUPPORTED
+    p256 = _p(D=64, E=256, chunk=256, precision=L.ATLAS_PREC_TENSOR)
+    assert lib.atlas_scan_workspace_bytes(ctypes.byref(p256)) > 0  # the batched forward takes it
 
 
 def test_linear_scan_checks():

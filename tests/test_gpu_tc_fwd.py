@@ -82,10 +82,12 @@ def test_tc_forward_many_chains_migrate_between_clusters():
 
 
 @pytest.mark.parametrize("T,chunk,omega,ns", [(1, 64, 16, 5), (96, 32, 8, 5), (128, 32, 64, 5), (70, 64, 16, 1),
-                                              (64, 64, 16, 3), (130, 16, 4, 5)])
+                                              (64, 64, 16, 3), (130, 16, 4, 5), (300, 128, 16, 5),
+                                              (256, 128, 128, 5), (129, 128, 8, 2), (100, 96, 16, 5)])
 def test_tc_forward_edge_cases(T, chunk, omega, ns):
-    """single token, chunk 32 / 16 (BASELINE sweep chunks), Omega >= chunk (full
-    in-chunk cumsum, memory_layer.py:247-248), fewer Newton-Schulz steps."""
+    """single token, chunk 32 / 16 / 128 / 96 (BASELINE sweep chunks; chunks above 64 run
+    their frozen pass in 64-token parts), Omega >= chunk (full in-chunk cumsum,
+    memory_layer.py:247-248), fewer Newton-Schulz steps."""
     from atlas_b200 import ScanConfig, ATLAS_PREC_TENSOR, scan_forward
     B, H = 1, 2
     ins = O.make_inputs(B, T, H, 64, seed=T + chunk, gamma_mode="random")
@@ -114,4 +116,17 @@ def test_tc_forward_sweep_384_chains():
     y, out = _run(ins, None, torch.bfloat16)
     y_o, fin = O.scan_forward(*ins, O.lm_initial_state(B, H, 64, 256), 64, 16, 5, dtype=np.float64)
     errs = [rel(y, y_o)] + [rel(a, b) for a, b in zip(out[:2], fin[:2])]
+    assert max(errs) < TOL, errs
+
+
+def test_tc_forward_chunk_128_many_chains():
+    """Config 4's chunk 128 on the fused forward: 96 chains, bf16, chunks migrating
+    between clusters, a padded last chunk."""
+    B, T, H = 8, 320, 12
+    ins = O.make_inputs(B, T, H, 64, seed=11)
+    ins = tuple(_bf(x) for x in ins[:3]) + tuple(ins[3:])
+    y, out = _run(ins, None, torch.bfloat16, chunk=128)
+    y_o, fin = O.scan_forward(*ins, O.lm_initial_state(B, H, 64, 256), 128, 16, 5, dtype=np.float64)
+    errs = [rel(y, y_o)] + [rel(a, b) for a, b in zip(out, fin)]
+    print("rel errors:", errs)
     assert max(errs) < TOL, errs
