@@ -103,6 +103,14 @@ cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, 
                    cudaStream_t s);
 }  // namespace tcpe
 
+// Polar Express of D = 128 matrices (E = 256 or 512) on 2-CTA clusters, matrix kept on
+// chip across the steps (pe_cluster.cu); tcpe::launch dispatches to it.
+namespace pecl {
+bool usable(int rows, int cols);
+cudaError_t launch(const float* S, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
+                   cudaStream_t s);
+}  // namespace pecl
+
 // Shape-generic tensor-path forward (scan_gen.cu): deep memory of any D in
 // {32, 64, 128, 256} / E / chunk, and linear memory (memory_layer.py:468-494).
 enum { KIND_DEEP = 0, KIND_LINEAR = 1 };

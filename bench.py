@@ -272,7 +272,7 @@ def next_rows(dev, stream, peak_tf, hbm):
     c4_fl = B * T * H * 2 * ns * (4 * D * D * E + 2 * D ** 3)  # Polar Express of W1 and W2 per token-head
     out["config4_d128"] = {"workload": f"forward scan B={B} H={H} T={T} (sample) D={D} E={E} chunk=64 bf16",
                            "ms": c4, "tokens_per_s": B * T / c4 * 1e3, "pe_tflops": c4_fl / c4 / 1e9,
-                           "unit": "tokens/s", "kernels": "scan_gen frozen/momentum/memory kernels + pe_tma GEMMs"}
+                           "unit": "tokens/s", "kernels": "scan_gen frozen/momentum/memory kernels + pe_cluster Polar Express"}
     del q, k, v, ga, ge, gt
     # config 4's chunk-128 sweep point at head_dim 64 (B x H = 96) on the fused forward
     B, T, H, D = 8, 8192, 12, 64

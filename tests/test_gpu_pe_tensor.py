@@ -55,6 +55,13 @@ def _rel(a, b):
     ((5, 64, 200), 5, 0.0),
     ((2, 64, 64), 5, 0.0),
     ((3, 64, 256), 0, 0.0),
+    # head_dim 128 on the 2-CTA cluster kernel: wide and tall, E = 256 / 512, no steps,
+    # and more matrices than resident clusters
+    ((3, 128, 512), 5, 1e-12),
+    ((2, 128, 256), 5, 0.0),
+    ((2, 256, 128), 3, 0.0),
+    ((2, 128, 512), 0, 0.0),
+    ((200, 512, 128), 5, 0.0),
 ])
 def test_tensor_pe_matches_float64(shape, steps, eps):
     from atlas_b200 import polar_express, ATLAS_PREC_TENSOR, device_status
