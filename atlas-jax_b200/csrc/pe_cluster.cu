@@ -50,7 +50,7 @@ struct __align__(128) Smem {
   uint8_t Xh[MAXR * D * 2], Xl[MAXR * D * 2];  // split of KX X~ (core-matrix tiles, 128 columns)
   uint8_t Ah[D * D * 2], Al[D * D * 2];        // split of KB A, then of KB B'
   float recv[D * 64];                          // the peer's partial Gram, owned columns (swizzled)
-  uint64_t bar;
+  uint64_t bar, bar2;  // MMA completion: every group; the second 128-row half of X~ B'^T
   double red[8];
   double peer_ss;  // the peer's sum of squares
   uint32_t tmem;
@@ -130,8 +130,8 @@ __device__ __forceinline__ void st4(float* Y, int e, int d, bool tall, int E, fl
 
 // All threads: wait for the MMAs committed to s.bar (bounded; a timeout marks the
 // CTA bad, records ATLAS_ERR_DEVICE_TIMEOUT and skips every later wait and MMA).
-__device__ __forceinline__ void wait_mma(Smem& s, uint32_t& phase, int* status) {
-  if (!s.bad && !mbar_wait(&s.bar, phase)) {
+__device__ __forceinline__ void wait_mma(Smem& s, uint64_t* bar, uint32_t& phase, int* status) {
+  if (!s.bad && !mbar_wait(bar, phase)) {
     s.bad = 1;
     set_status(status, ATLAS_ERR_DEVICE_TIMEOUT);
   }
@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
   if (tid == 0) {
     mbar_init(&s.bar, 1);
+    mbar_init(&s.bar2, 1);
     fence_mbar_init();
     s.bad = 0;
   }
@@ -165,13 +166,22 @@ __global__ void __launch_bounds__(NT, 1)
   fence_after();
   cluster_sync();  // both CTAs initialised before any DSMEM traffic
   const uint32_t tm = s.tmem;
-  uint32_t phase = 0;
+  uint32_t phase = 0, phase2 = 0;
   const uint32_t r_recv = peer_addr(s.recv, peer), r_Ah = peer_addr(s.Ah, peer), r_Al = peer_addr(s.Al, peer);
   const uint32_t r_ss = peer_addr(&s.peer_ss, peer);
 
   for (int64_t z = blockIdx.x >> 1; z < batch; z += ncl) {
     const float* Sz = S + z * DE;
     float* Yz = Y + z * DE;
+    if (w == 7 && z + ncl < batch) {  // the next matrix's rows of this CTA into L2
+      const float* Sn = S + (z + ncl) * DE;
+      if (tall) {
+        const uint32_t part = (uint32_t)ER * D * 4 / 32;
+        bulk_prefetch_l2((const uint8_t*)(Sn + (size_t)rank * ER * D) + l * part, part);
+      } else {
+        for (int d = l; d < D; d += 32) bulk_prefetch_l2(Sn + (size_t)d * E + (size_t)rank * ER, ER * 4);
+      }
+    }
     // ---- Frobenius normalisation: X = S / (1.01 sqrt(sum S^2 + eps) + 1e-6) ----
     float ssf = 0.f;
     for (int h = 0; h < MH; ++h) {
@@ -225,7 +235,7 @@ __global__ void __launch_bounds__(NT, 1)
         mma_split(tm + TM_G, xh, xl, xh, xl, 256, 256, ER / 16, idesc_f16(128, 128, true, true));
         mma_commit(&s.bar);
       }
-      wait_mma(s, phase, status);
+      wait_mma(s, &s.bar, phase, status);
       // ---- 2. reduce over the cluster; this CTA owns columns [64 rank, 64 rank + 64) ----
       float g[64];
       tmem_ld16(tm + lane_off + TM_G + 64 * ch, g);
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(NT, 1)
                   desc_kmajor(al + boff, D), 16, 16, D / 16, idesc_f16(128, 64, false, false));
         mma_commit(&s.bar);
       }
-      wait_mma(s, phase, status);
+      wait_mma(s, &s.bar, phase, status);
       cluster_sync();  // both CTAs' A A products have read the A tiles
       // ---- 4. B' = a I + b A + c A A for the owned columns, into both CTAs' tiles ----
       if (own) {
@@ -305,16 +315,19 @@ __global__ void __launch_bounds__(NT, 1)
       if (w == 0 && !s.bad) {
         fence_after();
         const uint32_t bh = smem_u32(s.Ah), bl = smem_u32(s.Al);
-        for (int h = 0; h < MH; ++h) {
+        for (int h = 0; h < MH; ++h) {  // one commit per half: half 0's epilogue overlaps half 1's MMAs
           const uint32_t xo = 32768u * h;
           mma_split(tm + TM_X + 128 * h, desc_kmajor(smem_u32(s.Xh) + xo, D), desc_kmajor(smem_u32(s.Xl) + xo, D),
                     desc_kmajor(bh, D), desc_kmajor(bl, D), 16, 16, D / 16, idesc_f16(128, 128, false, false));
+          mma_commit(h ? &s.bar2 : &s.bar);
         }
-        mma_commit(&s.bar);
       }
-      wait_mma(s, phase, status);
       const bool last = st + 1 == steps;
       for (int h = 0; h < MH; ++h) {
+        if (h)
+          wait_mma(s, &s.bar2, phase2, status);
+        else
+          wait_mma(s, &s.bar, phase, status);
         const int r = 128 * h + dA, e = (int)rank * ER + r;
         const uint32_t ta = tm + lane_off + TM_X + 128 * h + 64 * ch;
         tmem_ld16(ta, g);
