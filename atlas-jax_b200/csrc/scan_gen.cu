@@ -263,31 +263,32 @@ __global__ void __launch_bounds__(NTH) mom_kernel(FwdArgs a, Geo g, WS w, int c)
   if (idx >= g.RC) return;
   const int r = (int)(idx / g.C), cc = (int)(idx % g.C);
   float* Sp = w.st + ((size_t)q * g.nm + m) * 2 * g.RC + g.RC + idx;
-  const float* F = w.F + ((size_t)q * g.nm + m) * cs * g.R + r;
-  const float* Gc = w.G + ((size_t)q * g.nm + m) * cs * g.C + cc;
+  const float* __restrict__ F = w.F + ((size_t)q * g.nm + m) * cs * g.R + r;
+  const float* __restrict__ Gc = w.G + ((size_t)q * g.nm + m) * cs * g.C + cc;
+  float* __restrict__ out = w.pin + (size_t)m * g.RC + idx;
+  const size_t ostride = (size_t)g.nm * g.RC, obase = (size_t)q * cs * ostride;
   const float s = 2.0f / g.D;
   const int om = P.omega;
   const bool win = om > 1;
-  float S = *Sp, acc = 0.f;
+  float S = *Sp;
+  // G_t = sum_{i = t-om+1..t} gamma_i u_i (restarting at the chunk start), slid one token at
+  // a time in float64 so the running sum does not drift over long chunks
+  double acc = 0.0;
+#pragma unroll 4
   for (int t = 0; t < cs; ++t) {
-    const float u = F[(size_t)t * g.R] * Gc[(size_t)t * g.C];
-    if (win) {  // G_t = sum_{i = t-om+1..t} gamma_i u_i, restarting at the chunk start
-#ifndef ATLAS_MOM_REFRESH
-#define ATLAS_MOM_REFRESH 4  // rebuild the running window sum every 4 tokens (bounds its float32 drift)
-#endif
-      if (ATLAS_MOM_REFRESH > 0 && t % (ATLAS_MOM_REFRESH > 0 ? ATLAS_MOM_REFRESH : 1) == 0) {
-        acc = 0.f;
-        for (int i = max(0, t - om + 1); i <= t; ++i)
-          acc = fmaf(gs[2 * cs + i], F[(size_t)i * g.R] * Gc[(size_t)i * g.C], acc);
-      } else {
-        acc = fmaf(gs[2 * cs + t], u, acc);
-        if (t >= om) acc = fmaf(-gs[2 * cs + t - om], F[(size_t)(t - om) * g.R] * Gc[(size_t)(t - om) * g.C], acc);
-      }
+    const float u = __ldg(&F[(size_t)t * g.R]) * __ldg(&Gc[(size_t)t * g.C]);
+    float gt;
+    if (win) {
+      acc = fma((double)gs[2 * cs + t], (double)u, acc);
+      if (t >= om)
+        acc = fma(-(double)gs[2 * cs + t - om],
+                  (double)(__ldg(&F[(size_t)(t - om) * g.R]) * __ldg(&Gc[(size_t)(t - om) * g.C])), acc);
+      gt = (float)acc;
     } else {
-      acc = u;
+      gt = u;
     }
-    S = fmaf(gs[cs + t], S, -gs[t] * s * acc);
-    w.pin[(((size_t)q * cs + t) * g.nm + m) * g.RC + idx] = S;
+    S = fmaf(gs[cs + t], S, -gs[t] * s * gt);
+    __stcs(&out[obase + (size_t)t * ostride], S);
   }
   *Sp = S;
 }
