@@ -293,7 +293,7 @@ namespace tcpe {
 // Newton-Schulz steps.
 size_t workspace_bytes(int64_t batch, int rows, int cols) {
   const size_t D = std::min(rows, cols), DE = (size_t)rows * cols;
-  if (pecl::usable(rows, cols)) return 256;  // on-chip kernel: no workspace
+  if (pecl::usable(rows, cols) || pecta::usable(rows, cols)) return 256;  // on-chip kernels: no workspace
   if (pet2::usable(rows, cols)) return (size_t)batch * ((3 * DE + 3 * D * D) * sizeof(float) + 64 * sizeof(double));
   if (pet2::usable_packed(rows, cols))
     return (size_t)batch * ((3 * DE + 2 * D * D + D * 128) * sizeof(float) + 64 * sizeof(double));
@@ -436,6 +436,7 @@ cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, 
                    cudaStream_t s) {
   using pet::GemmArgs;
   if (pecl::usable(rows, cols)) return pecl::launch(X, Y, batch, rows, cols, steps, eps, s);
+  if (pecta::usable(rows, cols)) return pecta::launch(X, Y, batch, rows, cols, steps, eps, s);
   if (pet2::usable(rows, cols)) return launch_tma(X, Y, batch, rows, cols, steps, eps, ws, s);
   if (pet2::usable_packed(rows, cols)) return launch_packed(X, Y, batch, rows, cols, steps, eps, ws, s);
   const int D = std::min(rows, cols), E = std::max(rows, cols);

@@ -111,6 +111,14 @@ cudaError_t launch(const float* S, float* Y, int64_t batch, int rows, int cols, 
                    cudaStream_t s);
 }  // namespace pecl
 
+// Polar Express of 64 x 256 matrices, two per CTA in flight, on chip across the steps
+// (pe_cta.cu); tcpe::launch dispatches to it.
+namespace pecta {
+bool usable(int rows, int cols);
+cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
+                   cudaStream_t s);
+}  // namespace pecta
+
 // Shape-generic tensor-path forward (scan_gen.cu): deep memory of any D in
 // {32, 64, 128, 256} / E / chunk, and linear memory (memory_layer.py:468-494).
 enum { KIND_DEEP = 0, KIND_LINEAR = 1 };

@@ -62,6 +62,9 @@ def _rel(a, b):
     ((2, 256, 128), 3, 0.0),
     ((2, 128, 512), 0, 0.0),
     ((200, 512, 128), 5, 0.0),
+    # 64 x 256 on the on-chip per-CTA kernel: more pairs than CTAs, an odd tail, wide
+    ((301, 256, 64), 5, 0.0),
+    ((4, 64, 256), 4, 1e-12),
 ])
 def test_tensor_pe_matches_float64(shape, steps, eps):
     from atlas_b200 import polar_express, ATLAS_PREC_TENSOR, device_status
