@@ -1,5 +1,6 @@
 // C ABI entry points (include/atlas_scan.h): argument checks, dispatch to the
 // exact or the tcgen05 implementation, error reporting.
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -47,6 +48,20 @@ Impl impl_of(const AtlasScanParams& p) {
   const char* why = "";
   if (p.precision == ATLAS_PREC_TENSOR && atlas::tc::supported_fwd(p, &why)) return IMPL_FUSED;
   return IMPL_BATCHED;
+}
+
+// A forward-only ATLAS_PREC_TENSOR call (saved == NULL) with few chains runs the batched
+// forward: the fused kernels run one chain per 2-CTA cluster, so with fewer chains than
+// about half the clusters most SMs idle, while the batched forward spreads every chunk's
+// tokens over the whole GPU.  Calls that keep `saved` for a backward stay on the fused path,
+// whose carries the backward reads.
+bool few_chains(const AtlasScanParams& p) {
+  const char* why = "";
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms = 148;
+  return (long)p.B * p.H * 4 <= (long)sms &&
+         atlas::gen::supported(p, atlas::KIND_DEEP, &why);
 }
 
 // dir: 0 = forward (and the size queries), 1 = backward
@@ -109,7 +124,9 @@ size_t atlas_scan_workspace_bytes(const AtlasScanParams* p) {
   if (check_params(p) != ATLAS_OK) return 0;
   switch (impl_of(*p)) {
     case IMPL_EXACT: return atlas::exact::workspace_bytes(*p);
-    case IMPL_FUSED: return atlas::tc::workspace_bytes(*p);
+    case IMPL_FUSED:  // also sized for the batched forward that forward-only calls with few chains take
+      return few_chains(*p) ? std::max(atlas::tc::workspace_bytes(*p), atlas::gen::workspace_bytes(*p, atlas::KIND_DEEP))
+                            : atlas::tc::workspace_bytes(*p);
     default: return atlas::gen::workspace_bytes(*p, atlas::KIND_DEEP);
   }
 }
@@ -140,7 +157,8 @@ int atlas_scan_fwd(const AtlasScanParams* p, const void* q, const void* k, const
   a.ws = workspace;
   a.status = atlas::device_status_ptr();
   cudaStream_t s = (cudaStream_t)stream;
-  const Impl im = impl_of(*p);
+  Impl im = impl_of(*p);
+  if (im == IMPL_FUSED && !saved && few_chains(*p)) im = IMPL_BATCHED;
   cudaError_t e = im == IMPL_EXACT   ? atlas::exact::launch_fwd(a, s)
                   : im == IMPL_FUSED ? atlas::tc::launch_fwd(a, s)
                                      : atlas::gen::launch_fwd(a, atlas::KIND_DEEP, s);

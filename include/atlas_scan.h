@@ -75,7 +75,10 @@ enum {
    * float32 carries: as accurate as the reference's float32 arithmetic.  The
    * production path: the fused kernels for D=64, E=256, chunk <= 64 (forward and
    * backward) and 64 < chunk <= 128 (forward only); other shapes run the batched
-   * forward below (forward only). */
+   * forward below (forward only).  A forward call without saved carries (saved ==
+   * NULL, so no backward follows) whose B*H is at most a quarter of the SM count also
+   * runs the batched forward: the fused kernels keep one chain per 2-CTA cluster and
+   * would leave most SMs idle.  The two paths agree to float32 rounding, not bit for bit. */
   ATLAS_PREC_TENSOR = 1,
   /* Token-parallel batched forward on the tensor cores for any D in {32, 64, 128,
    * 256}, E <= 2048, chunk <= 4096: the chunk's momenta first, then one batched

@@ -115,3 +115,30 @@ def test_linear_memory_forward(act, D, chunk, omega, T):
             r32 = {"y": (y32, y_o), "M": (f32[0], fin[0]), "S": (f32[1], fin[1])}
             bounds = {n: f32_bound(*r32[n]) for n in errs}
         check_errs(errs, bounds)
+
+
+def test_forward_only_few_chains_takes_the_batched_forward():
+    """A forward-only ATLAS_PREC_TENSOR call (no saved carries) with few chains runs the
+    batched forward (as ATLAS_PREC_TENSOR_BATCHED does); with saved carries it stays
+    on the fused kernels the backward needs.  Both match the oracle."""
+    import numpy as np
+    from atlas_b200 import ATLAS_PREC_TENSOR, ATLAS_PREC_TENSOR_BATCHED, ScanConfig, scan_forward
+    B, T, H = 2, 150, 3
+    ins = O.make_inputs(B, T, H, 64, seed=21)
+    dev = [to_dev(x) for x in ins]
+    res = {}
+    for name, prec, keep in (("auto", ATLAS_PREC_TENSOR, False), ("batched", ATLAS_PREC_TENSOR_BATCHED, False),
+                             ("fused", ATLAS_PREC_TENSOR, True)):
+        cfg = ScanConfig(chunk=64, omega=16, ns_steps=5, precision=prec)
+        y, out, saved = scan_forward(*dev, None, cfg, need_saved=keep)
+        torch.cuda.synchronize()
+        res[name] = to_np(y)
+    # the batched read-out sums with float atomics, so two batched runs agree to rounding
+    # only; the fused kernels differ from it by far more than that
+    d_batched, d_fused = rel(res["auto"], res["batched"]), rel(res["auto"], res["fused"])
+    print(f"auto vs batched {d_batched:.2e}, auto vs fused {d_fused:.2e}")
+    assert d_batched < 1e-6 and d_batched < 0.1 * d_fused
+    y_o, _ = O.scan_forward(*ins, O.lm_initial_state(B, H, 64, 256), 64, 16, 5, dtype=np.float64)
+    y32, _ = O.scan_forward(*ins, O.lm_initial_state(B, H, 64, 256), 64, 16, 5, dtype=np.float32)
+    for name in ("auto", "fused"):
+        assert rel(res[name], y_o) <= f32_bound(y32, y_o), name
