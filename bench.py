@@ -284,6 +284,18 @@ def next_rows(dev, stream, peak_tf, hbm):
                                "ms": c128, "tokens_per_s": B * T / c128 * 1e3,
                                "fwd_tflops": B * T * H * F_FWD(D, 5) / c128 / 1e9,
                                "unit": "tokens/s", "kernels": "tc fwd_kernel (128-token chunks)"}
+    del q, k, v, ga, ge, gt
+    # config 4's smallest B x H (16 chains), forward only: fewer chains than clusters, so the
+    # forward-only call runs the batched forward with the on-chip Polar Express
+    B, T, H, D = 1, 8192, 16, 64
+    q, k, v = (nrm(torch.randn(B, T, H, D, device=dev, generator=g)).to(torch.bfloat16) for _ in range(3))
+    ga, ge, gt = gate(3.0), gate(-3.0), gate(1.0)
+    cfg = ScanConfig(chunk=64, omega=16, ns_steps=5, precision=ATLAS_PREC_TENSOR)
+    c16 = timed(lambda: scan_forward(q, k, v, ga, ge, gt, None, None, cfg, need_saved=False), n=2)
+    out["config4_bh16"] = {"workload": f"forward scan B={B} H={H} T={T} D={D} E=256 chunk=64 bf16 (16 chains)",
+                           "ms": c16, "tokens_per_s": B * T / c16 * 1e3,
+                           "fwd_tflops": B * T * H * F_FWD(D, 5) / c16 / 1e9,
+                           "unit": "tokens/s", "kernels": "scan_gen kernels + pe_cta Polar Express"}
     return out
 
 
