@@ -329,11 +329,8 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
         // ---- momentum: S <- theta S - eta * s * sum_i gamma_i f_i g_i^T ----
         window_sum(Gv, Fg, Gsrc, s.gate[3], r, P.omega, win, j > 0, e0, e1, dc);
         const float wg = -et * sc;
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          Sv[0][jj] = fmaf(th, Sv[0][jj], wg * Gv[0][jj]);
-          Sv[1][jj] = fmaf(th, Sv[1][jj], wg * Gv[1][jj]);
-        }
+        axpby<32>(Sv[0], th, Gv[0], wg);
+        axpby<32>(Sv[1], th, Gv[1], wg);
         PROF_ADD(2, ttok)
         PROF_T(tnorm)
         // ---- Frobenius normalisation (memory_layer.py:55-56) ----
@@ -375,11 +372,8 @@ __global__ void __launch_bounds__(NT + 128, 1) fwd_kernel(KArgs K) {
           tmem_ld32(sl[j].tm + lane_off + TM_X + dc, x0);
           tmem_ld32(sl[j].tm + lane_off + TM_X + 64 + dc, x1);
           tmem_wait_ld();
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {  // TMEM holds KSPLIT^2 X_ns
-            Wv[0][jj] = fmaf(al, Wv[0][jj], x0[jj] * KUNSC2);
-            Wv[1][jj] = fmaf(al, Wv[1][jj], x1[jj] * KUNSC2);
-          }
+          axpby<32>(Wv[0], al, x0, KUNSC2);  // TMEM holds KSPLIT^2 X_ns
+          axpby<32>(Wv[1], al, x1, KUNSC2);
         } else {  // PE with zero steps is the normalisation alone
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {

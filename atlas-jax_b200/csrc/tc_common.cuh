@@ -86,17 +86,69 @@ __device__ __forceinline__ void st_release(int* p, int v) {
 constexpr float KSPLIT = 256.f;
 constexpr float KUNSC2 = 1.f / 65536.f;
 
+__device__ __forceinline__ uint64_t f32x2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f32x2_unpack(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+// Same arithmetic as scalar fmul / fsub (round to nearest), two lanes per instruction.
+__device__ __forceinline__ uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// acc[0..3] += f * g (four lanes as two f32x2 FMAs; same rounding as fmaf)
+__device__ __forceinline__ void fma4(float* acc, float f, float4 g) {
+  const uint64_t ff = f32x2_pack(f, f);
+  const float2 lo = f32x2_unpack(f32x2_fma(ff, f32x2_pack(g.x, g.y), f32x2_pack(acc[0], acc[1])));
+  const float2 hi = f32x2_unpack(f32x2_fma(ff, f32x2_pack(g.z, g.w), f32x2_pack(acc[2], acc[3])));
+  acc[0] = lo.x;
+  acc[1] = lo.y;
+  acc[2] = hi.x;
+  acc[3] = hi.y;
+}
+// v[j] = a * v[j] + b * u[j] for n lanes (n even), as fmaf(a, v[j], b * u[j]) rounds
+template <int n>
+__device__ __forceinline__ void axpby(float* v, float a, const float* u, float b) {
+  const uint64_t a2 = f32x2_pack(a, a), b2 = f32x2_pack(b, b);
+#pragma unroll
+  for (int j = 0; j < n; j += 2) {
+    const uint64_t t = f32x2_mul(b2, f32x2_pack(u[j], u[j + 1]));
+    const float2 r = f32x2_unpack(f32x2_fma(a2, f32x2_pack(v[j], v[j + 1]), t));
+    v[j] = r.x;
+    v[j + 1] = r.y;
+  }
+}
+__device__ __forceinline__ uint64_t f32x2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // Split 8 consecutive float32 values (times scale) into fp16 hi and lo parts and
 // store them as one 16-byte core-matrix row segment in each tile.
 __device__ __forceinline__ void store_split8(uint8_t* th, uint8_t* tl, uint32_t off, const float* v,
                                              float scale = KSPLIT) {
   uint32_t h[4], l[4];
+  const uint64_t sc2 = f32x2_pack(scale, scale);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float y0 = v[2 * k] * scale, y1 = v[2 * k + 1] * scale;
-    const __half2 hv = __floats2half2_rn(y0, y1);  // .x (low half) = y0
+    const uint64_t y = f32x2_mul(f32x2_pack(v[2 * k], v[2 * k + 1]), sc2);
+    const float2 yf = f32x2_unpack(y);
+    const __half2 hv = __floats2half2_rn(yf.x, yf.y);  // .x (low half) = y0
     const float2 hf = __half22float2(hv);
-    const __half2 lv = __floats2half2_rn(y0 - hf.x, y1 - hf.y);
+    const float2 lf = f32x2_unpack(f32x2_sub(y, f32x2_pack(hf.x, hf.y)));
+    const __half2 lv = __floats2half2_rn(lf.x, lf.y);
     h[k] = *reinterpret_cast<const uint32_t*>(&hv);
     l[k] = *reinterpret_cast<const uint32_t*>(&lv);
   }
@@ -182,14 +234,8 @@ __device__ __forceinline__ void momentum_window(float (*Sv)[32], const float* F,
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         const float4 g = g4[j4];
-        Sv[0][4 * j4 + 0] = fmaf(fa[k], g.x, Sv[0][4 * j4 + 0]);
-        Sv[0][4 * j4 + 1] = fmaf(fa[k], g.y, Sv[0][4 * j4 + 1]);
-        Sv[0][4 * j4 + 2] = fmaf(fa[k], g.z, Sv[0][4 * j4 + 2]);
-        Sv[0][4 * j4 + 3] = fmaf(fa[k], g.w, Sv[0][4 * j4 + 3]);
-        Sv[1][4 * j4 + 0] = fmaf(fb[k], g.x, Sv[1][4 * j4 + 0]);
-        Sv[1][4 * j4 + 1] = fmaf(fb[k], g.y, Sv[1][4 * j4 + 1]);
-        Sv[1][4 * j4 + 2] = fmaf(fb[k], g.z, Sv[1][4 * j4 + 2]);
-        Sv[1][4 * j4 + 3] = fmaf(fb[k], g.w, Sv[1][4 * j4 + 3]);
+        fma4(&Sv[0][4 * j4], fa[k], g);
+        fma4(&Sv[1][4 * j4], fb[k], g);
       }
     }
   }
@@ -230,14 +276,8 @@ __device__ __forceinline__ void rank1_add(float (*Gv)[32], const float* F, const
 #pragma unroll
   for (int j4 = 0; j4 < 8; ++j4) {
     const float4 g = g4[j4];
-    Gv[0][4 * j4 + 0] = fmaf(fa, g.x, Gv[0][4 * j4 + 0]);
-    Gv[0][4 * j4 + 1] = fmaf(fa, g.y, Gv[0][4 * j4 + 1]);
-    Gv[0][4 * j4 + 2] = fmaf(fa, g.z, Gv[0][4 * j4 + 2]);
-    Gv[0][4 * j4 + 3] = fmaf(fa, g.w, Gv[0][4 * j4 + 3]);
-    Gv[1][4 * j4 + 0] = fmaf(fb, g.x, Gv[1][4 * j4 + 0]);
-    Gv[1][4 * j4 + 1] = fmaf(fb, g.y, Gv[1][4 * j4 + 1]);
-    Gv[1][4 * j4 + 2] = fmaf(fb, g.z, Gv[1][4 * j4 + 2]);
-    Gv[1][4 * j4 + 3] = fmaf(fb, g.w, Gv[1][4 * j4 + 3]);
+    fma4(&Gv[0][4 * j4], fa, g);
+    fma4(&Gv[1][4 * j4], fb, g);
   }
 }
 
