@@ -34,7 +34,7 @@ F_BWD = lambda D, ns: ns * 56 * D ** 3 + 80 * D ** 2   # noqa: E731
 # capture of the small case (1 layer, B=8, H=12, T=256).  Both kernels' traffic is
 # per token-head (the backward's Newton-Schulz operand scratch, S_t and W_{t-1}; the
 # forward's saved carries and outputs), so a full launch scales by token-heads.
-NCU_TRAFFIC = {"tc_bwd_kernel": 61.15e9, "tc_fwd_kernel": 130.9e6}
+NCU_TRAFFIC = {"tc_bwd_kernel": 61.30e9, "tc_fwd_kernel": 112.8e6}
 NCU_TOKEN_HEADS = 8 * 256 * 12
 
 
