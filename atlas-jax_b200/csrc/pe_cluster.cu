@@ -79,7 +79,6 @@ __device__ __forceinline__ void st_peer_v4(uint32_t addr, uint4 v) {
                "r"(v.w)
                : "memory");
 }
-__device__ __forceinline__ void epi_sync() { __syncthreads(); }
 
 // Splits 8 consecutive values (times scale) into fp16 hi / lo 16-byte row segments.
 __device__ __forceinline__ void split8(const float* v, float scale, uint4& h, uint4& l) {
@@ -372,6 +371,7 @@ static DeviceCache g_max_clusters;
 
 cudaError_t launch(const float* S, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
                    cudaStream_t st) {
+  if (batch <= 0) return cudaSuccess;
   const int E = std::max(rows, cols);
   const size_t smem = sizeof(Smem) + 128;
   cudaError_t e = cudaFuncSetAttribute(pe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -180,6 +180,7 @@ static DeviceCache g_blocks;  // resident CTAs per device
 
 cudaError_t launch(const float* X, float* Y, int64_t batch, int rows, int cols, int steps, float eps,
                    cudaStream_t st) {
+  if (batch <= 0) return cudaSuccess;
   const size_t smem = sizeof(Smem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(pe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

@@ -142,6 +142,15 @@ def test_fused_forward_chunk_128_sizes_and_backward_refusal():
     assert lib.atlas_scan_workspace_bytes(ctypes.byref(p256)) > 0  # the batched forward takes it
 
 
+def test_forward_only_few_chains_workspace_covers_the_batched_forward():
+    """A forward-only ATLAS_PREC_TENSOR call with few chains may run the batched forward,
+    so the workspace it is told to allocate covers that path too."""
+    lib = L.load()
+    p = _p(B=1, T=300, H=4, D=64, E=256, chunk=64, precision=L.ATLAS_PREC_TENSOR)
+    pb = _p(B=1, T=300, H=4, D=64, E=256, chunk=64, precision=L.ATLAS_PREC_TENSOR_BATCHED)
+    assert lib.atlas_scan_workspace_bytes(ctypes.byref(p)) >= lib.atlas_scan_workspace_bytes(ctypes.byref(pb)) > 0
+
+
 def test_linear_scan_checks():
     lib = L.load()
     p = _p(D=64, precision=L.ATLAS_PREC_TENSOR)
