@@ -101,6 +101,15 @@ __global__ void __launch_bounds__(NT + 32, 1)
   if (w == 8) {  // ---- producer warp ----
     for (int64_t p = blockIdx.x; p < npairs; p += gridDim.x) {
       const int n = (int)std::min<int64_t>(2, batch - 2 * p);
+      const int64_t pn = p + gridDim.x;  // the next pair's inputs into L2 while this one runs
+      if (pn < npairs && l < (int)std::min<int64_t>(2, batch - 2 * pn)) {
+        const float* Xn = X + (2 * pn + l) * DEs;
+        if (tall) {
+          bulk_prefetch_l2(Xn, DE * sizeof(float));
+        } else {
+          for (int d = 0; d < D; ++d) bulk_prefetch_l2(Xn + (size_t)d * E, E * sizeof(float));
+        }
+      }
       if (steps > 0 && !pe_produce(sl, B, n, steps, &s.bad) && !s.bad) {
         set_status(status, ATLAS_ERR_DEVICE_TIMEOUT);
         s.bad = 1;
