@@ -490,10 +490,14 @@ static __device__ __forceinline__ bool pe_consume(PESlot* sl, PEBars& B, int nsl
   const uint32_t lane_off = (uint32_t)(32 * qd) << 16;
   const int P = 3 * steps;
   bool ok = true;
-  for (int s = 0; s < nslots; ++s) pe_publish(B, s);
+#pragma unroll
+  for (int s = 0; s < 2; ++s)
+    if (s < nslots) pe_publish(B, s);
   for (int p = 0; p < P; ++p) {
     const int type = p % 3, st = p / 3;
-    for (int s = 0; s < nslots; ++s) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {  // static slot index: sl[] and B stay in registers
+      if (s >= nslots) break;
       PESlot& q = sl[s];
       long long tw = prof ? clock64() : 0;
       if (!*bad && !mbar_wait(B.done[s], B.done_phase[s])) ok = false;
@@ -554,7 +558,9 @@ static __device__ __forceinline__ bool pe_produce(PESlot* sl, PEBars& B, int nsl
   bool ok = true;
   for (int p = 0; p < P; ++p) {
     const int type = p % 3, st = p / 3;
-    for (int s = 0; s < nslots; ++s) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (s >= nslots) break;
       PESlot& q = sl[s];
       if (!*bad && !mbar_wait(B.ready[s], B.ready_phase[s])) ok = false;
       B.ready_phase[s] ^= 1;
