@@ -55,11 +55,17 @@ Impl impl_of(const AtlasScanParams& p) {
 // about half the clusters most SMs idle, while the batched forward spreads every chunk's
 // tokens over the whole GPU.  Calls that keep `saved` for a backward stay on the fused path,
 // whose carries the backward reads.
+atlas::DeviceCache g_sms;  // multiprocessors per device
+
 bool few_chains(const AtlasScanParams& p) {
   const char* why = "";
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    sms = 148;
+  const int sms = g_sms.get([] {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        n <= 0)
+      n = 148;
+    return n;
+  });
   return (long)p.B * p.H * 4 <= (long)sms &&
          atlas::gen::supported(p, atlas::KIND_DEEP, &why);
 }
